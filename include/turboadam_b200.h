@@ -1,0 +1,211 @@
+/*
+ * turboadam_b200.h -- C ABI of the B200-native TurboAdam optimizer step.
+ *
+ * Plain pointers and sizes only. Every pointer argument named *_dev is a
+ * device pointer owned by the caller (the library never allocates or frees
+ * device memory); `stream` is a cudaStream_t passed as void*. All compute
+ * entry points are asynchronous on that stream; the returned ta_status only
+ * reports host-side validation and launch errors. Device-side anomalies
+ * (non-finite gradients, a bounded wait that ran out) are OR-ed into a
+ * status word in the caller's workspace, read back with ta_read_status().
+ *
+ * Reference interfaces (davidkny22/turboadam, src/turboadam/...) that each
+ * entry point replaces are cited beside it.
+ */
+#ifndef TURBOADAM_B200_H
+#define TURBOADAM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define TA_API __attribute__((visibility("default")))
+#else
+#define TA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TA_ABI_VERSION 1
+
+typedef enum ta_status {
+  TA_OK = 0,
+  TA_ERR_INVALID = 1,     /* bad argument (null pointer, size, enum)        */
+  TA_ERR_ALIGN = 2,       /* a pointer is not 16-byte aligned               */
+  TA_ERR_UNSUPPORTED = 3, /* valid in the reference but not built here      */
+  TA_ERR_WORKSPACE = 4,   /* workspace too small                            */
+  TA_ERR_CUDA = 5         /* a CUDA runtime call failed (see ta_last_error) */
+} ta_status;
+
+/* element types of params / grads */
+enum { TA_F32 = 0, TA_BF16 = 1 };
+
+/* ta_tensor.flags */
+enum {
+  TA_M_COSTATE = 1u << 0,   /* first moment is CoState (else fp32 exp_avg)        */
+  TA_V_ONEQ = 1u << 1,      /* second moment is 1Q (else fp32 exp_avg_sq)         */
+  TA_M_HAS_STATE = 1u << 2, /* CoState holds a previous encoding (not first step) */
+  TA_NO_PARAM = 1u << 3     /* skip weight decay and the parameter update         */
+};
+
+/* device status bits (ta_read_status) */
+enum {
+  TA_STATUS_NONFINITE_GRAD = 1u << 0,
+  TA_STATUS_WAIT_TIMEOUT = 1u << 1
+};
+
+/*
+ * One parameter tensor of an optimizer step.
+ * Replaces the per-parameter `state` dict of TurboAdam (optimizer.py:242-286)
+ * with the same packed layout:
+ *   v_idx   compressed_v["indices"]  u8 [B*block]   (quantize.py:134)
+ *   v_hdr   compressed_v["scales"]   fp16 [B][2] = (log_min, log_max) of ln v
+ *   m_*     CoStateManager._encoded  labels u8[B], sign_packed u8[ceil(n/8)]
+ *           (MSB first), block_norms fp32[B], scales fp16[B]; _alpha fp32[1]
+ *   exp_avg / exp_avg_sq             fp32 [n]
+ * with B = ceil(n / block). State arrays (everything but param/grad) must be
+ * allocated with room for a whole number of 16-block tiles:
+ * ta_state_padded_blocks(n) blocks (idx: that many * block bytes).
+ */
+typedef struct ta_tensor {
+  void* param_dev;            /* [n] fp32 or bf16, updated in place                */
+  const void* grad_dev;       /* [n] same dtype as param                           */
+  int64_t numel;              /* n                                                 */
+  int32_t dtype;              /* TA_F32 | TA_BF16                                  */
+  int32_t group;              /* index into the ta_group array                     */
+  uint32_t flags;             /* TA_M_COSTATE | TA_V_ONEQ | ...                    */
+  uint32_t tensor_id;         /* stable id of the tensor (stochastic-rounding key) */
+  uint32_t step;              /* this tensor's step count after increment (>= 1)   */
+  int32_t reserved0;
+  uint8_t* v_idx_dev;         /* TA_V_ONEQ                                         */
+  uint16_t* v_hdr_dev;        /* TA_V_ONEQ                                         */
+  float* exp_avg_sq_dev;      /* !TA_V_ONEQ                                        */
+  uint8_t* m_labels_dev;      /* TA_M_COSTATE                                      */
+  uint8_t* m_signs_dev;       /* TA_M_COSTATE                                      */
+  float* m_norms_dev;         /* TA_M_COSTATE                                      */
+  uint16_t* m_amp_dev;        /* TA_M_COSTATE                                      */
+  float* m_alpha_dev;         /* TA_M_COSTATE, [1]                                 */
+  float* exp_avg_dev;         /* !TA_M_COSTATE                                     */
+  const float* sr_uniforms_dev; /* optional [B*block]: replaces the Philox draws   */
+  const float* alpha_inject_dev;/* optional [1]: replaces the computed alpha       */
+  float* m_out_dev;           /* optional [n]: receives m_new (CoState.update seam)*/
+  float* v_out_dev;           /* optional [n]: receives fp32 v_new                 */
+} ta_tensor;
+
+/*
+ * Hyper-parameters of one param group (optimizer.py:67-80 defaults).
+ * bc1/bc2 are the fp32 bias corrections 1-beta^t the reference fills into
+ * its shared `_bc1/_bc2` tensors (optimizer.py:172-188).
+ */
+typedef struct ta_group {
+  double lr, beta1, beta2, eps, weight_decay;
+  double null_pct, amp_pct;
+  float bc1, bc2;
+  int32_t block_size;         /* only 128 is built                                 */
+  int32_t v_bits;             /* 2, 3, 4, 6 or 8                                   */
+} ta_group;
+
+/* Library ABI version (TA_ABI_VERSION). */
+TA_API int ta_abi_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+TA_API const char* ta_last_error(void);
+
+/* Blocks to allocate per state array for a tensor of n elements (B rounded up
+ * to whole 16-block tiles). */
+TA_API int64_t ta_state_padded_blocks(int64_t n, int32_t block_size);
+
+/* Workspace bytes ta_step needs for this tensor list. */
+TA_API size_t ta_workspace_size(const ta_tensor* tensors, int32_t n_tensors);
+
+/*
+ * One fused optimizer step over a list of tensors.
+ * Replaces TurboAdam._full_step_kernel (optimizer.py:88-170), i.e. per tensor
+ * decoupled weight decay, the m update (CoStateManager.update,
+ * costate.py:367-464, or the fp32 EMA), the v update (fused_v_update,
+ * quantize.py:222-299, or the fp32 EMA) and p.addcdiv_ -- as a fixed
+ * sequence of multi-tensor kernels (pass 1 over p/g/state, per-tensor alpha,
+ * pass 2 CoState encode, exact P10/P90 radix select, labels).
+ * seed: 64-bit key of the stochastic-rounding generator.
+ */
+TA_API ta_status ta_step(const ta_tensor* tensors, int32_t n_tensors, const ta_group* groups,
+                  int32_t n_groups, uint64_t seed, void* workspace_dev,
+                  size_t workspace_bytes, void* stream);
+
+/*
+ * ta_step with timing marks: phase_events[0..4] (cudaEvent_t as void*, any
+ * may be NULL) are recorded on `stream` before pass 1, after pass 1, after
+ * the alpha reduction, after pass 2 and after the labels kernel, so a caller
+ * can time each kernel inside its own timed region. No counterpart in the
+ * reference (which has no per-kernel timing); same semantics as ta_step.
+ */
+TA_API ta_status ta_step_profiled(const ta_tensor* tensors, int32_t n_tensors,
+                                  const ta_group* groups, int32_t n_groups, uint64_t seed,
+                                  void* workspace_dev, size_t workspace_bytes, void* stream,
+                                  void* const* phase_events);
+
+/* Reads (and optionally clears) the device status word of a workspace
+ * (synchronises the stream). */
+TA_API ta_status ta_read_status(void* workspace_dev, int32_t clear, uint32_t* status_out,
+                         void* stream);
+
+/*
+ * 1Q fused v update of one tensor.
+ * Replaces quantize.fused_v_update (quantize.py:222-299) and
+ * triton_kernels.triton_fused_v_update (triton_kernels.py:105-165).
+ * idx/hdr are read, out_idx/out_hdr written (may alias the inputs).
+ * uniforms_dev: optional [B*block] draws (else Philox keyed by seed,
+ * tensor_id, step). v_out_dev: [n] fp32 v_new.
+ */
+TA_API ta_status ta_v_update(const uint8_t* idx_dev, const uint16_t* hdr_dev, const void* grad_dev,
+                      int32_t grad_dtype, int64_t n, int32_t block_size, int32_t v_bits,
+                      double beta2, const float* uniforms_dev, uint64_t seed,
+                      uint32_t tensor_id, uint32_t step, uint8_t* out_idx_dev,
+                      uint16_t* out_hdr_dev, float* v_out_dev, void* workspace_dev,
+                      size_t workspace_bytes, void* stream);
+
+/* 1Q state of a fresh tensor: compress_v_logscale(full(1e-30)) as done at
+ * optimizer.py:273-280 (all indices 0, both headers fp16(ln 1e-30)). */
+TA_API ta_status ta_v_init(int64_t n, int32_t block_size, uint8_t* idx_dev, uint16_t* hdr_dev,
+                    void* stream);
+
+/* Decode 1Q state to fp32 v.
+ * Replaces oneq.decompress_v (oneq.py:51-67) / quantize.dequantize_logscale_nbits
+ * (quantize.py:183-214). */
+TA_API ta_status ta_v_decode(const uint8_t* idx_dev, const uint16_t* hdr_dev, int64_t n,
+                      int32_t block_size, int32_t v_bits, float* v_out_dev, void* stream);
+
+/* CoState decode m_hat = alpha*g + scale*sign.
+ * Replaces costate.decode_blocks (costate.py:261-323) and
+ * triton_kernels.triton_costate_decode (triton_kernels.py:217-261). */
+TA_API ta_status ta_costate_decode(const uint8_t* labels_dev, const uint8_t* signs_dev,
+                            const float* norms_dev, const uint16_t* amp_dev,
+                            const float* alpha_dev, const void* grad_dev,
+                            int32_t grad_dtype, int64_t n, int32_t block_size,
+                            float* m_out_dev, void* stream);
+
+/* CoState encode (block norms, fp16 amplitude scales, MSB-first sign bits).
+ * Replaces costate.encode_blocks (costate.py:213-258) and
+ * triton_kernels.triton_costate_encode (triton_kernels.py:313-358). */
+TA_API ta_status ta_costate_encode(const float* delta_dev, int64_t n, int32_t block_size,
+                            uint8_t* signs_dev, float* norms_dev, uint16_t* amp_dev,
+                            void* stream);
+
+/* Exact P-quantile thresholds of per-block ratios (fp32-bit radix select).
+ * Replaces costate.compute_thresholds (costate.py:94-118); tau_dev[0..1] =
+ * (tau0, tau1). Also writes labels (costate.classify_blocks,
+ * costate.py:126-149) when labels_dev is not NULL. */
+TA_API ta_status ta_thresholds(const float* ratios_dev, int64_t n_blocks, double null_pct,
+                        double amp_pct, float* tau_dev, uint8_t* labels_dev,
+                        void* workspace_dev, size_t workspace_bytes, void* stream);
+
+/* Workspace bytes for ta_v_update / ta_thresholds on n elements / blocks. */
+TA_API size_t ta_aux_workspace_size(int64_t n);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TURBOADAM_B200_H */

@@ -1,0 +1,37 @@
+"""Helpers to replay the golden fixtures (tests/golden/*.npz)."""
+import importlib.util
+import os
+
+import numpy as np
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def load(name):
+    return np.load(os.path.join(GOLDEN, name))
+
+
+def runs():
+    """RUNS table of make_golden.py (imported without running the generator)."""
+    spec = importlib.util.spec_from_file_location(
+        "_make_golden", os.path.join(GOLDEN, "make_golden.py"))
+    m = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(m)
+    return m.RUNS
+
+
+def bf16_to_f32(bits):
+    return (np.asarray(bits, np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def p_close(ours, ref, update_scale, rtol=1e-6):
+    """Parameter agreement: |ours - ref| <= rtol * (|ref| + update_scale).
+
+    ``update_scale`` is the largest per-element update the reference applied
+    so far, so elements where p crosses zero are judged against the update
+    size, not against |p| ~ 0.
+    """
+    ours = np.asarray(ours, np.float64)
+    ref = np.asarray(ref, np.float64)
+    tol = rtol * (np.abs(ref) + np.asarray(update_scale, np.float64))
+    return np.abs(ours - ref) <= tol

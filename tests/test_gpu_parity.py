@@ -1,0 +1,342 @@
+"""CUDA path vs the CPU checker: bit-exact packed state and parameters.
+
+The checker (oracle/) restates the reference step with the same arithmetic
+spec (op order, ta_math.h transcendentals, canonical alpha reduction,
+Philox counter layout), so the sm_100a kernels must agree with it on every
+bit: indices, fp16 headers, labels, sign bits, block norms, fp16 scales,
+alpha, exp_avg / exp_avg_sq and the updated parameters -- with injected
+uniforms (reference-parity mode) and with the production Philox draws.
+A second group of tests replays the reference's own golden runs on the GPU
+(uniforms and alpha injected) and compares against the reference outputs.
+"""
+import numpy as np
+import pytest
+import torch
+
+import golden_util as GU
+
+pytestmark = pytest.mark.gpu
+
+
+def cuda(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def to_np(t):
+    return t.detach().cpu().numpy()
+
+
+def bits16(t):
+    return to_np(t.contiguous().view(torch.int16)).view(np.uint16)
+
+
+def evolved_v_state(oracle, n, nbits, rng, steps=2):
+    idx, hdr = oracle.v_init(n)
+    B = (n + 127) // 128
+    for _ in range(steps):
+        g = (rng.standard_normal(n) * 10.0 ** rng.uniform(-5, -1, n)).astype(np.float32)
+        idx, hdr, _ = oracle.v_update(idx, hdr, g, nbits, 0.999, rng.random(B * 128, np.float32))
+    return idx, hdr
+
+
+@pytest.mark.parametrize("nbits", [2, 3, 4, 6, 8])
+@pytest.mark.parametrize("n", [1, 127, 129, 5000, 65536 + 37])
+def test_v_update_seam_injected(oracle, nbits, n):
+    from turboadam_b200.oneq import fused_v_update
+
+    rng = np.random.default_rng(nbits * 1000 + n)
+    idx, hdr = evolved_v_state(oracle, n, nbits, rng)
+    B = (n + 127) // 128
+    g = (rng.standard_t(3, n) * 1e-3).astype(np.float32)
+    u = rng.random(B * 128, np.float32)
+    ni, nh, v = fused_v_update(cuda(idx), cuda(hdr.view(np.float16)), cuda(g), 0.999, nbits, 128,
+                               n, rand_buf=cuda(u))
+    oi, oh, ov = oracle.v_update(idx, hdr, g, nbits, 0.999, u)
+    np.testing.assert_array_equal(to_np(ni), oi)
+    np.testing.assert_array_equal(bits16(nh).reshape(-1), oh)
+    np.testing.assert_array_equal(to_np(v).view(np.uint32), ov.view(np.uint32))
+
+
+@pytest.mark.parametrize("nbits", [3, 4, 8])
+def test_v_update_seam_philox(oracle, nbits):
+    from turboadam_b200.oneq import fused_v_update
+
+    n = 3 * 2048 + 77
+    rng = np.random.default_rng(7)
+    idx, hdr = evolved_v_state(oracle, n, nbits, rng)
+    g = (rng.standard_normal(n) * 1e-3).astype(np.float32)
+    seed, tid, step = 0xDEADBEEF12345678, 17, 42
+    ni, nh, v = fused_v_update(cuda(idx), cuda(hdr.view(np.float16)), cuda(g), 0.999, nbits, 128,
+                               n, seed=seed, tensor_id=tid, step=step)
+    u = oracle.sr_uniforms(n, tid, step, seed)
+    oi, oh, ov = oracle.v_update(idx, hdr, g, nbits, 0.999, u)
+    np.testing.assert_array_equal(to_np(ni), oi)
+    np.testing.assert_array_equal(bits16(nh).reshape(-1), oh)
+
+
+# ---------------------------------------------------------------------------
+# whole optimizer step vs the checker replay
+# ---------------------------------------------------------------------------
+
+GPT2_BLOCK = [(768,), (768,), (768, 2304), (2304,), (768, 768), (768,), (768,), (768,),
+              (768, 3072), (3072,), (3072, 768), (768,)]
+
+
+def _init_np(shape, rng, kind):
+    if kind == "ones":
+        return np.ones(shape, np.float32)
+    if kind == "zeros":
+        return np.zeros(shape, np.float32)
+    return (rng.standard_normal(shape) * 0.02).astype(np.float32)
+
+
+def run_compare(oracle, shapes, groups_kw, nsteps, dtype=torch.float32, parity=False,
+                seed=1234, grad_scale=1e-3, assign=None, zero_rows=None):
+    """Runs TurboAdam on the GPU and the checker replay side by side and
+    asserts bit equality of every parameter and state tensor after each step."""
+    from turboadam_b200 import TurboAdam
+
+    rng = np.random.default_rng(seed)
+    assign = assign or [0] * len(shapes)
+    inits = [_init_np(s, rng, "normal") for s in shapes]
+    bf = dtype == torch.bfloat16
+    tparams = []
+    oparams = []
+    for a in inits:
+        t = torch.from_numpy(a).to(dtype).cuda()
+        tparams.append(torch.nn.Parameter(t))
+        if bf:
+            oparams.append(oracle.OracleParam(bits16(t).reshape(-1).copy(), bf16=True))
+        else:
+            oparams.append(oracle.OracleParam(a.reshape(-1).copy()))
+    tg = [{"params": [tparams[i] for i in range(len(shapes)) if assign[i] == gi], **kw}
+          for gi, kw in enumerate(groups_kw)]
+    og = [oracle.OracleTurboAdam.make_group(
+        [oparams[i] for i in range(len(shapes)) if assign[i] == gi], **kw)
+        for gi, kw in enumerate(groups_kw)]
+    opt = TurboAdam(tg, seed=seed)
+    oopt = oracle.OracleTurboAdam(og)
+    # the optimizer's tensor ids: flattened index over param groups
+    order = [i for gi in range(len(groups_kw)) for i in range(len(shapes)) if assign[i] == gi]
+    for s in range(nsteps):
+        unis = {}
+        for i in range(len(shapes)):
+            g = (rng.standard_normal(shapes[i]) * grad_scale).astype(np.float32)
+            if zero_rows is not None and i == zero_rows[0]:
+                g[rng.random(g.shape[0]) < zero_rows[1]] = 0.0
+            gt = torch.from_numpy(g).to(dtype).cuda()
+            tparams[i].grad = gt
+            oparams[i].grad = to_np(gt.float()).reshape(-1)
+        if parity:
+            for i in range(len(shapes)):
+                B = (tparams[i].numel() + 127) // 128
+                unis[i] = rng.random(B * 128, np.float32)
+            opt._parity = {"uniforms": {tparams[i]: cuda(unis[i]) for i in unis}}
+            ufn = lambda oi, st, npad: unis[order[oi]]  # noqa: E731
+        else:
+            n_of = [tparams[order[k]].numel() for k in range(len(order))]
+            ufn = lambda oi, st, npad: oracle.sr_uniforms(n_of[oi], oi, st, seed)  # noqa: E731
+        opt.step()
+        oopt.step(uniforms=ufn)
+        torch.cuda.synchronize()
+        for i in range(len(shapes)):
+            tag = f"step {s} param {i} shape {shapes[i]}"
+            tp, op = tparams[i], oparams[i]
+            st, ost = opt.state[tp], oopt.state[id(op)]
+            if bf:
+                np.testing.assert_array_equal(bits16(tp.data).reshape(-1), op.data, err_msg=tag)
+            else:
+                np.testing.assert_array_equal(to_np(tp.data).reshape(-1).view(np.uint32),
+                                              op.data.view(np.uint32), err_msg=tag)
+            if "compressed_v" in st:
+                cv = st["compressed_v"]
+                np.testing.assert_array_equal(to_np(cv["indices"]), ost.v_idx, err_msg=tag)
+                np.testing.assert_array_equal(bits16(cv["scales"]).reshape(-1), ost.v_hdr,
+                                              err_msg=tag)
+            if "m_mgr" in st:
+                mg, om = st["m_mgr"], ost.mgr
+                enc = mg._encoded
+                assert float(mg._alpha) == om.alpha or (np.isnan(om.alpha)), tag
+                np.testing.assert_array_equal(to_np(enc["labels"]), om.labels, err_msg=tag)
+                np.testing.assert_array_equal(to_np(enc["sign_packed"]), om.signs, err_msg=tag)
+                np.testing.assert_array_equal(to_np(enc["block_norms"]).view(np.uint32),
+                                              om.norms.view(np.uint32), err_msg=tag)
+                np.testing.assert_array_equal(bits16(enc["scales"]), om.amp, err_msg=tag)
+            if "exp_avg" in st:
+                np.testing.assert_array_equal(to_np(st["exp_avg"]).reshape(-1).view(np.uint32),
+                                              ost.exp_avg.view(np.uint32), err_msg=tag)
+            if "exp_avg_sq" in st:
+                np.testing.assert_array_equal(
+                    to_np(st["exp_avg_sq"]).reshape(-1).view(np.uint32),
+                    ost.exp_avg_sq.view(np.uint32), err_msg=tag)
+    return opt
+
+
+@pytest.mark.parametrize("parity", [True, False])
+def test_gpt2_block_bitexact(oracle, parity):
+    """Config 1: one GPT-2-small block, 4-bit v + CoState, lr 6e-4, wd 0.01."""
+    run_compare(oracle, GPT2_BLOCK, [dict(lr=6e-4, betas=(0.9, 0.999), weight_decay=0.01,
+                                          v_bits=4)], nsteps=3, parity=parity)
+
+
+@pytest.mark.parametrize("v_bits", [2, 3, 4, 6, 8])
+def test_v_only_odd_tail_bitexact(oracle, v_bits):
+    """Config 3 in miniature: compress_m=False, flat tensor with a 37-element tail."""
+    run_compare(oracle, [(2 ** 17 + 37,)], [dict(lr=1e-3, compress_m=False, v_bits=v_bits)],
+                nsteps=2, seed=v_bits)
+
+
+def test_bf16_3bit_bitexact(oracle):
+    """Config 5 dtype: bf16 params and grads, 3-bit v + CoState."""
+    run_compare(oracle, [(256, 96), (4099,), (640,)],
+                [dict(lr=1e-3, weight_decay=0.01, v_bits=3)], nsteps=3, dtype=torch.bfloat16,
+                grad_scale=1e-4)
+
+
+def test_groups_and_kinds_bitexact(oracle):
+    """Mixed kinds in one step: CoState/1Q, fp32-m/1Q, CoState/fp32-v, fp32/fp32."""
+    run_compare(oracle, [(64, 80), (70,), (50, 90), (4500,), (20,), (8192 + 3,)],
+                [dict(lr=1e-3, v_bits=3), dict(lr=3e-4, weight_decay=0.05, v_bits=8,
+                                               compress_m=False),
+                 dict(lr=2e-3, weight_decay=0.1, compress_v=False)],
+                nsteps=3, assign=[0, 0, 1, 2, 2, 0], parity=True)
+
+
+def test_sparse_embedding_rows(oracle):
+    """Config 2 feature: whole zero-gradient rows (768 = 6 blocks per row)."""
+    run_compare(oracle, [(512, 768), (768,)], [dict(lr=6e-4, weight_decay=0.01)], nsteps=3,
+                zero_rows=(0, 0.05))
+
+
+# ---------------------------------------------------------------------------
+# reference golden runs replayed on the GPU (uniforms + alpha injected)
+# ---------------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("name", ["block", "groups", "bf16", "gradnone"])
+def test_reference_golden_on_gpu(name):
+    from turboadam_b200 import TurboAdam
+
+    pspecs, gkw, nsteps, none_set = GU.runs()[name]
+    d = GU.load(f"opt_{name}.npz")
+    params = []
+    for pi, (shape, dt, gi) in enumerate(pspecs):
+        init = d[f"p{pi}_init"].reshape(shape)
+        if dt == "bf16":
+            t = torch.from_numpy(init.view(np.int16).copy()).view(torch.bfloat16).cuda()
+        else:
+            t = torch.from_numpy(init.copy()).cuda()
+        params.append(torch.nn.Parameter(t))
+    groups = [dict(params=[params[i] for i, s in enumerate(pspecs) if s[2] == gi], **kw)
+              for gi, kw in enumerate(gkw)]
+    opt = TurboAdam(groups)
+    order = [i for gi in range(len(gkw)) for i, s in enumerate(pspecs) if s[2] == gi]
+    prev, scale = {}, {}
+    for s in range(nsteps):
+        uni, alph = {}, {}
+        for pi, p in enumerate(params):
+            if (s, pi) in none_set:
+                p.grad = None
+                continue
+            g = d[f"s{s}_g{pi}"].reshape(pspecs[pi][0])
+            if pspecs[pi][1] == "bf16":
+                p.grad = torch.from_numpy(g.view(np.int16).copy()).view(torch.bfloat16).cuda()
+            else:
+                p.grad = cuda(g)
+        # reference draw order = param order of the step; ours keyed by param
+        for pi, p in enumerate(params):
+            if f"s{s}_u{pi}" in d:
+                uni[p] = cuda(d[f"s{s}_u{pi}"])
+            if f"s{s}_alpha{pi}" in d:
+                alph[p] = cuda(d[f"s{s}_alpha{pi}"])
+        opt._parity = {"uniforms": uni, "alpha": alph}
+        opt.step()
+        torch.cuda.synchronize()
+        for pi, p in enumerate(params):
+            if f"s{s}_p{pi}" not in d:
+                continue
+            tag = f"{name} step {s} param {pi}"
+            st = opt.state[p]
+            assert st["step"] == int(d[f"s{s}_step{pi}"][0]), tag
+            rp = d[f"s{s}_p{pi}"].reshape(-1)
+            if pspecs[pi][1] == "bf16":
+                ours, ref = GU.bf16_to_f32(bits16(p.data).reshape(-1)), GU.bf16_to_f32(rp)
+                before = prev.get(pi, GU.bf16_to_f32(d[f"p{pi}_init"].reshape(-1)))
+            else:
+                ours, ref = to_np(p.data).reshape(-1), rp
+                before = prev.get(pi, d[f"p{pi}_init"].reshape(-1))
+            scale[pi] = np.maximum(scale.get(pi, 0.0), np.abs(ref.astype(np.float64) - before))
+            ok = GU.p_close(ours, ref, scale[pi])
+            assert ok.all(), f"{tag}: {np.sum(~ok)} params off"
+            prev[pi] = ref
+            if "compressed_v" in st:
+                np.testing.assert_array_equal(to_np(st["compressed_v"]["indices"]),
+                                              d[f"s{s}_vidx{pi}"], err_msg=tag)
+                np.testing.assert_array_equal(bits16(st["compressed_v"]["scales"]).reshape(-1),
+                                              d[f"s{s}_vhdr{pi}"].reshape(-1), err_msg=tag)
+            if "m_mgr" in st:
+                enc = st["m_mgr"]._encoded
+                np.testing.assert_array_equal(to_np(enc["labels"]), d[f"s{s}_labels{pi}"],
+                                              err_msg=tag)
+                np.testing.assert_array_equal(to_np(enc["sign_packed"]), d[f"s{s}_signs{pi}"],
+                                              err_msg=tag)
+                np.testing.assert_array_equal(to_np(enc["block_norms"]), d[f"s{s}_norms{pi}"],
+                                              err_msg=tag)
+                np.testing.assert_array_equal(bits16(enc["scales"]), d[f"s{s}_amp{pi}"],
+                                              err_msg=tag)
+            if "exp_avg" in st:
+                np.testing.assert_array_equal(to_np(st["exp_avg"]).reshape(-1),
+                                              d[f"s{s}_m{pi}"].reshape(-1), err_msg=tag)
+            if "exp_avg_sq" in st:
+                np.testing.assert_array_equal(to_np(st["exp_avg_sq"]).reshape(-1),
+                                              d[f"s{s}_vsq{pi}"].reshape(-1), err_msg=tag)
+    assert order
+
+
+def test_reference_costate_golden_on_gpu():
+    """CoStateManager.update seam on the GPU vs the reference, alpha injected."""
+    from turboadam_b200.costate import CoStateManager
+    from turboadam_b200.optimizer import _single_costate_update
+
+    d = GU.load("costate.npz")
+    for c in range(int(d["n_cases"][0])):
+        k = f"c{c:03d}"
+        n, ns = (int(x) for x in d[k + "_meta"])
+        lo, hi = (float(x) for x in d[k + "_pct"])
+        mgr = CoStateManager(128, null_pct=lo, amp_pct=hi)
+        for s in range(ns):
+            m = _single_costate_update(mgr, cuda(d[f"{k}_s{s}_g"]), 0.9,
+                                       alpha_inject=cuda(d[f"{k}_s{s}_alpha"]))
+            torch.cuda.synchronize()
+            tag = f"{k} step {s}"
+            enc = mgr._encoded
+            np.testing.assert_array_equal(to_np(m), d[f"{k}_s{s}_m_new"], err_msg=tag)
+            np.testing.assert_array_equal(to_np(enc["labels"]), d[f"{k}_s{s}_labels"], err_msg=tag)
+            np.testing.assert_array_equal(to_np(enc["sign_packed"]), d[f"{k}_s{s}_signs"],
+                                          err_msg=tag)
+            np.testing.assert_array_equal(to_np(enc["block_norms"]), d[f"{k}_s{s}_norms"],
+                                          err_msg=tag)
+            np.testing.assert_array_equal(bits16(enc["scales"]), d[f"{k}_s{s}_amp"], err_msg=tag)
+
+
+def test_v_update_golden_on_gpu():
+    """fused_v_update seam on the GPU vs the reference (uniforms injected)."""
+    from turboadam_b200.oneq import fused_v_update
+
+    d = GU.load("v_update.npz")
+    beta2 = float(d["beta2"][0])
+    for c in range(int(d["n_cases"][0])):
+        k = f"c{c:03d}"
+        nbits, n, ns = (int(x) for x in d[k + "_meta"])
+        for s in range(ns):
+            ni, nh, v = fused_v_update(cuda(d[f"{k}_s{s}_idx_in"]),
+                                       cuda(d[f"{k}_s{s}_hdr_in"].view(np.float16)),
+                                       cuda(d[f"{k}_s{s}_g"]), beta2, nbits, 128, n,
+                                       rand_buf=cuda(d[f"{k}_s{s}_u"]))
+            tag = f"{k} s{s}"
+            np.testing.assert_array_equal(to_np(ni), d[f"{k}_s{s}_idx_out"], err_msg=tag)
+            np.testing.assert_array_equal(bits16(nh).reshape(-1),
+                                          d[f"{k}_s{s}_hdr_out"].reshape(-1), err_msg=tag)
+            rv = d[f"{k}_s{s}_v_out"]
+            rel = np.abs(to_np(v).astype(np.float64) - rv) / np.maximum(np.abs(rv), 1e-45)
+            assert rel.max() <= 1e-6, tag

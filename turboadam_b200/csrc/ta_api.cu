@@ -1,0 +1,652 @@
+// ta_api.cu -- host side of the C ABI (include/turboadam_b200.h): argument
+// validation, per-tensor constant derivation (exactly as torch rounds the
+// Python scalars), workspace carving, multi-tensor launch lists and the
+// fixed kernel sequence of one optimizer step.
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string.h>
+
+#include <algorithm>
+#include <cmath>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/turboadam_b200.h"
+#include "ta_codec.cuh"
+#include "ta_kernels.cuh"
+
+using namespace ta;
+
+namespace {
+
+thread_local std::string g_err;
+
+ta_status fail(ta_status s, const std::string& m) {
+  g_err = m;
+  return s;
+}
+
+#define TA_CU(x)                                                                  \
+  do {                                                                            \
+    cudaError_t e_ = (x);                                                         \
+    if (e_ != cudaSuccess)                                                        \
+      return fail(TA_ERR_CUDA, std::string(#x) + ": " + cudaGetErrorString(e_));  \
+  } while (0)
+
+inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+inline size_t al256(size_t x) { return (x + 255) & ~(size_t)255; }
+inline bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
+int sm_count() {
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+// Python int(pct * n) (trunc toward zero of an IEEE double product),
+// costate.py:116-117.
+void threshold_ranks(int64_t B, double null_pct, double amp_pct, int64_t* lo, int64_t* hi) {
+  int64_t a = (int64_t)(null_pct * (double)B) - 1;
+  int64_t b = (int64_t)(amp_pct * (double)B);
+  *lo = a < 0 ? 0 : a;
+  *hi = b > B - 1 ? B - 1 : b;
+}
+
+// ---- workspace layout ---------------------------------------------------
+constexpr int kMaxLists = 32;
+
+struct CsSlot {
+  size_t part, ratios, hist, sel, alpha;
+};
+
+struct Layout {
+  size_t status = 0;
+  size_t table = 0;
+  size_t lists = 0;
+  size_t list_stride = 0;
+  std::vector<CsSlot> cs;  // per CoState tensor
+  size_t total = 0;
+};
+
+Layout layout_for(int nT, const std::vector<int64_t>& cs_bpad) {
+  Layout L;
+  size_t off = 0;
+  L.status = off;
+  off += 256;
+  L.table = off;
+  off = al256(off + (size_t)nT * sizeof(DevTensor));
+  L.lists = off;
+  L.list_stride = al256((size_t)(nT + 1) * sizeof(int64_t) + (size_t)nT * sizeof(int32_t));
+  off += L.list_stride * kMaxLists;
+  for (int64_t bp : cs_bpad) {
+    CsSlot s;
+    s.part = off;
+    off = al256(off + (size_t)bp * 2 * 4);
+    s.ratios = off;
+    off = al256(off + (size_t)bp * 4);
+    s.hist = off;
+    off = al256(off + (size_t)3 * 2 * HBINS * 4);
+    s.sel = off;
+    off = al256(off + 16 * 4);
+    s.alpha = off;
+    off = al256(off + 4 * 4);
+    L.cs.push_back(s);
+  }
+  L.total = off;
+  return L;
+}
+
+bool is_costate(const ta_tensor& t) { return (t.flags & TA_M_COSTATE) != 0; }
+
+std::vector<int64_t> cs_bpads(const ta_tensor* ts, int n) {
+  std::vector<int64_t> v;
+  for (int i = 0; i < n; ++i)
+    if (ts[i].numel > 0 && is_costate(ts[i])) v.push_back(cdiv(cdiv(ts[i].numel, BS), TB) * TB);
+  return v;
+}
+
+// ---- kernel registry (one-time attribute setup, occupancy) --------------
+template <typename K>
+int setup_kernel(K kern, size_t smem, int threads) {
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  int occ = 0;
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, threads, smem);
+  return occ > 0 ? occ : 1;
+}
+
+struct LaunchList {
+  std::vector<int64_t> beg;  // tile (or chunk) prefix, size n+1
+  std::vector<int32_t> idx;
+};
+
+template <int MK, int VK, int PT, bool UNI>
+ta_status launch_p1(const KParams& kp, cudaStream_t s) {
+  constexpr size_t smem = p1_smem_bytes<MK, VK, PT, UNI>();
+  static std::once_flag once;
+  static int occ = 1;
+  std::call_once(once, [] { occ = setup_kernel(k_pass1<MK, VK, PT, UNI>, smem, NTHR); });
+  int64_t grid = std::min<int64_t>(kp.total, (int64_t)sm_count() * occ);
+  if (grid <= 0) return TA_OK;
+  k_pass1<MK, VK, PT, UNI><<<(unsigned)grid, NTHR, smem, s>>>(kp);
+  TA_CU(cudaGetLastError());
+  return TA_OK;
+}
+
+template <int MK, int VK, int PT>
+ta_status launch_p1_u(bool uni, const KParams& kp, cudaStream_t s) {
+  return uni ? launch_p1<MK, VK, PT, true>(kp, s) : launch_p1<MK, VK, PT, false>(kp, s);
+}
+
+ta_status dispatch_p1(int mk, int vk, int pt, bool uni, const KParams& kp, cudaStream_t s) {
+#define TA_P1(M, V)                                                      \
+  if (mk == M && vk == V)                                                \
+    return pt ? launch_p1_u<M, V, 1>(uni, kp, s) : launch_p1_u<M, V, 0>(uni, kp, s);
+  TA_P1(MK_COSTATE, VK_ONEQ)
+  TA_P1(MK_COSTATE, VK_FP32)
+  TA_P1(MK_COSTATE, VK_NONE)
+  TA_P1(MK_FP32, VK_ONEQ)
+  TA_P1(MK_FP32, VK_FP32)
+  TA_P1(MK_NONE, VK_ONEQ)
+#undef TA_P1
+  return fail(TA_ERR_UNSUPPORTED, "moment combination not built");
+}
+
+template <int PT>
+ta_status launch_p2(const KParams& kp, cudaStream_t s) {
+  constexpr size_t smem = p2_smem_bytes<PT>();
+  static std::once_flag once;
+  static int occ = 1;
+  std::call_once(once, [] { occ = setup_kernel(k_pass2<PT>, smem, NTHR); });
+  int64_t grid = std::min<int64_t>(kp.total, (int64_t)sm_count() * occ);
+  if (grid <= 0) return TA_OK;
+  k_pass2<PT><<<(unsigned)grid, NTHR, smem, s>>>(kp);
+  TA_CU(cudaGetLastError());
+  return TA_OK;
+}
+
+int mk_of(const ta_tensor& t) {
+  if (t.flags & TA_M_COSTATE) return MK_COSTATE;
+  return t.exp_avg_dev ? MK_FP32 : MK_NONE;
+}
+int vk_of(const ta_tensor& t) {
+  if (t.flags & TA_V_ONEQ) return VK_ONEQ;
+  return t.exp_avg_sq_dev ? VK_FP32 : VK_NONE;
+}
+
+ta_status validate(const ta_tensor& t, int i, int n_groups, const ta_group* groups) {
+  auto bad = [&](const char* what) {
+    return fail(TA_ERR_INVALID, "tensor " + std::to_string(i) + ": " + what);
+  };
+  if (t.numel < 0) return bad("negative numel");
+  if (t.numel == 0) return TA_OK;
+  if (t.dtype != TA_F32 && t.dtype != TA_BF16) return bad("dtype must be TA_F32 or TA_BF16");
+  if (t.group < 0 || t.group >= n_groups) return bad("group index out of range");
+  const ta_group& g = groups[t.group];
+  if (g.block_size != BS)
+    return fail(TA_ERR_UNSUPPORTED, "tensor " + std::to_string(i) + ": block_size " +
+                                        std::to_string(g.block_size) + " (only 128 is built)");
+  if ((t.flags & TA_V_ONEQ) && !(g.v_bits == 2 || g.v_bits == 3 || g.v_bits == 4 ||
+                                 g.v_bits == 6 || g.v_bits == 8))
+    return bad("v_bits must be one of {2, 3, 4, 6, 8}");
+  if (t.step == 0) return bad("step must be >= 1 (count after increment)");
+  const bool param = !(t.flags & TA_NO_PARAM);
+  if (!t.grad_dev) return bad("null grad");
+  if (param && !t.param_dev) return bad("null param");
+  const int mk = mk_of(t), vk = vk_of(t);
+  if (param && (mk == MK_NONE || vk == VK_NONE))
+    return bad("parameter update needs both moments (set exp_avg / exp_avg_sq or flags)");
+  if (mk == MK_COSTATE && (!t.m_labels_dev || !t.m_signs_dev || !t.m_norms_dev ||
+                           !t.m_amp_dev || !t.m_alpha_dev))
+    return bad("CoState state pointer missing");
+  if (vk == VK_ONEQ && (!t.v_idx_dev || !t.v_hdr_dev)) return bad("1Q state pointer missing");
+  const void* al[] = {t.param_dev, t.grad_dev, t.v_idx_dev, t.v_hdr_dev, t.exp_avg_sq_dev,
+                      t.m_labels_dev, t.m_signs_dev, t.m_norms_dev, t.m_amp_dev, t.exp_avg_dev,
+                      t.sr_uniforms_dev};
+  for (const void* p : al)
+    if (p && !aligned16(p))
+      return fail(TA_ERR_ALIGN, "tensor " + std::to_string(i) + ": pointer not 16-byte aligned");
+  return TA_OK;
+}
+
+DevTensor make_dev(const ta_tensor& t, const ta_group& g, uint64_t seed) {
+  DevTensor D;
+  memset(&D, 0, sizeof(D));
+  D.p = t.param_dev;
+  D.g = t.grad_dev;
+  D.v_idx = t.v_idx_dev;
+  D.v_hdr = t.v_hdr_dev;
+  D.eas = t.exp_avg_sq_dev;
+  D.lab = t.m_labels_dev;
+  D.sgn = t.m_signs_dev;
+  D.nrm = t.m_norms_dev;
+  D.amp = t.m_amp_dev;
+  D.alpha_state = t.m_alpha_dev;
+  D.ea = t.exp_avg_dev;
+  D.uni = t.sr_uniforms_dev;
+  D.alpha_inj = t.alpha_inject_dev;
+  D.m_out = t.m_out_dev;
+  D.v_out = t.v_out_dev;
+  D.n = t.numel;
+  D.nblk = cdiv(t.numel, BS);
+  D.bpad = cdiv(D.nblk, TB) * TB;
+  threshold_ranks(D.nblk, g.null_pct, g.amp_pct, &D.k_lo, &D.k_hi);
+  // fp32 values of the Python scalars exactly as torch rounds them
+  D.b1 = (float)g.beta1;
+  D.omb1 = (float)(1.0 - g.beta1);
+  D.b2 = (float)g.beta2;
+  D.omb2 = (float)(1.0 - g.beta2);
+  D.wdf = (float)(1.0 - g.lr * g.weight_decay);
+  D.nlr = (float)(-g.lr);
+  D.eps = (float)g.eps;
+  D.bc1 = g.bc1;
+  D.bc2 = g.bc2;
+  D.rbc2 = 1.0f / g.bc2;
+  D.nbits = g.v_bits;
+  D.nbf = (float)(1 << g.v_bits);
+  D.sqbs = (float)std::sqrt((double)g.block_size);
+  uint32_t f = 0;
+  if (t.flags & TA_M_COSTATE) f |= DF_M_COSTATE;
+  if (t.flags & TA_V_ONEQ) f |= DF_V_ONEQ;
+  if (t.flags & TA_M_HAS_STATE) f |= DF_M_HAS_STATE;
+  if (t.flags & TA_NO_PARAM) f |= DF_NO_PARAM;
+  if (g.weight_decay != 0.0) f |= DF_WD;
+  if (t.sr_uniforms_dev) f |= DF_UNI;
+  if (t.alpha_inject_dev) f |= DF_ALPHA_INJ;
+  if (t.m_out_dev) f |= DF_M_OUT;
+  if (t.v_out_dev) f |= DF_V_OUT;
+  if (t.dtype == TA_BF16) f |= DF_BF16;
+  D.flags = f;
+  D.tid = t.tensor_id;
+  D.step = t.step;
+  D.seed_lo = (uint32_t)seed;
+  D.seed_hi = (uint32_t)(seed >> 32);
+  D.sel_chunks = (int32_t)cdiv(D.bpad, SEL_CHUNK);
+  return D;
+}
+
+// Runs the fixed kernel sequence for an already validated tensor list.
+// ev (optional, 5 entries, may be null individually): cudaEvent_t recorded on
+// `st` before pass 1, after pass 1, after alpha, after pass 2, after labels.
+ta_status run_step(const ta_tensor* ts, int nT, const ta_group* groups, uint64_t seed,
+                   uint8_t* ws, size_t ws_bytes, cudaStream_t st, void* const* ev = nullptr) {
+  auto mark = [&](int i) -> cudaError_t {
+    if (ev && ev[i]) return cudaEventRecord((cudaEvent_t)ev[i], st);
+    return cudaSuccess;
+  };
+  std::vector<int64_t> bp = cs_bpads(ts, nT);
+  Layout L = layout_for(nT, bp);
+  if (ws_bytes < L.total)
+    return fail(TA_ERR_WORKSPACE, "workspace too small: need " + std::to_string(L.total) +
+                                      " bytes, got " + std::to_string(ws_bytes));
+  std::vector<uint8_t> host(L.lists + L.list_stride * kMaxLists, 0);
+  DevTensor* H = reinterpret_cast<DevTensor*>(host.data() + L.table);
+  std::vector<int32_t> cs_list;
+  int ci = 0;
+  for (int i = 0; i < nT; ++i) {
+    if (ts[i].numel == 0) {
+      memset(&H[i], 0, sizeof(DevTensor));
+      continue;
+    }
+    H[i] = make_dev(ts[i], groups[ts[i].group], seed);
+    if (is_costate(ts[i])) {
+      const CsSlot& s = L.cs[ci++];
+      H[i].part = reinterpret_cast<float*>(ws + s.part);
+      H[i].ratios = reinterpret_cast<float*>(ws + s.ratios);
+      H[i].hist = reinterpret_cast<uint32_t*>(ws + s.hist);
+      H[i].sel = reinterpret_cast<uint32_t*>(ws + s.sel);
+      H[i].alpha_new = reinterpret_cast<float*>(ws + s.alpha);
+      cs_list.push_back(i);
+    }
+  }
+  // launch lists: pass 1 by (mk, vk, pt, uni), pass 2 by pt, select chunks
+  struct P1Key { int mk, vk, pt; bool uni; };
+  std::vector<std::pair<P1Key, LaunchList>> p1;
+  auto p1_list = [&](P1Key k) -> LaunchList& {
+    for (auto& e : p1)
+      if (e.first.mk == k.mk && e.first.vk == k.vk && e.first.pt == k.pt && e.first.uni == k.uni)
+        return e.second;
+    p1.push_back({k, LaunchList()});
+    p1.back().second.beg.push_back(0);
+    return p1.back().second;
+  };
+  LaunchList p2[2];
+  p2[0].beg.push_back(0);
+  p2[1].beg.push_back(0);
+  LaunchList sel;
+  sel.beg.push_back(0);
+  for (int i = 0; i < nT; ++i) {
+    if (ts[i].numel == 0) continue;
+    const DevTensor& D = H[i];
+    const int pt = ts[i].dtype == TA_BF16 ? 1 : 0;
+    P1Key k{mk_of(ts[i]), vk_of(ts[i]), pt, (D.flags & DF_UNI) && vk_of(ts[i]) == VK_ONEQ};
+    LaunchList& l = p1_list(k);
+    const int64_t tiles = cdiv(D.nblk, TB);
+    l.idx.push_back(i);
+    l.beg.push_back(l.beg.back() + tiles);
+    if (is_costate(ts[i])) {
+      p2[pt].idx.push_back(i);
+      p2[pt].beg.push_back(p2[pt].beg.back() + tiles);
+      sel.idx.push_back(i);
+      sel.beg.push_back(sel.beg.back() + D.sel_chunks);
+    }
+  }
+  // serialise the lists into the host image of the workspace
+  int slot = 0;
+  auto put = [&](const LaunchList& l, const int64_t** dbeg, const int32_t** didx) {
+    uint8_t* base = host.data() + L.lists + L.list_stride * slot;
+    memcpy(base, l.beg.data(), l.beg.size() * sizeof(int64_t));
+    memcpy(base + (size_t)(nT + 1) * sizeof(int64_t), l.idx.data(),
+           l.idx.size() * sizeof(int32_t));
+    *dbeg = reinterpret_cast<const int64_t*>(ws + L.lists + L.list_stride * slot);
+    *didx = reinterpret_cast<const int32_t*>(ws + L.lists + L.list_stride * slot +
+                                             (size_t)(nT + 1) * sizeof(int64_t));
+    ++slot;
+  };
+  std::vector<KParams> p1k(p1.size());
+  uint32_t* status = reinterpret_cast<uint32_t*>(ws + L.status);
+  const DevTensor* dT = reinterpret_cast<const DevTensor*>(ws + L.table);
+  for (size_t i = 0; i < p1.size(); ++i) {
+    KParams& kp = p1k[i];
+    put(p1[i].second, &kp.lbeg, &kp.lidx);
+    kp.T = dT;
+    kp.nl = (int32_t)p1[i].second.idx.size();
+    kp.total = p1[i].second.beg.back();
+    kp.status = status;
+  }
+  KParams p2k[2];
+  for (int pt = 0; pt < 2; ++pt) {
+    put(p2[pt], &p2k[pt].lbeg, &p2k[pt].lidx);
+    p2k[pt].T = dT;
+    p2k[pt].nl = (int32_t)p2[pt].idx.size();
+    p2k[pt].total = p2[pt].beg.back();
+    p2k[pt].status = status;
+  }
+  SelParams sp;
+  sp.T = dT;
+  put(sel, &sp.cbeg, &sp.cidx);
+  sp.ncs = (int32_t)sel.idx.size();
+  const int64_t nchunks = sel.beg.back();
+  // the cs list for k_alpha reuses the select list's tensor indices
+  const int32_t* d_cs = sp.cidx;
+
+  TA_CU(cudaMemcpyAsync(ws + L.table, host.data() + L.table, host.size() - L.table,
+                        cudaMemcpyHostToDevice, st));
+  TA_CU(mark(0));
+  for (size_t i = 0; i < p1.size(); ++i) {
+    const P1Key& k = p1[i].first;
+    ta_status r = dispatch_p1(k.mk, k.vk, k.pt, k.uni, p1k[i], st);
+    if (r != TA_OK) return r;
+  }
+  TA_CU(mark(1));
+  if (!cs_list.empty()) {
+    k_alpha<<<(unsigned)cs_list.size(), FIN_THREADS, 0, st>>>(dT, d_cs, (int)cs_list.size());
+    TA_CU(cudaGetLastError());
+    TA_CU(mark(2));
+    if (p2k[0].total) {
+      ta_status r = launch_p2<0>(p2k[0], st);
+      if (r != TA_OK) return r;
+    }
+    if (p2k[1].total) {
+      ta_status r = launch_p2<1>(p2k[1], st);
+      if (r != TA_OK) return r;
+    }
+    TA_CU(mark(3));
+    k_select<0><<<(unsigned)nchunks, SEL_THREADS, 0, st>>>(sp);
+    k_select<1><<<(unsigned)nchunks, SEL_THREADS, 0, st>>>(sp);
+    k_select<2><<<(unsigned)nchunks, SEL_THREADS, 0, st>>>(sp);
+    k_labels<<<(unsigned)nchunks, SEL_THREADS, 0, st>>>(sp);
+    TA_CU(cudaGetLastError());
+  } else {
+    TA_CU(mark(2));
+    TA_CU(mark(3));
+  }
+  TA_CU(mark(4));
+  return TA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ta_abi_version(void) { return TA_ABI_VERSION; }
+
+const char* ta_last_error(void) { return g_err.c_str(); }
+
+int64_t ta_state_padded_blocks(int64_t n, int32_t block_size) {
+  if (n <= 0 || block_size <= 0) return 0;
+  return cdiv(cdiv(n, block_size), TB) * TB;
+}
+
+size_t ta_workspace_size(const ta_tensor* tensors, int32_t n_tensors) {
+  if (n_tensors < 0 || (n_tensors > 0 && !tensors)) return 0;
+  return layout_for(n_tensors, cs_bpads(tensors, n_tensors)).total;
+}
+
+ta_status ta_step(const ta_tensor* tensors, int32_t n_tensors, const ta_group* groups,
+                  int32_t n_groups, uint64_t seed, void* workspace_dev, size_t workspace_bytes,
+                  void* stream) {
+  g_err.clear();
+  if (n_tensors < 0 || (n_tensors > 0 && (!tensors || !groups)) || n_groups < 0)
+    return fail(TA_ERR_INVALID, "bad tensor / group arrays");
+  if (!workspace_dev || !aligned16(workspace_dev))
+    return fail(TA_ERR_INVALID, "workspace must be a 16-byte aligned device pointer");
+  for (int i = 0; i < n_tensors; ++i) {
+    ta_status r = validate(tensors[i], i, n_groups, groups);
+    if (r != TA_OK) return r;
+  }
+  return run_step(tensors, n_tensors, groups, seed, (uint8_t*)workspace_dev, workspace_bytes,
+                  (cudaStream_t)stream);
+}
+
+ta_status ta_step_profiled(const ta_tensor* tensors, int32_t n_tensors, const ta_group* groups,
+                           int32_t n_groups, uint64_t seed, void* workspace_dev,
+                           size_t workspace_bytes, void* stream, void* const* phase_events) {
+  g_err.clear();
+  if (n_tensors < 0 || (n_tensors > 0 && (!tensors || !groups)) || n_groups < 0)
+    return fail(TA_ERR_INVALID, "bad tensor / group arrays");
+  if (!workspace_dev || !aligned16(workspace_dev))
+    return fail(TA_ERR_INVALID, "workspace must be a 16-byte aligned device pointer");
+  for (int i = 0; i < n_tensors; ++i) {
+    ta_status r = validate(tensors[i], i, n_groups, groups);
+    if (r != TA_OK) return r;
+  }
+  return run_step(tensors, n_tensors, groups, seed, (uint8_t*)workspace_dev, workspace_bytes,
+                  (cudaStream_t)stream, phase_events);
+}
+
+ta_status ta_read_status(void* workspace_dev, int32_t clear, uint32_t* status_out,
+                         void* stream) {
+  if (!workspace_dev || !status_out) return fail(TA_ERR_INVALID, "null argument");
+  cudaStream_t st = (cudaStream_t)stream;
+  uint32_t v = 0;
+  TA_CU(cudaMemcpyAsync(&v, workspace_dev, 4, cudaMemcpyDeviceToHost, st));
+  if (clear) TA_CU(cudaMemsetAsync(workspace_dev, 0, 4, st));
+  TA_CU(cudaStreamSynchronize(st));
+  *status_out = v;
+  return TA_OK;
+}
+
+size_t ta_aux_workspace_size(int64_t n) {
+  if (n <= 0) return 0;
+  const int64_t bpad = cdiv(cdiv(n, BS), TB) * TB;
+  ta_tensor t;
+  memset(&t, 0, sizeof(t));
+  t.numel = n;
+  t.flags = TA_M_COSTATE;
+  const size_t step_ws = layout_for(1, {bpad}).total;
+  // padded 1Q copies for the single-tensor seams: idx + hdr
+  return al256(step_ws) + al256((size_t)bpad * BS) + al256((size_t)bpad * 4);
+}
+
+ta_status ta_v_init(int64_t n, int32_t block_size, uint8_t* idx_dev, uint16_t* hdr_dev,
+                    void* stream) {
+  g_err.clear();
+  if (n <= 0 || !idx_dev || !hdr_dev) return fail(TA_ERR_INVALID, "bad arguments");
+  if (block_size != BS) return fail(TA_ERR_UNSUPPORTED, "only block_size 128 is built");
+  // compress_v_logscale(full(1e-30), stochastic_round=False): min == max
+  const float l = ta_logf(1e-30f);
+  const uint16_t h = ta_f32_to_f16(l);
+  const int64_t nblk = cdiv(n, BS);
+  const int grid = (int)std::min<int64_t>(cdiv(nblk * BS, 256), (int64_t)sm_count() * 8);
+  k_v_init<<<grid, 256, 0, (cudaStream_t)stream>>>(idx_dev, hdr_dev, nblk, h);
+  TA_CU(cudaGetLastError());
+  return TA_OK;
+}
+
+ta_status ta_v_decode(const uint8_t* idx_dev, const uint16_t* hdr_dev, int64_t n,
+                      int32_t block_size, int32_t v_bits, float* v_out_dev, void* stream) {
+  g_err.clear();
+  if (n <= 0 || !idx_dev || !hdr_dev || !v_out_dev) return fail(TA_ERR_INVALID, "bad arguments");
+  if (block_size != BS) return fail(TA_ERR_UNSUPPORTED, "only block_size 128 is built");
+  if (v_bits < 1 || v_bits > 8) return fail(TA_ERR_INVALID, "v_bits out of range");
+  const int grid = (int)std::min<int64_t>(cdiv(n, 256), (int64_t)sm_count() * 8);
+  k_v_decode<<<grid, 256, 0, (cudaStream_t)stream>>>(idx_dev, hdr_dev, n,
+                                                      (float)(1 << v_bits), v_out_dev);
+  TA_CU(cudaGetLastError());
+  return TA_OK;
+}
+
+ta_status ta_v_update(const uint8_t* idx_dev, const uint16_t* hdr_dev, const void* grad_dev,
+                      int32_t grad_dtype, int64_t n, int32_t block_size, int32_t v_bits,
+                      double beta2, const float* uniforms_dev, uint64_t seed,
+                      uint32_t tensor_id, uint32_t step, uint8_t* out_idx_dev,
+                      uint16_t* out_hdr_dev, float* v_out_dev, void* workspace_dev,
+                      size_t workspace_bytes, void* stream) {
+  g_err.clear();
+  if (n <= 0 || !idx_dev || !hdr_dev || !grad_dev || !out_idx_dev || !out_hdr_dev ||
+      !workspace_dev)
+    return fail(TA_ERR_INVALID, "bad arguments");
+  if (workspace_bytes < ta_aux_workspace_size(n))
+    return fail(TA_ERR_WORKSPACE, "workspace too small (ta_aux_workspace_size)");
+  cudaStream_t st = (cudaStream_t)stream;
+  const int64_t nblk = cdiv(n, BS), bpad = cdiv(nblk, TB) * TB;
+  uint8_t* ws = (uint8_t*)workspace_dev;
+  const size_t step_ws = al256(layout_for(1, {bpad}).total);
+  uint8_t* pidx = ws + step_ws;
+  uint16_t* phdr = reinterpret_cast<uint16_t*>(pidx + al256((size_t)bpad * BS));
+  TA_CU(cudaMemcpyAsync(pidx, idx_dev, (size_t)nblk * BS, cudaMemcpyDeviceToDevice, st));
+  TA_CU(cudaMemcpyAsync(phdr, hdr_dev, (size_t)nblk * 4, cudaMemcpyDeviceToDevice, st));
+  ta_tensor t;
+  memset(&t, 0, sizeof(t));
+  t.grad_dev = grad_dev;
+  t.numel = n;
+  t.dtype = grad_dtype;
+  t.group = 0;
+  t.flags = TA_V_ONEQ | TA_NO_PARAM;
+  t.tensor_id = tensor_id;
+  t.step = step ? step : 1;
+  t.v_idx_dev = pidx;
+  t.v_hdr_dev = phdr;
+  t.sr_uniforms_dev = uniforms_dev;
+  t.v_out_dev = v_out_dev;
+  ta_group g;
+  memset(&g, 0, sizeof(g));
+  g.beta2 = beta2;
+  g.beta1 = 0.9;
+  g.bc1 = g.bc2 = 1.0f;
+  g.block_size = block_size;
+  g.v_bits = v_bits;
+  g.null_pct = 0.1;
+  g.amp_pct = 0.9;
+  ta_status r = validate(t, 0, 1, &g);
+  if (r != TA_OK) return r;
+  r = run_step(&t, 1, &g, seed, ws, step_ws, st);
+  if (r != TA_OK) return r;
+  TA_CU(cudaMemcpyAsync(out_idx_dev, pidx, (size_t)nblk * BS, cudaMemcpyDeviceToDevice, st));
+  TA_CU(cudaMemcpyAsync(out_hdr_dev, phdr, (size_t)nblk * 4, cudaMemcpyDeviceToDevice, st));
+  return TA_OK;
+}
+
+ta_status ta_costate_decode(const uint8_t* labels_dev, const uint8_t* signs_dev,
+                            const float* norms_dev, const uint16_t* amp_dev,
+                            const float* alpha_dev, const void* grad_dev, int32_t grad_dtype,
+                            int64_t n, int32_t block_size, float* m_out_dev, void* stream) {
+  g_err.clear();
+  if (n <= 0 || !labels_dev || !signs_dev || !norms_dev || !amp_dev || !alpha_dev ||
+      !grad_dev || !m_out_dev)
+    return fail(TA_ERR_INVALID, "bad arguments");
+  if (block_size != BS) return fail(TA_ERR_UNSUPPORTED, "only block_size 128 is built");
+  const int grid = (int)std::min<int64_t>(cdiv(n, 256), (int64_t)sm_count() * 8);
+  const float sq = (float)std::sqrt((double)block_size);
+  if (grad_dtype == TA_BF16)
+    k_cs_decode<1><<<grid, 256, 0, (cudaStream_t)stream>>>(
+        labels_dev, signs_dev, norms_dev, amp_dev, alpha_dev, grad_dev, n, sq, m_out_dev);
+  else
+    k_cs_decode<0><<<grid, 256, 0, (cudaStream_t)stream>>>(
+        labels_dev, signs_dev, norms_dev, amp_dev, alpha_dev, grad_dev, n, sq, m_out_dev);
+  TA_CU(cudaGetLastError());
+  return TA_OK;
+}
+
+ta_status ta_costate_encode(const float* delta_dev, int64_t n, int32_t block_size,
+                            uint8_t* signs_dev, float* norms_dev, uint16_t* amp_dev,
+                            void* stream) {
+  g_err.clear();
+  if (n <= 0 || !delta_dev || !signs_dev || !norms_dev || !amp_dev)
+    return fail(TA_ERR_INVALID, "bad arguments");
+  if (block_size != BS) return fail(TA_ERR_UNSUPPORTED, "only block_size 128 is built");
+  const int64_t nblk = cdiv(n, BS);
+  const int64_t warps = cdiv(nblk, 4);
+  const int grid = (int)std::min<int64_t>(cdiv(warps * 32, 256), (int64_t)sm_count() * 8);
+  k_cs_encode<<<grid, 256, 0, (cudaStream_t)stream>>>(delta_dev, n, nblk,
+                                                      (float)std::sqrt((double)block_size),
+                                                      signs_dev, norms_dev, amp_dev);
+  TA_CU(cudaGetLastError());
+  return TA_OK;
+}
+
+ta_status ta_thresholds(const float* ratios_dev, int64_t n_blocks, double null_pct,
+                        double amp_pct, float* tau_dev, uint8_t* labels_dev,
+                        void* workspace_dev, size_t workspace_bytes, void* stream) {
+  g_err.clear();
+  if (n_blocks <= 0 || !ratios_dev || !tau_dev || !workspace_dev)
+    return fail(TA_ERR_INVALID, "bad arguments");
+  const int64_t bpad = cdiv(n_blocks, TB) * TB;
+  Layout L = layout_for(1, {bpad});
+  if (workspace_bytes < L.total) return fail(TA_ERR_WORKSPACE, "workspace too small");
+  cudaStream_t st = (cudaStream_t)stream;
+  uint8_t* ws = (uint8_t*)workspace_dev;
+  std::vector<uint8_t> host(L.lists + L.list_stride, 0);
+  DevTensor* H = reinterpret_cast<DevTensor*>(host.data() + L.table);
+  memset(H, 0, sizeof(DevTensor));
+  H->n = n_blocks * BS;
+  H->nblk = n_blocks;
+  H->bpad = bpad;
+  threshold_ranks(n_blocks, null_pct, amp_pct, &H->k_lo, &H->k_hi);
+  H->ratios = const_cast<float*>(ratios_dev);
+  H->hist = reinterpret_cast<uint32_t*>(ws + L.cs[0].hist);
+  H->sel = reinterpret_cast<uint32_t*>(ws + L.cs[0].sel);
+  H->alpha_new = reinterpret_cast<float*>(ws + L.cs[0].alpha);
+  H->lab = labels_dev;
+  H->sel_chunks = (int32_t)cdiv(n_blocks, SEL_CHUNK);
+  int64_t* beg = reinterpret_cast<int64_t*>(host.data() + L.lists);
+  beg[0] = 0;
+  beg[1] = H->sel_chunks;
+  int32_t* idx = reinterpret_cast<int32_t*>(host.data() + L.lists + 2 * sizeof(int64_t));
+  idx[0] = 0;
+  TA_CU(cudaMemcpyAsync(ws + L.table, host.data() + L.table, host.size() - L.table,
+                        cudaMemcpyHostToDevice, st));
+  // zero histograms / counters, set the ranks (what k_alpha does in a step)
+  TA_CU(cudaMemsetAsync(ws + L.cs[0].hist, 0, (size_t)3 * 2 * HBINS * 4, st));
+  uint32_t sel0[16] = {0};
+  sel0[SEL_RLO] = (uint32_t)H->k_lo;
+  sel0[SEL_RHI] = (uint32_t)H->k_hi;
+  TA_CU(cudaMemcpyAsync(ws + L.cs[0].sel, sel0, sizeof(sel0), cudaMemcpyHostToDevice, st));
+  SelParams sp;
+  sp.T = reinterpret_cast<const DevTensor*>(ws + L.table);
+  sp.cbeg = reinterpret_cast<const int64_t*>(ws + L.lists);
+  sp.cidx = reinterpret_cast<const int32_t*>(ws + L.lists + 2 * sizeof(int64_t));
+  sp.ncs = 1;
+  const unsigned nch = (unsigned)H->sel_chunks;
+  k_select<0><<<nch, SEL_THREADS, 0, st>>>(sp);
+  k_select<1><<<nch, SEL_THREADS, 0, st>>>(sp);
+  k_select<2><<<nch, SEL_THREADS, 0, st>>>(sp);
+  if (labels_dev) k_labels<<<nch, SEL_THREADS, 0, st>>>(sp);
+  TA_CU(cudaGetLastError());
+  TA_CU(cudaMemcpyAsync(tau_dev, ws + L.cs[0].alpha + 4, 8, cudaMemcpyDeviceToDevice, st));
+  return TA_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,177 @@
+// ta_device.cuh -- sm_100a device helpers: mbarrier pipeline, 1D TMA bulk
+// copies (cp.async.bulk, no multicast), warp utilities, and the per-tensor
+// descriptor shared by every kernel of the step.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "ta_math.h"
+
+namespace ta {
+
+constexpr int BS = 128;             // elements per quantisation block
+constexpr int TB = 16;              // blocks per work tile
+constexpr int TE = BS * TB;         // elements per work tile
+constexpr int NCW = 4;              // consumer warps per CTA (4 blocks each)
+constexpr int NTHR = (NCW + 1) * 32;// + one producer warp
+constexpr int NSTAGE = 3;           // smem pipeline depth
+constexpr uint32_t WAIT_LIMIT = 1u << 27;  // bounded mbarrier polling
+
+constexpr int FIN_THREADS = 256;    // alpha finalisation CTA
+constexpr int SEL_CHUNK = 4096;     // ratios per radix-select CTA
+constexpr int SEL_THREADS = 256;
+constexpr int HBINS = 2048;
+
+enum { MK_COSTATE = 0, MK_FP32 = 1, MK_NONE = 2 };
+enum { VK_ONEQ = 0, VK_FP32 = 1, VK_NONE = 2 };
+
+// DevTensor.flags (superset of the public TA_* flags)
+enum : uint32_t {
+  DF_M_COSTATE = 1u << 0,
+  DF_V_ONEQ = 1u << 1,
+  DF_M_HAS_STATE = 1u << 2,
+  DF_NO_PARAM = 1u << 3,
+  DF_WD = 1u << 8,
+  DF_UNI = 1u << 9,
+  DF_ALPHA_INJ = 1u << 10,
+  DF_M_OUT = 1u << 11,
+  DF_V_OUT = 1u << 12,
+  DF_BF16 = 1u << 13,
+};
+
+// Per-tensor descriptor, built on the host, uploaded into the workspace.
+struct __align__(16) DevTensor {
+  void* p;
+  const void* g;
+  uint8_t* v_idx;
+  uint16_t* v_hdr;
+  float* eas;
+  uint8_t* lab;
+  uint8_t* sgn;
+  float* nrm;
+  uint16_t* amp;
+  float* alpha_state;
+  float* ea;
+  const float* uni;
+  const float* alpha_inj;
+  float* m_out;
+  float* v_out;
+  // workspace (CoState tensors)
+  float* part;       // [2][bpad] per-block fp32 partial dots (m.g, g.g)
+  float* ratios;     // [bpad]
+  uint32_t* hist;    // [3][2][HBINS]
+  uint32_t* sel;     // [16] select state
+  float* alpha_new;  // [4]: alpha_new, tau0, tau1
+  int64_t n;
+  int64_t nblk;
+  int64_t bpad;      // nblk rounded up to whole tiles
+  int64_t k_lo, k_hi;
+  float b1, omb1, b2, omb2;
+  float wdf, nlr, eps, bc1;
+  float bc2, rbc2, nbf, sqbs;
+  int32_t nbits;
+  uint32_t flags;
+  uint32_t tid;
+  uint32_t step;
+  uint32_t seed_lo, seed_hi;
+  int32_t sel_chunks;  // ceil(bpad / SEL_CHUNK)
+  int32_t pad_;
+};
+
+// sel[] layout
+enum { SEL_CNT0 = 0, SEL_CNT1 = 1, SEL_CNT2 = 2, SEL_PLO = 4, SEL_PHI = 5, SEL_RLO = 6,
+       SEL_RHI = 7 };
+
+// ---- PTX wrappers --------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+               : "memory");
+}
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ uint32_t mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok;
+}
+// Bounded wait: gives up after WAIT_LIMIT polls, records the timeout in the
+// status word and reports false so the caller can drain and return.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status) {
+  for (uint32_t i = 0; i < WAIT_LIMIT; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  atomicOr(status, 2u /* TA_STATUS_WAIT_TIMEOUT */);
+  return false;
+}
+// 1D bulk async copy global -> shared, completion counted on `bar`.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
+                                         uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+// 1D bulk async copy shared -> global (bulk-group completion).
+__device__ __forceinline__ void bulk_s2g(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst),
+               "r"(smem_u32(src)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+// ---- arithmetic helpers (bit-identical to the host checker) ------------
+// torch clamp(min=lo) semantics: NaN propagates.
+__device__ __forceinline__ float clamp_min(float v, float lo) { return (v < lo) ? lo : v; }
+
+// a / b, correctly rounded, given y = RN(1/b) (Markstein: q = RN(a*y),
+// r = a - b*q exact by FMA, RN(q + r*y) = RN(a/b) when nothing under- or
+// overflows); falls back to the IEEE division outside a safe range.
+__device__ __forceinline__ float div_by(float a, float b, float y) {
+  float aa = fabsf(a);
+  if (aa < 0x1p100f && (aa >= 0x1p-100f || a == 0.0f)) {
+    float q = __fmul_rn(a, y);
+    float r = __fmaf_rn(-q, b, a);
+    return __fmaf_rn(r, y, q);
+  }
+  return __fdiv_rn(a, b);
+}
+
+__device__ __forceinline__ float ld_elem_f32(const float* p) { return *p; }
+
+template <int PT>
+__device__ __forceinline__ float to_f32(const void* base, int64_t i) {
+  if (PT == 0) return reinterpret_cast<const float*>(base)[i];
+  return ta_bf16_to_f32(reinterpret_cast<const uint16_t*>(base)[i]);
+}
+
+}  // namespace ta

@@ -1,0 +1,845 @@
+// ta_kernels.cuh -- B200 (sm_100a) kernels of the fused TurboAdam step
+// (launched by ta_api.cu, the C-ABI of include/turboadam_b200.h).
+//
+// Data flow of one step (all tensors of a kind share one launch):
+//   pass 1  (HBM stream over p, g and packed state; 1D TMA bulk copies into a
+//            3-stage smem ring, one producer warp, four consumer warps):
+//            weight decay, m update (CoState decode+EMA or fp32 EMA), v update
+//            (1Q decode -> EMA -> Philox stochastic re-quantisation, or fp32
+//            EMA), p.addcdiv_, per-block partial dots m.g and g.g.
+//   finalise alpha = (m.g)/(g.g) per CoState tensor (fixed-order fp64 sum).
+//   pass 2  (CoState tensors: re-read g and the old encoding, recompute m_new
+//            bit-identically, delta = m - alpha g, MSB-first sign bits, torch-
+//            order block norms, fp16 scales, block ratios).
+//   select  exact P10/P90 of the ratios: 3 histogram rounds over the fp32 bit
+//            pattern (11/11/10 bits), the last CTA of each tensor scans.
+//   labels  0/1/2 by >= thresholds, alpha committed to the state.
+// Arithmetic matches the reference CPU path op by op (see oracle/ta_oracle.c,
+// which restates it) and ta_math.h for log/exp/fp16/Philox.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "ta_device.cuh"
+#include "ta_math.h"
+
+namespace ta {
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded mbarrier wait against wall time (2 s), see ta_device.cuh.
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, uint32_t* status) {
+  if (mbar_try_wait(bar, parity)) return true;
+  uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (globaltimer_ns() - t0 > 2000000000ull) {
+      atomicOr(status, 2u);
+      return false;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Stage layouts
+// ---------------------------------------------------------------------------
+template <int MK, int VK, int PT, bool UNI>
+struct P1L {
+  static constexpr int ESZ = PT ? 2 : 4;
+  static constexpr int STR_P = BS * ESZ + (PT ? 16 : 32);  // skewed block stride
+  static constexpr int STR_4 = BS * 4 + 32;
+  static constexpr int STR_1 = BS + 16;
+  static constexpr int OFF_P = 0;
+  static constexpr int OFF_G = OFF_P + TB * STR_P;
+  static constexpr int OFF_IDX = OFF_G + TB * STR_P;
+  static constexpr int OFF_HDR = OFF_IDX + (VK == VK_ONEQ ? TB * STR_1 : 0);
+  static constexpr int OFF_EAS = OFF_HDR + (VK == VK_ONEQ ? TB * 4 : 0);
+  static constexpr int OFF_LAB = OFF_EAS + (VK == VK_FP32 ? TB * STR_4 : 0);
+  static constexpr int OFF_SGN = OFF_LAB + (MK == MK_COSTATE ? 16 : 0);
+  static constexpr int OFF_NRM = OFF_SGN + (MK == MK_COSTATE ? TB * 16 : 0);
+  static constexpr int OFF_AMP = OFF_NRM + (MK == MK_COSTATE ? TB * 4 : 0);
+  static constexpr int OFF_EA = OFF_AMP + (MK == MK_COSTATE ? TB * 2 : 0);
+  static constexpr int OFF_UNI = OFF_EA + (MK == MK_FP32 ? TB * STR_4 : 0);
+  static constexpr int END = OFF_UNI + ((UNI && VK == VK_ONEQ) ? TB * STR_4 : 0);
+  static constexpr int STAGE = (END + 127) / 128 * 128;
+};
+
+template <int PT>
+struct P2L {
+  static constexpr int ESZ = PT ? 2 : 4;
+  static constexpr int STR_G = BS * ESZ + (PT ? 16 : 32);
+  static constexpr int OFF_G = 0;
+  static constexpr int OFF_LAB = OFF_G + TB * STR_G;
+  static constexpr int OFF_SGN = OFF_LAB + 16;
+  static constexpr int OFF_NRM = OFF_SGN + TB * 16;
+  static constexpr int OFF_AMP = OFF_NRM + TB * 4;
+  static constexpr int OFF_RAT = OFF_AMP + TB * 2;
+  static constexpr int END = OFF_RAT + TB * 4;
+  static constexpr int STAGE = (END + 127) / 128 * 128;
+};
+
+struct StageMeta {
+  int32_t t;     // tensor index
+  int32_t nblk;  // blocks of this tile
+  int64_t b0;    // first block (within tensor)
+};
+
+constexpr int TABLE_STRIDE = 65;  // per-group exp table (<= 64 entries), padded
+
+struct KParams {
+  const DevTensor* T;
+  const int64_t* lbeg;  // [nl + 1] tile prefix of the launch list
+  const int32_t* lidx;  // [nl] tensor indices
+  int32_t nl;
+  int64_t total;        // tiles in this launch
+  uint32_t* status;
+};
+
+__device__ __forceinline__ int find_entry(const int64_t* lbeg, int nl, int64_t tile) {
+  int lo = 0, hi = nl - 1;
+  while (lo < hi) {
+    int mid = (lo + hi + 1) >> 1;
+    if (lbeg[mid] <= tile) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
+}
+
+// Shared CoState decode of one element (costate.py:261-323, :416):
+//   m_hat = fl(fl(alpha_old*g) + fl(scale*sign)), m = fl(fl(b1*m_hat) + fl(omb1*g)).
+__device__ __forceinline__ float costate_m(float g, float alpha_old, float scale, uint32_t bit,
+                                           bool has_state, float b1, float omb1) {
+  float mh = 0.0f;
+  if (has_state) {
+    float sd = __fmul_rn(scale, bit ? -1.0f : 1.0f);
+    mh = __fadd_rn(__fmul_rn(alpha_old, g), sd);
+  }
+  return __fadd_rn(__fmul_rn(b1, mh), __fmul_rn(omb1, g));
+}
+
+__device__ __forceinline__ float costate_scale(uint8_t label, float norm, uint16_t amp,
+                                               float sqbs) {
+  if (label == 1) return __fdiv_rn(norm, sqbs);
+  if (label == 2) return ta_f16_to_f32(amp);
+  return 0.0f;
+}
+
+// ---------------------------------------------------------------------------
+// Pass 1
+// ---------------------------------------------------------------------------
+template <int MK, int VK, int PT, bool UNI>
+__device__ __forceinline__ void p1_issue(const DevTensor& D, uint8_t* st, int nblk, int64_t b0,
+                                         uint64_t* bar, bool count_only, uint32_t& bytes) {
+  using L = P1L<MK, VK, PT, UNI>;
+  const bool param = !(D.flags & DF_NO_PARAM);
+  bytes = 0;
+  auto cp = [&](void* dst, const void* src, uint32_t nb) {
+    bytes += nb;
+    if (!count_only) bulk_g2s(dst, src, nb, bar);
+  };
+  for (int i = 0; i < nblk; ++i) {
+    int64_t b = b0 + i;
+    int64_t e0 = b * BS;
+    bool full = (D.n - e0) >= BS;
+    if (full) {
+      if (param)
+        cp(st + L::OFF_P + i * L::STR_P, (const uint8_t*)D.p + e0 * L::ESZ, BS * L::ESZ);
+      cp(st + L::OFF_G + i * L::STR_P, (const uint8_t*)D.g + e0 * L::ESZ, BS * L::ESZ);
+      if (MK == MK_FP32) cp(st + L::OFF_EA + i * L::STR_4, D.ea + e0, BS * 4);
+      if (VK == VK_FP32) cp(st + L::OFF_EAS + i * L::STR_4, D.eas + e0, BS * 4);
+    }
+    if (VK == VK_ONEQ) {
+      cp(st + L::OFF_IDX + i * L::STR_1, D.v_idx + e0, BS);
+      if (UNI && (D.flags & DF_UNI)) cp(st + L::OFF_UNI + i * L::STR_4, D.uni + e0, BS * 4);
+    }
+  }
+  // per-tile arrays (state arrays are padded to whole tiles)
+  if (VK == VK_ONEQ) cp(st + L::OFF_HDR, D.v_hdr + b0 * 2, TB * 4);
+  if (MK == MK_COSTATE && (D.flags & DF_M_HAS_STATE)) {
+    cp(st + L::OFF_LAB, D.lab + b0, 16);
+    cp(st + L::OFF_SGN, D.sgn + b0 * 16, TB * 16);
+    cp(st + L::OFF_NRM, D.nrm + b0, TB * 4);
+    cp(st + L::OFF_AMP, D.amp + b0, TB * 2);
+  }
+}
+
+template <int MK, int VK, int PT, bool UNI>
+__device__ __forceinline__ void p1_store(const DevTensor& D, uint8_t* st, int nblk, int64_t b0) {
+  using L = P1L<MK, VK, PT, UNI>;
+  const bool param = !(D.flags & DF_NO_PARAM);
+  for (int i = 0; i < nblk; ++i) {
+    int64_t e0 = (b0 + i) * BS;
+    bool full = (D.n - e0) >= BS;
+    if (full) {
+      if (param) bulk_s2g((uint8_t*)D.p + e0 * L::ESZ, st + L::OFF_P + i * L::STR_P, BS * L::ESZ);
+      if (MK == MK_FP32) bulk_s2g(D.ea + e0, st + L::OFF_EA + i * L::STR_4, BS * 4);
+      if (VK == VK_FP32) bulk_s2g(D.eas + e0, st + L::OFF_EAS + i * L::STR_4, BS * 4);
+    }
+    if (VK == VK_ONEQ) bulk_s2g(D.v_idx + e0, st + L::OFF_IDX + i * L::STR_1, BS);
+  }
+  if (VK == VK_ONEQ) bulk_s2g(D.v_hdr + b0 * 2, st + L::OFF_HDR, TB * 4);
+}
+
+// One 128-element block per 8-lane group: lane j owns elements j + 8k.
+template <int MK, int VK, int PT, bool UNI>
+__device__ __forceinline__ void p1_block(const DevTensor& D, uint8_t* st, int nblk, int64_t b0,
+                                         float* table, uint32_t* status) {
+  using L = P1L<MK, VK, PT, UNI>;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int q = lane >> 3;
+  const int j = lane & 7;
+  const int bi = warp * 4 + q;
+  const bool active = bi < nblk;
+  const int64_t b = b0 + bi;
+  const int64_t e0 = b * BS;
+  const int nv = active ? (int)min((int64_t)BS, D.n - e0) : 0;
+  const bool full = nv == BS;
+  const bool param = !(D.flags & DF_NO_PARAM);
+
+  uint8_t* sp = st + L::OFF_P + bi * L::STR_P;
+  uint8_t* sg = st + L::OFF_G + bi * L::STR_P;
+
+  // ---- per-block CoState decode scalars (costate.py:290-314)
+  float cs_scale = 0.0f, alpha_old = 0.0f;
+  uint32_t sw[4] = {0, 0, 0, 0};
+  const bool has_state = (MK == MK_COSTATE) && (D.flags & DF_M_HAS_STATE);
+  if (MK == MK_COSTATE && has_state && active) {
+    uint8_t lab = st[L::OFF_LAB + bi];
+    float nrm = reinterpret_cast<const float*>(st + L::OFF_NRM)[bi];
+    uint16_t amp = reinterpret_cast<const uint16_t*>(st + L::OFF_AMP)[bi];
+    cs_scale = costate_scale(lab, nrm, amp, D.sqbs);
+    uint4 w = *reinterpret_cast<const uint4*>(st + L::OFF_SGN + bi * 16);
+    sw[0] = w.x; sw[1] = w.y; sw[2] = w.z; sw[3] = w.w;
+    alpha_old = *D.alpha_state;
+  }
+
+  // ---- per-block 1Q decode scalars (quantize.py:252-256) and exp table
+  float lmin = 0.0f, span = 0.0f;
+  const int nb = 1 << D.nbits;
+  const bool use_table = D.nbits <= 6;
+  if (VK == VK_ONEQ) {
+    const uint16_t* hdr = reinterpret_cast<const uint16_t*>(st + L::OFF_HDR);
+    if (active) {
+      lmin = ta_f16_to_f32(hdr[bi * 2]);
+      span = __fsub_rn(ta_f16_to_f32(hdr[bi * 2 + 1]), lmin);
+    }
+    if (use_table) {
+      for (int t = j; t < nb; t += 8) {
+        float qv = __fdiv_rn(__fadd_rn((float)t, 0.5f), D.nbf);
+        table[q * TABLE_STRIDE + t] = ta_expf(__fadd_rn(lmin, __fmul_rn(qv, span)));
+      }
+    }
+    __syncwarp();
+  }
+
+  // ---- phase A: m, v, log v per element
+  float mk[16], vk[16], lk[16];
+  float mg = 0.0f, gg = 0.0f, gbad = 0.0f;
+  float vmin = INFINITY, vmax = -INFINITY;
+  const float b1 = D.b1, omb1 = D.omb1, b2 = D.b2, omb2 = D.omb2;
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    const int t = j + 8 * k;
+    const int64_t e = e0 + t;
+    const bool ve = t < nv;
+    float g;
+    if (full) g = PT ? ta_bf16_to_f32(reinterpret_cast<const uint16_t*>(sg)[t])
+                     : reinterpret_cast<const float*>(sg)[t];
+    else g = ve ? to_f32<PT>(D.g, e) : 0.0f;
+    gbad = __fmaf_rn(g, 0.0f, gbad);
+    float m = 0.0f;
+    if (MK == MK_COSTATE) {
+      uint32_t bit = (sw[k >> 2] >> (8 * (k & 3) + 7 - j)) & 1u;
+      m = costate_m(g, alpha_old, cs_scale, bit, has_state, b1, omb1);
+      if (ve) {
+        mg = __fmaf_rn(m, g, mg);
+        gg = __fmaf_rn(g, g, gg);
+      }
+    } else if (MK == MK_FP32) {
+      float* sea = reinterpret_cast<float*>(st + L::OFF_EA + bi * L::STR_4);
+      float ea = full ? sea[t] : (ve ? D.ea[e] : 0.0f);
+      m = __fmaf_rn(g, omb1, __fmul_rn(ea, b1));  // optimizer.py:113
+      if (full) sea[t] = m;
+      else if (ve) D.ea[e] = m;
+    }
+    mk[k] = m;
+    float vn = 0.0f;
+    if (VK == VK_ONEQ) {
+      const int id = active ? st[L::OFF_IDX + bi * L::STR_1 + t] : 0;
+      float vo;
+      if (use_table && id < nb) vo = table[q * TABLE_STRIDE + id];
+      else {
+        float qv = __fdiv_rn(__fadd_rn((float)id, 0.5f), D.nbf);
+        vo = ta_expf(__fadd_rn(lmin, __fmul_rn(qv, span)));
+      }
+      float g2 = ve ? __fmul_rn(g, g) : 0.0f;
+      vn = __fmaf_rn(g2, omb2, __fmul_rn(vo, b2));  // quantize.py:270
+      float lv = ta_logf(clamp_min(vn, 1e-38f));   // quantize.py:275
+      lk[k] = lv;
+      if (ve) {
+        vmin = (lv < vmin) ? lv : vmin;
+        vmax = (lv > vmax) ? lv : vmax;
+      }
+    } else if (VK == VK_FP32) {
+      float* sea = reinterpret_cast<float*>(st + L::OFF_EAS + bi * L::STR_4);
+      float vs = full ? sea[t] : (ve ? D.eas[e] : 0.0f);
+      vn = __fmaf_rn(__fmul_rn(omb2, g), g, __fmul_rn(vs, b2));  // optimizer.py:166
+      if (full) sea[t] = vn;
+      else if (ve) D.eas[e] = vn;
+    }
+    vk[k] = vn;
+  }
+  if (gbad != gbad) atomicOr(status, 1u);
+
+  // ---- block partial dots for alpha (canonical order, see ta_oracle.c)
+  if (MK == MK_COSTATE) {
+#pragma unroll
+    for (int off = 4; off >= 1; off >>= 1) {
+      mg = __fadd_rn(mg, __shfl_xor_sync(0xffffffffu, mg, off));
+      gg = __fadd_rn(gg, __shfl_xor_sync(0xffffffffu, gg, off));
+    }
+    if (active && j == 0) {
+      D.part[b] = mg;
+      D.part[D.bpad + b] = gg;
+    }
+  }
+
+  // ---- 1Q block min/max, new header (quantize.py:276-285)
+  float mn = 0.0f, nspan = 1.0f, rspan = 1.0f;
+  if (VK == VK_ONEQ) {
+#pragma unroll
+    for (int off = 4; off >= 1; off >>= 1) {
+      float o1 = __shfl_xor_sync(0xffffffffu, vmin, off);
+      float o2 = __shfl_xor_sync(0xffffffffu, vmax, off);
+      vmin = (o1 < vmin) ? o1 : vmin;
+      vmax = (o2 > vmax) ? o2 : vmax;
+    }
+    mn = vmin;
+    if (active && j == 0) {
+      uint16_t* hdr = reinterpret_cast<uint16_t*>(st + L::OFF_HDR);
+      hdr[bi * 2] = ta_f32_to_f16(vmin);
+      hdr[bi * 2 + 1] = ta_f32_to_f16(vmax);
+    }
+    nspan = clamp_min(__fsub_rn(vmax, vmin), 1e-10f);
+    rspan = __frcp_rn(nspan);
+  }
+
+  // ---- phase B: stochastic re-quantisation and the parameter update
+  uint32_t rnd[4] = {0, 0, 0, 0};
+  const bool uni = UNI && (D.flags & DF_UNI);
+  const float* suni = reinterpret_cast<const float*>(st + L::OFF_UNI + bi * L::STR_4);
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    const int t = j + 8 * k;
+    const int64_t e = e0 + t;
+    const bool ve = t < nv;
+    if (VK == VK_ONEQ) {
+      float u;
+      if (uni) {
+        u = suni[t];
+      } else {
+        if ((k & 3) == 0) {
+          uint32_t c0, c1, c2, c3;
+          ta_sr_counter((uint64_t)b, (uint32_t)j, (uint32_t)(k >> 2), D.tid, D.step, &c0, &c1,
+                        &c2, &c3);
+          ta_philox4x32_10(c0, c1, c2, c3, D.seed_lo, D.seed_hi, rnd);
+        }
+        u = ta_u01(rnd[k & 3]);
+      }
+      float c = __fmul_rn(div_by(__fsub_rn(lk[k], mn), nspan, rspan), D.nbf);
+      float fl = floorf(c);
+      float fr = __fsub_rn(c, fl);
+      float r = __fadd_rn(fl, (u < fr) ? 1.0f : 0.0f);
+      r = (r < 0.0f) ? 0.0f : r;
+      r = (r > D.nbf - 1.0f) ? D.nbf - 1.0f : r;
+      if (active) st[L::OFF_IDX + bi * L::STR_1 + t] = (uint8_t)r;
+    }
+    if (param && ve) {
+      float pv;
+      if (full) pv = PT ? ta_bf16_to_f32(reinterpret_cast<const uint16_t*>(sp)[t])
+                        : reinterpret_cast<const float*>(sp)[t];
+      else pv = to_f32<PT>(D.p, e);
+      if (D.flags & DF_WD) {  // optimizer.py:106-107
+        pv = __fmul_rn(pv, D.wdf);
+        if (PT) pv = ta_bf16_to_f32(ta_f32_to_bf16(pv));
+      }
+      // optimizer.py:163 / :167 and :170
+      float d = __fadd_rn(__fsqrt_rn(div_by(vk[k], D.bc2, D.rbc2)), D.eps);
+      float upd = __fdiv_rn(__fmul_rn(D.nlr, mk[k]), __fmul_rn(d, D.bc1));
+      pv = __fadd_rn(pv, upd);
+      if (PT) {
+        uint16_t h = ta_f32_to_bf16(pv);
+        if (full) reinterpret_cast<uint16_t*>(sp)[t] = h;
+        else reinterpret_cast<uint16_t*>(D.p)[e] = h;
+      } else {
+        if (full) reinterpret_cast<float*>(sp)[t] = pv;
+        else reinterpret_cast<float*>(D.p)[e] = pv;
+      }
+    }
+    if (ve && (D.flags & DF_M_OUT)) D.m_out[e] = mk[k];
+    if (ve && (D.flags & DF_V_OUT)) D.v_out[e] = vk[k];
+  }
+}
+
+template <int MK, int VK, int PT, bool UNI>
+__global__ void __launch_bounds__(NTHR) k_pass1(KParams kp) {
+  using L = P1L<MK, VK, PT, UNI>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* stages = smem;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + NSTAGE * L::STAGE);
+  uint64_t* done = full + NSTAGE;
+  StageMeta* meta = reinterpret_cast<StageMeta*>(done + NSTAGE);
+  float* tables = reinterpret_cast<float*>(meta + NSTAGE);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NSTAGE; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&done[s], NCW);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == NCW) {  // producer / storer
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int64_t tile = blockIdx.x; tile < kp.total; tile += gridDim.x, ++it) {
+        const int s = it % NSTAGE;
+        const uint32_t ph = (uint32_t)(it / NSTAGE) & 1u;
+        uint8_t* st = stages + s * L::STAGE;
+        if (it >= NSTAGE) {
+          if (!wait_bar(&done[s], ph ^ 1u, kp.status)) { ok = false; break; }
+          const StageMeta& pm = meta[s];
+          p1_store<MK, VK, PT, UNI>(kp.T[pm.t], st, pm.nblk, pm.b0);
+          bulk_commit();
+          bulk_wait_read_all();
+        }
+        const int en = find_entry(kp.lbeg, kp.nl, tile);
+        const int t = kp.lidx[en];
+        const DevTensor& D = kp.T[t];
+        const int64_t lt = tile - kp.lbeg[en];
+        const int64_t b0 = lt * TB;
+        const int nblk = (int)min((int64_t)TB, D.nblk - b0);
+        meta[s].t = t;
+        meta[s].nblk = nblk;
+        meta[s].b0 = b0;
+        uint32_t bytes;
+        p1_issue<MK, VK, PT, UNI>(D, st, nblk, b0, &full[s], true, bytes);
+        mbar_arrive_expect_tx(&full[s], bytes);
+        p1_issue<MK, VK, PT, UNI>(D, st, nblk, b0, &full[s], false, bytes);
+      }
+      const int first = it > NSTAGE ? it - NSTAGE : 0;
+      if (ok) {
+        for (int r = first; r < it; ++r) {
+          const int s = r % NSTAGE;
+          if (!wait_bar(&done[s], (uint32_t)(r / NSTAGE) & 1u, kp.status)) { ok = false; break; }
+          const StageMeta& pm = meta[s];
+          p1_store<MK, VK, PT, UNI>(kp.T[pm.t], stages + s * L::STAGE, pm.nblk, pm.b0);
+          bulk_commit();
+        }
+      }
+      if (!ok)  // a wait ran out: let this CTA's own loads land before exiting
+        for (int r = first; r < it; ++r) wait_bar(&full[r % NSTAGE], (uint32_t)(r / NSTAGE) & 1u,
+                                                  kp.status);
+      bulk_wait_all();
+    }
+    return;
+  }
+
+  float* table = tables + warp * 4 * TABLE_STRIDE;
+  int it = 0;
+  for (int64_t tile = blockIdx.x; tile < kp.total; tile += gridDim.x, ++it) {
+    const int s = it % NSTAGE;
+    const uint32_t ph = (uint32_t)(it / NSTAGE) & 1u;
+    if (!wait_bar(&full[s], ph, kp.status)) break;
+    const StageMeta pm = meta[s];
+    p1_block<MK, VK, PT, UNI>(kp.T[pm.t], stages + s * L::STAGE, pm.nblk, pm.b0, table,
+                              kp.status);
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&done[s]);
+  }
+}
+
+template <int MK, int VK, int PT, bool UNI>
+constexpr size_t p1_smem_bytes() {
+  return (size_t)NSTAGE * P1L<MK, VK, PT, UNI>::STAGE + 2 * NSTAGE * 8 +
+         NSTAGE * sizeof(StageMeta) + NCW * 4 * TABLE_STRIDE * 4;
+}
+
+// ---------------------------------------------------------------------------
+// alpha finalisation (costate.py:22-43 with the canonical reduction order)
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(FIN_THREADS) k_alpha(const DevTensor* T, const int32_t* cs,
+                                                       int ncs) {
+  const DevTensor& D = T[cs[blockIdx.x]];
+  const int tid = threadIdx.x;
+  const int64_t ntile = (D.nblk + TB - 1) / TB;
+  double amg = 0.0, agg = 0.0;
+  for (int64_t i = tid; i < ntile; i += FIN_THREADS) {
+    double tm = 0.0, tg = 0.0;
+    const int64_t bend = min(D.nblk, (i + 1) * TB);
+    for (int64_t b = i * TB; b < bend; ++b) {
+      tm += (double)D.part[b];
+      tg += (double)D.part[D.bpad + b];
+    }
+    amg += tm;
+    agg += tg;
+  }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    amg = amg + __shfl_xor_sync(0xffffffffu, amg, off);
+    agg = agg + __shfl_xor_sync(0xffffffffu, agg, off);
+  }
+  __shared__ double wm[FIN_THREADS / 32], wg[FIN_THREADS / 32];
+  if ((tid & 31) == 0) {
+    wm[tid >> 5] = amg;
+    wg[tid >> 5] = agg;
+  }
+  // zero the select histograms / counters of this tensor for this step
+  for (int i = tid; i < 3 * 2 * HBINS; i += FIN_THREADS) D.hist[i] = 0u;
+  if (tid < 16) D.sel[tid] = 0u;
+  __syncthreads();
+  if (tid == 0) {
+    double tm = wm[0], tg = wg[0];
+    for (int w = 1; w < FIN_THREADS / 32; ++w) {
+      tm += wm[w];
+      tg += wg[w];
+    }
+    float mg = (float)tm, gg = (float)tg;
+    float a = (gg > 0.0f) ? __fdiv_rn(mg, gg) : 0.0f;
+    if (D.flags & DF_ALPHA_INJ) a = *D.alpha_inj;
+    D.alpha_new[0] = a;
+    D.sel[SEL_RLO] = (uint32_t)D.k_lo;
+    D.sel[SEL_RHI] = (uint32_t)D.k_hi;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Pass 2: CoState encode (costate.py:419-425, :51-86, :213-258)
+// ---------------------------------------------------------------------------
+template <int PT>
+__device__ __forceinline__ void p2_block(const DevTensor& D, uint8_t* st, int nblk, int64_t b0) {
+  using L = P2L<PT>;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int q = lane >> 3;
+  const int j = lane & 7;
+  const int bi = warp * 4 + q;
+  const bool active = bi < nblk;
+  const int64_t b = b0 + bi;
+  const int64_t e0 = b * BS;
+  const int nv = active ? (int)min((int64_t)BS, D.n - e0) : 0;
+  const bool full = nv == BS;
+  const uint32_t gbase = lane & ~7u;
+  const uint8_t* sg = st + L::OFF_G + bi * L::STR_G;
+
+  const bool has_state = D.flags & DF_M_HAS_STATE;
+  float cs_scale = 0.0f, alpha_old = 0.0f;
+  uint32_t sw[4] = {0, 0, 0, 0};
+  if (has_state && active) {
+    uint8_t lab = st[L::OFF_LAB + bi];
+    float nrm = reinterpret_cast<const float*>(st + L::OFF_NRM)[bi];
+    uint16_t amp = reinterpret_cast<const uint16_t*>(st + L::OFF_AMP)[bi];
+    cs_scale = costate_scale(lab, nrm, amp, D.sqbs);
+    uint4 w = *reinterpret_cast<const uint4*>(st + L::OFF_SGN + bi * 16);
+    sw[0] = w.x; sw[1] = w.y; sw[2] = w.z; sw[3] = w.w;
+    alpha_old = *D.alpha_state;
+  }
+  const float alpha = D.alpha_new[0];
+  float accd = 0.0f, accm = 0.0f;
+  uint32_t myw = 0;
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    const int t = j + 8 * k;
+    const bool ve = t < nv;
+    float g;
+    if (full) g = PT ? ta_bf16_to_f32(reinterpret_cast<const uint16_t*>(sg)[t])
+                     : reinterpret_cast<const float*>(sg)[t];
+    else g = ve ? to_f32<PT>(D.g, e0 + t) : 0.0f;
+    uint32_t bit = (sw[k >> 2] >> (8 * (k & 3) + 7 - j)) & 1u;
+    float m = costate_m(g, alpha_old, cs_scale, bit, has_state, D.b1, D.omb1);
+    float dl = ve ? __fsub_rn(m, __fmul_rn(alpha, g)) : 0.0f;  // costate.py:42
+    float mm = ve ? m : 0.0f;
+    accd = __fadd_rn(accd, __fmul_rn(dl, dl));
+    accm = __fadd_rn(accm, __fmul_rn(mm, mm));
+    uint32_t w = __ballot_sync(0xffffffffu, dl < 0.0f);
+    if (lane == k) myw = w;
+  }
+  // torch row-norm order: lane accumulators summed 0..7 in sequence
+  float sd = __shfl_sync(0xffffffffu, accd, gbase);
+  float sm = __shfl_sync(0xffffffffu, accm, gbase);
+#pragma unroll
+  for (int i = 1; i < 8; ++i) {
+    sd = __fadd_rn(sd, __shfl_sync(0xffffffffu, accd, gbase + i));
+    sm = __fadd_rn(sm, __shfl_sync(0xffffffffu, accm, gbase + i));
+  }
+  const float dn = __fsqrt_rn(sd);
+  const float mnorm = __fsqrt_rn(sm);
+  // sign bytes k = 2j, 2j+1 of this block (MSB = lane 0)
+  uint32_t w0 = __shfl_sync(0xffffffffu, myw, 2 * j);
+  uint32_t w1 = __shfl_sync(0xffffffffu, myw, 2 * j + 1);
+  if (active) {
+    uint32_t by0 = __brev((w0 >> (8 * q)) & 0xffu) >> 24;
+    uint32_t by1 = __brev((w1 >> (8 * q)) & 0xffu) >> 24;
+    reinterpret_cast<uint16_t*>(st + L::OFF_SGN + bi * 16)[j] = (uint16_t)(by0 | (by1 << 8));
+    if (j == 0) {
+      reinterpret_cast<float*>(st + L::OFF_NRM)[bi] = dn;
+      reinterpret_cast<uint16_t*>(st + L::OFF_AMP)[bi] = ta_f32_to_f16(__fdiv_rn(dn, D.sqbs));
+      reinterpret_cast<float*>(st + L::OFF_RAT)[bi] =
+          (mnorm == 0.0f) ? 0.0f : __fdiv_rn(dn, mnorm);
+    }
+  }
+}
+
+template <int PT>
+__global__ void __launch_bounds__(NTHR) k_pass2(KParams kp) {
+  using L = P2L<PT>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* stages = smem;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + NSTAGE * L::STAGE);
+  uint64_t* done = full + NSTAGE;
+  StageMeta* meta = reinterpret_cast<StageMeta*>(done + NSTAGE);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NSTAGE; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&done[s], NCW);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  auto store = [&](uint8_t* st, const StageMeta& pm) {
+    const DevTensor& D = kp.T[pm.t];
+    bulk_s2g(D.sgn + pm.b0 * 16, st + L::OFF_SGN, TB * 16);
+    bulk_s2g(D.nrm + pm.b0, st + L::OFF_NRM, TB * 4);
+    bulk_s2g(D.amp + pm.b0, st + L::OFF_AMP, TB * 2);
+    bulk_s2g(D.ratios + pm.b0, st + L::OFF_RAT, TB * 4);
+  };
+
+  if (warp == NCW) {
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int64_t tile = blockIdx.x; tile < kp.total; tile += gridDim.x, ++it) {
+        const int s = it % NSTAGE;
+        const uint32_t ph = (uint32_t)(it / NSTAGE) & 1u;
+        uint8_t* st = stages + s * L::STAGE;
+        if (it >= NSTAGE) {
+          if (!wait_bar(&done[s], ph ^ 1u, kp.status)) { ok = false; break; }
+          store(st, meta[s]);
+          bulk_commit();
+          bulk_wait_read_all();
+        }
+        const int en = find_entry(kp.lbeg, kp.nl, tile);
+        const int t = kp.lidx[en];
+        const DevTensor& D = kp.T[t];
+        const int64_t b0 = (tile - kp.lbeg[en]) * TB;
+        const int nblk = (int)min((int64_t)TB, D.nblk - b0);
+        meta[s].t = t;
+        meta[s].nblk = nblk;
+        meta[s].b0 = b0;
+        uint32_t bytes = 0;
+        for (int i = 0; i < nblk; ++i)
+          if (D.n - (b0 + i) * BS >= BS) bytes += BS * L::ESZ;
+        const bool hs = D.flags & DF_M_HAS_STATE;
+        if (hs) bytes += 16 + TB * 16 + TB * 4 + TB * 2;
+        mbar_arrive_expect_tx(&full[s], bytes);
+        for (int i = 0; i < nblk; ++i) {
+          const int64_t e0 = (b0 + i) * BS;
+          if (D.n - e0 >= BS)
+            bulk_g2s(st + L::OFF_G + i * L::STR_G, (const uint8_t*)D.g + e0 * L::ESZ,
+                     BS * L::ESZ, &full[s]);
+        }
+        if (hs) {
+          bulk_g2s(st + L::OFF_LAB, D.lab + b0, 16, &full[s]);
+          bulk_g2s(st + L::OFF_SGN, D.sgn + b0 * 16, TB * 16, &full[s]);
+          bulk_g2s(st + L::OFF_NRM, D.nrm + b0, TB * 4, &full[s]);
+          bulk_g2s(st + L::OFF_AMP, D.amp + b0, TB * 2, &full[s]);
+        }
+      }
+      const int first = it > NSTAGE ? it - NSTAGE : 0;
+      if (ok) {
+        for (int r = first; r < it; ++r) {
+          const int s = r % NSTAGE;
+          if (!wait_bar(&done[s], (uint32_t)(r / NSTAGE) & 1u, kp.status)) { ok = false; break; }
+          store(stages + s * L::STAGE, meta[s]);
+          bulk_commit();
+        }
+      }
+      if (!ok)
+        for (int r = first; r < it; ++r) wait_bar(&full[r % NSTAGE], (uint32_t)(r / NSTAGE) & 1u,
+                                                  kp.status);
+      bulk_wait_all();
+    }
+    return;
+  }
+  int it = 0;
+  for (int64_t tile = blockIdx.x; tile < kp.total; tile += gridDim.x, ++it) {
+    const int s = it % NSTAGE;
+    const uint32_t ph = (uint32_t)(it / NSTAGE) & 1u;
+    if (!wait_bar(&full[s], ph, kp.status)) break;
+    const StageMeta pm = meta[s];
+    p2_block<PT>(kp.T[pm.t], stages + s * L::STAGE, pm.nblk, pm.b0);
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&done[s]);
+  }
+}
+
+template <int PT>
+constexpr size_t p2_smem_bytes() {
+  return (size_t)NSTAGE * P2L<PT>::STAGE + 2 * NSTAGE * 8 + NSTAGE * sizeof(StageMeta);
+}
+
+// ---------------------------------------------------------------------------
+// Exact order statistics of the ratios (costate.py:94-118) by radix select
+// on the fp32 bit pattern (non-negative floats order like their bits).
+// Round r: 0 -> bits[31:21], 1 -> bits[20:10], 2 -> bits[9:0].
+// ---------------------------------------------------------------------------
+struct SelParams {
+  const DevTensor* T;
+  const int64_t* cbeg;  // [ncs + 1] chunk prefix
+  const int32_t* cidx;  // [ncs] tensor indices
+  int32_t ncs;
+};
+
+__device__ __forceinline__ void scan_pick(const uint32_t* h, int nbins, uint32_t rank,
+                                          uint32_t* bin_out, uint32_t* rank_out,
+                                          uint32_t* sh) {
+  // single-CTA scan over nbins global bins (nbins <= 2048, 256 threads x 8)
+  const int tid = threadIdx.x;
+  const int per = nbins / SEL_THREADS;
+  uint32_t loc[8];
+  uint32_t s = 0;
+  for (int i = 0; i < per; ++i) {
+    loc[i] = __ldcg(&h[tid * per + i]);
+    s += loc[i];
+  }
+  sh[tid] = s;
+  __syncthreads();
+  // inclusive scan in smem (Hillis-Steele)
+  for (int off = 1; off < SEL_THREADS; off <<= 1) {
+    uint32_t v = (tid >= off) ? sh[tid - off] : 0u;
+    __syncthreads();
+    sh[tid] += v;
+    __syncthreads();
+  }
+  const uint32_t incl = sh[tid];
+  const uint32_t excl = incl - s;
+  if (rank >= excl && rank < incl) {
+    uint32_t c = excl;
+    for (int i = 0; i < per; ++i) {
+      if (rank < c + loc[i]) {
+        *bin_out = (uint32_t)(tid * per + i);
+        *rank_out = rank - c;
+        break;
+      }
+      c += loc[i];
+    }
+  }
+  __syncthreads();
+}
+
+template <int R>
+__global__ void __launch_bounds__(SEL_THREADS) k_select(SelParams sp) {
+  __shared__ uint32_t h[2][HBINS];
+  __shared__ uint32_t sh[SEL_THREADS];
+  __shared__ int last;
+  const int tid = threadIdx.x;
+  const int64_t chunk = blockIdx.x;
+  const int en = find_entry(sp.cbeg, sp.ncs, chunk);
+  const DevTensor& D = sp.T[sp.cidx[en]];
+  const int64_t c = chunk - sp.cbeg[en];
+  const int64_t i0 = c * SEL_CHUNK;
+  const int64_t i1 = min(D.nblk, i0 + SEL_CHUNK);
+  constexpr int NB = (R == 2) ? 1024 : 2048;
+  for (int i = tid; i < 2 * HBINS; i += SEL_THREADS) (&h[0][0])[i] = 0u;
+  __syncthreads();
+  uint32_t plo = 0, phi = 0;
+  if (R > 0) {
+    plo = D.sel[SEL_PLO];
+    phi = D.sel[SEL_PHI];
+  }
+  for (int64_t i = i0 + tid; i < i1; i += SEL_THREADS) {
+    const uint32_t x = __float_as_uint(D.ratios[i]);
+    if (R == 0) {
+      atomicAdd(&h[0][x >> 21], 1u);
+    } else if (R == 1) {
+      const uint32_t top = x >> 21, d = (x >> 10) & 0x7ffu;
+      if (top == plo) atomicAdd(&h[0][d], 1u);
+      if (top == phi) atomicAdd(&h[1][d], 1u);
+    } else {
+      const uint32_t top = x >> 10, d = x & 0x3ffu;
+      if (top == plo) atomicAdd(&h[0][d], 1u);
+      if (top == phi) atomicAdd(&h[1][d], 1u);
+    }
+  }
+  __syncthreads();
+  uint32_t* gh = D.hist + R * 2 * HBINS;
+  const int nh = (R == 0) ? 1 : 2;
+  for (int k = 0; k < nh; ++k)
+    for (int i = tid; i < NB; i += SEL_THREADS)
+      if (h[k][i]) atomicAdd(&gh[k * HBINS + i], h[k][i]);
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) last = (atomicAdd(&D.sel[SEL_CNT0 + R], 1u) == (uint32_t)D.sel_chunks - 1u);
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  __shared__ uint32_t pick[4];
+  if (tid < 4) pick[tid] = 0u;
+  __syncthreads();
+  // L2 (__ldcg) reads: the histogram was built by other CTAs' atomics
+  const uint32_t rlo = __ldcg(&D.sel[SEL_RLO]), rhi = __ldcg(&D.sel[SEL_RHI]);
+  for (int k = 0; k < 2; ++k) {
+    const uint32_t* src = gh + ((R == 0) ? 0 : k * HBINS);
+    scan_pick(src, NB, k == 0 ? rlo : rhi, &pick[2 * k], &pick[2 * k + 1], sh);
+  }
+  if (tid == 0) {
+    const uint32_t blo = pick[0], bhi = pick[2];
+    if (R == 0) {
+      D.sel[SEL_PLO] = blo;
+      D.sel[SEL_PHI] = bhi;
+    } else if (R == 1) {
+      D.sel[SEL_PLO] = (plo << 11) | blo;
+      D.sel[SEL_PHI] = (phi << 11) | bhi;
+    } else {
+      D.alpha_new[1] = __uint_as_float((plo << 10) | blo);
+      D.alpha_new[2] = __uint_as_float((phi << 10) | bhi);
+    }
+    D.sel[SEL_RLO] = pick[1];
+    D.sel[SEL_RHI] = pick[3];
+  }
+}
+
+// labels (costate.py:126-149) and commit alpha (costate.py:443-456)
+__global__ void __launch_bounds__(SEL_THREADS) k_labels(SelParams sp) {
+  const int64_t chunk = blockIdx.x;
+  const int en = find_entry(sp.cbeg, sp.ncs, chunk);
+  const DevTensor& D = sp.T[sp.cidx[en]];
+  const int64_t c = chunk - sp.cbeg[en];
+  const int64_t i0 = c * SEL_CHUNK;
+  const int64_t i1 = min(D.nblk, i0 + SEL_CHUNK);
+  const float t0 = D.alpha_new[1], t1 = D.alpha_new[2];
+  for (int64_t i = i0 + threadIdx.x; i < i1; i += SEL_THREADS) {
+    const float r = D.ratios[i];
+    uint8_t l = 0;
+    if (r >= t0) l = 1;
+    if (r >= t1) l = 2;
+    D.lab[i] = l;
+  }
+  if (c == 0 && threadIdx.x == 0 && D.alpha_state) *D.alpha_state = D.alpha_new[0];
+}
+
+}  // namespace ta

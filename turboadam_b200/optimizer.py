@@ -1,0 +1,389 @@
+"""TurboAdam on B200: drop-in for the reference optimizer step.
+
+Same constructor, validation, lazy state initialisation, state keys and
+bias-correction semantics as reference ``src/turboadam/optimizer.py``. The
+per-parameter Python loop of the reference (optimizer.py:88-170, ~20-30
+eager launches per CoState tensor) is replaced by one ``ta_step`` call per
+device: a fixed sequence of multi-tensor sm_100a kernels over every
+parameter of the step.
+
+Stochastic rounding draws come from a counter-based Philox4x32-10 stream
+keyed by (seed, tensor id, step, element); the reference draws them from
+``torch.rand_like`` / ``rand_buf.uniform_()``, so with the same uniforms the
+two produce identical packed state (see tests/).
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import torch
+from torch.optim import Optimizer
+
+from . import _lib
+from .costate import CoStateManager
+from .oneq import adopt_compressed_v, init_compressed_v, is_padded, storage_capacity
+
+_DTYPES = {torch.float32: _lib.TA_F32, torch.bfloat16: _lib.TA_BF16}
+
+
+class TurboAdam(Optimizer):
+    """Adam with CoState-compressed m and 1Q log-scale v (reference API).
+
+    Args mirror the reference (optimizer.py:44-81). ``seed`` (keyword-only,
+    extra) keys the stochastic-rounding generator; default torch.initial_seed().
+    """
+
+    def __init__(
+        self,
+        params,
+        lr: float = 1e-3,
+        betas: tuple[float, float] = (0.9, 0.999),
+        eps: float = 1e-8,
+        weight_decay: float = 0.0,
+        block_size: int = 128,
+        v_bits: int = 4,
+        compress_m: bool = True,
+        compress_v: bool = True,
+        null_pct: float = 0.10,
+        amp_pct: float = 0.90,
+        error_feedback: bool = False,
+        capturable: bool = False,
+        min_m_compress_elements: int = 4096,
+        *,
+        seed: int | None = None,
+    ):
+        if v_bits not in (2, 3, 4, 6, 8):
+            raise ValueError(f"v_bits must be one of {{2, 3, 4, 6, 8}}, got {v_bits}")
+        if capturable:
+            raise NotImplementedError(
+                "CUDA graph capture is not yet supported. Set capturable=False.")
+        defaults = dict(
+            lr=lr,
+            betas=betas,
+            eps=eps,
+            weight_decay=weight_decay,
+            block_size=block_size,
+            v_bits=v_bits,
+            compress_m=compress_m,
+            compress_v=compress_v,
+            null_pct=null_pct,
+            amp_pct=amp_pct,
+            error_feedback=error_feedback,
+            min_m_compress_elements=min_m_compress_elements,
+        )
+        super().__init__(params, defaults)
+        self._group_step_tensors = {}
+        self._seed = (torch.initial_seed() if seed is None else int(seed)) & 0xFFFFFFFFFFFFFFFF
+        self._plans = None
+        self._ws = {}
+        # test hook: {"uniforms": {param: fp32 [B*128] cuda}, "alpha": {param: fp32 [1] cuda}}
+        self._parity = None
+        # timing hook: 5 recorded torch.cuda.Event objects marking the kernel
+        # phases of the next step(s) (see ta_step_profiled)
+        self._phase_events = None
+
+    # ------------------------------------------------------------------
+    # state dict
+    # ------------------------------------------------------------------
+    def add_param_group(self, param_group):
+        super().add_param_group(param_group)
+        self._plans = None
+
+    def load_state_dict(self, state_dict):
+        """Load and re-home packed state into the padded device layout
+        (reference optimizer.py:194-218 migrates CoState tensors by hand)."""
+        super().load_state_dict(state_dict)
+        for group in self.param_groups:
+            for p in group["params"]:
+                if p not in self.state:
+                    continue
+                st = self.state[p]
+                if "compressed_v" in st and not is_padded(st["compressed_v"], p.device):
+                    st["compressed_v"] = adopt_compressed_v(st["compressed_v"], p.device)
+                mgr = st.get("m_mgr")
+                if isinstance(mgr, CoStateManager):
+                    mgr.adopt(p.numel(), p.device)
+                for k in ("exp_avg", "exp_avg_sq"):
+                    if k in st:
+                        st[k] = st[k].to(device=p.device, dtype=torch.float32).contiguous()
+                for k in ("_bc1", "_bc2"):
+                    if k in st:
+                        st[k] = st[k].to(device=p.device, dtype=torch.float32)
+        self._plans = None
+
+    # ------------------------------------------------------------------
+    # step
+    # ------------------------------------------------------------------
+    def _init_state(self, group_idx, group, p):
+        state = self.state[p]
+        block_size = group["block_size"]
+        if len(state) == 0:  # optimizer.py:243-269
+            state["step"] = 0
+            compress_this_m = group["compress_m"] and p.numel() >= group["min_m_compress_elements"]
+            state["_compress_m"] = compress_this_m
+            if compress_this_m:
+                mgr = CoStateManager(block_size=block_size, null_pct=group["null_pct"],
+                                     amp_pct=group["amp_pct"],
+                                     error_feedback=group["error_feedback"])
+                mgr.allocate(p.numel(), p.device)
+                state["m_mgr"] = mgr
+            else:
+                state["exp_avg"] = torch.zeros_like(p, dtype=torch.float32,
+                                                    memory_format=torch.contiguous_format)
+            if not group["compress_v"]:
+                state["exp_avg_sq"] = torch.zeros_like(p, dtype=torch.float32,
+                                                       memory_format=torch.contiguous_format)
+            key = (group_idx, p.device.type, p.device.index)
+            if key not in self._group_step_tensors:
+                self._group_step_tensors[key] = {
+                    "bc1": torch.empty(1, dtype=torch.float32, device=p.device),
+                    "bc2": torch.empty(1, dtype=torch.float32, device=p.device),
+                }
+            gt = self._group_step_tensors[key]
+            state["_bc1"] = gt["bc1"]
+            state["_bc2"] = gt["bc2"]
+            self._plans = None
+        if group["compress_v"] and "compressed_v" not in state:  # optimizer.py:273-280
+            state["compressed_v"] = init_compressed_v(p.shape, group["v_bits"], p.device,
+                                                      block_size)
+            self._plans = None
+
+    def _bias_corrections(self):
+        """optimizer.py:172-188: per group, the last param holding state wins."""
+        out = {}
+        for gi, group in enumerate(self.param_groups):
+            beta1, beta2 = group["betas"]
+            for p in group["params"]:
+                if p not in self.state:
+                    continue
+                nxt = self.state[p]["step"] + 1
+                out[gi] = (np.float32(1.0 - beta1 ** nxt), np.float32(1.0 - beta2 ** nxt))
+        return out
+
+    @torch.no_grad()
+    def step(self, closure=None):
+        """Perform a single optimization step."""
+        loss = None
+        if closure is not None:
+            with torch.enable_grad():
+                loss = closure()
+
+        work = []
+        for gi, group in enumerate(self.param_groups):
+            for p in group["params"]:
+                if p.grad is None:
+                    continue
+                _lib.require_cuda(p)
+                if p.dtype not in _DTYPES:
+                    raise NotImplementedError(
+                        f"param dtype {p.dtype}: the sm_100a step is built for float32 and "
+                        "bfloat16 parameters")
+                if group["block_size"] != 128:
+                    raise NotImplementedError("block_size != 128 is not built for the device step")
+                if group["error_feedback"]:
+                    raise NotImplementedError("error_feedback=True is not built for the device step")
+                self._init_state(gi, group, p)
+                work.append((gi, p))
+        if not work:
+            return loss
+        bcs = self._bias_corrections()
+        for gi, (bc1, bc2) in bcs.items():
+            for key, gt in self._group_step_tensors.items():
+                if key[0] == gi:
+                    gt["bc1"].fill_(float(bc1))
+                    gt["bc2"].fill_(float(bc2))
+
+        by_dev = {}
+        for gi, p in work:
+            by_dev.setdefault(p.device, []).append((gi, p))
+        for dev, items in by_dev.items():
+            self._run_device(dev, items, bcs)
+        return loss
+
+    # ------------------------------------------------------------------
+    def _tensor_ids(self):
+        ids = {}
+        i = 0
+        for group in self.param_groups:
+            for p in group["params"]:
+                ids.setdefault(id(p), i)
+                i += 1
+        return ids
+
+    def _build_plan(self, dev, items):
+        lib = _lib.load()
+        tids = self._tensor_ids()
+        n = len(items)
+        arr = np.zeros(n, dtype=_lib.TENSOR_DTYPE)
+        for i, (gi, p) in enumerate(items):
+            st = self.state[p]
+            group = self.param_groups[gi]
+            r = arr[i]
+            r["param_dev"] = p.data_ptr()
+            r["numel"] = p.numel()
+            r["dtype"] = _DTYPES[p.dtype]
+            r["group"] = gi
+            r["tensor_id"] = tids[id(p)] & 0xFFFFFFFF
+            flags = 0
+            if st["_compress_m"]:
+                mgr = st["m_mgr"]
+                flags |= _lib.TA_M_COSTATE
+                lab, sgn, nrm, amp, alpha = mgr.pointers()
+                r["m_labels_dev"], r["m_signs_dev"], r["m_norms_dev"] = lab, sgn, nrm
+                r["m_amp_dev"], r["m_alpha_dev"] = amp, alpha
+            else:
+                r["exp_avg_dev"] = st["exp_avg"].data_ptr()
+            if group["compress_v"]:
+                flags |= _lib.TA_V_ONEQ
+                cv = st["compressed_v"]
+                r["v_idx_dev"] = cv["indices"].data_ptr()
+                r["v_hdr_dev"] = cv["scales"].data_ptr()
+            else:
+                r["exp_avg_sq_dev"] = st["exp_avg_sq"].data_ptr()
+            r["flags"] = flags
+            if p.data_ptr() % 16 != 0:
+                raise NotImplementedError("parameter storage must be 16-byte aligned")
+        ws_bytes = lib.ta_workspace_size(arr.ctypes.data, n)
+        ws = self._ws.get(dev)
+        if ws is None or ws.numel() < ws_bytes:
+            ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)
+            self._ws[dev] = ws
+        groups = np.zeros(len(self.param_groups), dtype=_lib.GROUP_DTYPE)
+        return {"key": tuple(id(p) for _, p in items), "arr": arr, "groups": groups}
+
+    def _run_device(self, dev, items, bcs):
+        lib = _lib.load()
+        if self._plans is None:
+            self._plans = {}
+        plan = self._plans.get(dev)
+        key = tuple(id(p) for _, p in items)
+        if plan is None or plan["key"] != key:
+            plan = self._build_plan(dev, items)
+            self._plans[dev] = plan
+        arr = plan["arr"]
+        keep = []
+        grad_ptr = arr["grad_dev"]
+        steps = arr["step"]
+        flags = arr["flags"]
+        uni = arr["sr_uniforms_dev"]
+        ainj = arr["alpha_inject_dev"]
+        parity = self._parity
+        for i, (gi, p) in enumerate(items):
+            st = self.state[p]
+            g = p.grad
+            if g.dtype != p.dtype:
+                if p.dtype == torch.float32 and g.dtype == torch.bfloat16:
+                    g = g.float()
+                else:
+                    raise NotImplementedError(f"grad dtype {g.dtype} with param dtype {p.dtype}")
+            if not g.is_contiguous() or g.data_ptr() % 16:
+                g = g.contiguous().clone() if g.data_ptr() % 16 else g.contiguous()
+            keep.append(g)
+            st["step"] += 1  # optimizer.py:103
+            grad_ptr[i] = g.data_ptr()
+            steps[i] = st["step"]
+            f = int(flags[i]) & ~_lib.TA_M_HAS_STATE
+            mgr = st.get("m_mgr")
+            if mgr is not None and mgr._has_state:
+                f |= _lib.TA_M_HAS_STATE
+            flags[i] = f
+            if parity is not None:
+                u = parity.get("uniforms", {}).get(p)
+                a = parity.get("alpha", {}).get(p)
+                uni[i] = u.data_ptr() if u is not None else 0
+                ainj[i] = a.data_ptr() if a is not None else 0
+                keep += [u, a]
+            elif uni[i] or ainj[i]:
+                uni[i] = 0
+                ainj[i] = 0
+        groups = plan["groups"]
+        for gi, group in enumerate(self.param_groups):
+            g = groups[gi]
+            g["lr"] = group["lr"]
+            g["beta1"], g["beta2"] = group["betas"]
+            g["eps"] = group["eps"]
+            g["weight_decay"] = group["weight_decay"]
+            g["null_pct"] = group["null_pct"]
+            g["amp_pct"] = group["amp_pct"]
+            bc = bcs.get(gi, (np.float32(1.0), np.float32(1.0)))
+            g["bc1"], g["bc2"] = bc
+            g["block_size"] = group["block_size"]
+            g["v_bits"] = group["v_bits"]
+        ws = self._ws[dev]
+        with torch.cuda.device(dev):
+            if self._phase_events is None:
+                rc = lib.ta_step(arr.ctypes.data, len(items), groups.ctypes.data, len(groups),
+                                 self._seed, ws.data_ptr(), ws.numel(), _lib.stream_ptr(dev))
+            else:
+                evs = (ctypes.c_void_p * 5)(*[e.cuda_event for e in self._phase_events])
+                rc = lib.ta_step_profiled(arr.ctypes.data, len(items), groups.ctypes.data,
+                                          len(groups), self._seed, ws.data_ptr(), ws.numel(),
+                                          _lib.stream_ptr(dev), evs)
+        _lib.check(rc, "ta_step")
+        for _, p in items:
+            mgr = self.state[p].get("m_mgr")
+            if mgr is not None:
+                mgr.mark_updated()
+        # Temporaries in `keep` were allocated on the current stream, so the
+        # caching allocator only reuses them for work ordered after ta_step.
+        del keep
+
+    # ------------------------------------------------------------------
+    def read_status(self, clear: bool = True) -> int:
+        """Device status bits accumulated since the last read
+        (TA_STATUS_NONFINITE_GRAD, TA_STATUS_WAIT_TIMEOUT)."""
+        lib = _lib.load()
+        out = 0
+        for dev, ws in self._ws.items():
+            v = ctypes.c_uint32(0)
+            _lib.check(lib.ta_read_status(ws.data_ptr(), int(clear), ctypes.byref(v),
+                                          _lib.stream_ptr(dev)), "ta_read_status")
+            out |= v.value
+        return out
+
+
+def _single_costate_update(mgr: CoStateManager, g: torch.Tensor, beta1: float,
+                           uniforms=None, alpha_inject=None) -> torch.Tensor:
+    """CoStateManager.update (costate.py:367-464) through ta_step with
+    TA_NO_PARAM: decode, EMA, alpha, encode, thresholds, labels."""
+    _lib.require_cuda(g)
+    lib = _lib.load()
+    dev = g.device
+    gf = g.reshape(-1)
+    if gf.dtype not in (torch.float32, torch.bfloat16):
+        gf = gf.float()
+    gf = gf.contiguous()
+    n = gf.numel()
+    if mgr._bufs is None:
+        mgr.allocate(n, dev)
+    arr = np.zeros(1, dtype=_lib.TENSOR_DTYPE)
+    r = arr[0]
+    r["grad_dev"] = gf.data_ptr()
+    r["numel"] = n
+    r["dtype"] = _DTYPES[gf.dtype]
+    r["flags"] = _lib.TA_M_COSTATE | _lib.TA_NO_PARAM | (
+        _lib.TA_M_HAS_STATE if mgr._has_state else 0)
+    r["step"] = 1
+    lab, sgn, nrm, amp, alpha = mgr.pointers()
+    r["m_labels_dev"], r["m_signs_dev"], r["m_norms_dev"] = lab, sgn, nrm
+    r["m_amp_dev"], r["m_alpha_dev"] = amp, alpha
+    m_out = torch.empty(n, dtype=torch.float32, device=dev)
+    r["m_out_dev"] = m_out.data_ptr()
+    if alpha_inject is not None:
+        r["alpha_inject_dev"] = alpha_inject.data_ptr()
+    groups = np.zeros(1, dtype=_lib.GROUP_DTYPE)
+    gr = groups[0]
+    gr["beta1"] = beta1
+    gr["beta2"] = 0.999
+    gr["null_pct"] = mgr._null_pct
+    gr["amp_pct"] = mgr._amp_pct
+    gr["bc1"] = gr["bc2"] = 1.0
+    gr["block_size"] = mgr.block_size
+    gr["v_bits"] = 4
+    ws = torch.zeros(lib.ta_workspace_size(arr.ctypes.data, 1), dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        _lib.check(lib.ta_step(arr.ctypes.data, 1, groups.ctypes.data, 1, 0, ws.data_ptr(),
+                               ws.numel(), _lib.stream_ptr(dev)), "ta_step")
+    mgr.mark_updated()
+    return m_out.reshape(g.shape)
