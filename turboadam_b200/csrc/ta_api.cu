@@ -58,7 +58,7 @@ void threshold_ranks(int64_t B, double null_pct, double amp_pct, int64_t* lo, in
 constexpr int kMaxLists = 32;
 
 struct CsSlot {
-  size_t part, ratios, hist, sel, alpha;
+  size_t part, ratios, hist, sel, alpha, chunk;
 };
 
 struct Layout {
@@ -92,6 +92,8 @@ Layout layout_for(int nT, const std::vector<int64_t>& cs_bpad) {
     off = al256(off + 16 * 4);
     s.alpha = off;
     off = al256(off + 4 * 4);
+    s.chunk = off;
+    off = al256(off + (size_t)2 * cdiv(bp / TB, FIN_THREADS) * 8);
     L.cs.push_back(s);
   }
   L.total = off;
@@ -121,28 +123,36 @@ struct LaunchList {
   std::vector<int32_t> idx;
 };
 
-template <int MK, int VK, int PT, bool UNI>
+template <int MK, int VK, int PT, bool UNI, bool TABLE>
 ta_status launch_p1(const KParams& kp, cudaStream_t s) {
   constexpr size_t smem = p1_smem_bytes<MK, VK, PT, UNI>();
   static std::once_flag once;
   static int occ = 1;
-  std::call_once(once, [] { occ = setup_kernel(k_pass1<MK, VK, PT, UNI>, smem, NTHR); });
+  std::call_once(once, [] { occ = setup_kernel(k_pass1<MK, VK, PT, UNI, TABLE>, smem, NTHR); });
   int64_t grid = std::min<int64_t>(kp.total, (int64_t)sm_count() * occ);
   if (grid <= 0) return TA_OK;
-  k_pass1<MK, VK, PT, UNI><<<(unsigned)grid, NTHR, smem, s>>>(kp);
+  k_pass1<MK, VK, PT, UNI, TABLE><<<(unsigned)grid, NTHR, smem, s>>>(kp);
   TA_CU(cudaGetLastError());
   return TA_OK;
 }
 
 template <int MK, int VK, int PT>
-ta_status launch_p1_u(bool uni, const KParams& kp, cudaStream_t s) {
-  return uni ? launch_p1<MK, VK, PT, true>(kp, s) : launch_p1<MK, VK, PT, false>(kp, s);
+ta_status launch_p1_u(bool uni, bool table, const KParams& kp, cudaStream_t s) {
+  if (VK != VK_ONEQ)  // uniforms and the exp table only matter for 1Q
+    return launch_p1<MK, VK, PT, false, false>(kp, s);
+  if (uni)
+    return table ? launch_p1<MK, VK, PT, true, true>(kp, s)
+                 : launch_p1<MK, VK, PT, true, false>(kp, s);
+  return table ? launch_p1<MK, VK, PT, false, true>(kp, s)
+               : launch_p1<MK, VK, PT, false, false>(kp, s);
 }
 
-ta_status dispatch_p1(int mk, int vk, int pt, bool uni, const KParams& kp, cudaStream_t s) {
-#define TA_P1(M, V)                                                      \
-  if (mk == M && vk == V)                                                \
-    return pt ? launch_p1_u<M, V, 1>(uni, kp, s) : launch_p1_u<M, V, 0>(uni, kp, s);
+ta_status dispatch_p1(int mk, int vk, int pt, bool uni, bool table, const KParams& kp,
+                      cudaStream_t s) {
+#define TA_P1(M, V)                                                               \
+  if (mk == M && vk == V)                                                         \
+    return pt ? launch_p1_u<M, V, 1>(uni, table, kp, s)                           \
+              : launch_p1_u<M, V, 0>(uni, table, kp, s);
   TA_P1(MK_COSTATE, VK_ONEQ)
   TA_P1(MK_COSTATE, VK_FP32)
   TA_P1(MK_COSTATE, VK_NONE)
@@ -263,6 +273,7 @@ DevTensor make_dev(const ta_tensor& t, const ta_group& g, uint64_t seed) {
   D.seed_lo = (uint32_t)seed;
   D.seed_hi = (uint32_t)(seed >> 32);
   D.sel_chunks = (int32_t)cdiv(D.bpad, SEL_CHUNK);
+  D.alpha_chunks = (int32_t)cdiv(D.bpad / TB, FIN_THREADS);
   return D;
 }
 
@@ -297,15 +308,17 @@ ta_status run_step(const ta_tensor* ts, int nT, const ta_group* groups, uint64_t
       H[i].hist = reinterpret_cast<uint32_t*>(ws + s.hist);
       H[i].sel = reinterpret_cast<uint32_t*>(ws + s.sel);
       H[i].alpha_new = reinterpret_cast<float*>(ws + s.alpha);
+      H[i].chunk = reinterpret_cast<double*>(ws + s.chunk);
       cs_list.push_back(i);
     }
   }
   // launch lists: pass 1 by (mk, vk, pt, uni), pass 2 by pt, select chunks
-  struct P1Key { int mk, vk, pt; bool uni; };
+  struct P1Key { int mk, vk, pt; bool uni, table; };
   std::vector<std::pair<P1Key, LaunchList>> p1;
   auto p1_list = [&](P1Key k) -> LaunchList& {
     for (auto& e : p1)
-      if (e.first.mk == k.mk && e.first.vk == k.vk && e.first.pt == k.pt && e.first.uni == k.uni)
+      if (e.first.mk == k.mk && e.first.vk == k.vk && e.first.pt == k.pt &&
+          e.first.uni == k.uni && e.first.table == k.table)
         return e.second;
     p1.push_back({k, LaunchList()});
     p1.back().second.beg.push_back(0);
@@ -314,13 +327,15 @@ ta_status run_step(const ta_tensor* ts, int nT, const ta_group* groups, uint64_t
   LaunchList p2[2];
   p2[0].beg.push_back(0);
   p2[1].beg.push_back(0);
-  LaunchList sel;
+  LaunchList sel, alist;
   sel.beg.push_back(0);
+  alist.beg.push_back(0);
   for (int i = 0; i < nT; ++i) {
     if (ts[i].numel == 0) continue;
     const DevTensor& D = H[i];
     const int pt = ts[i].dtype == TA_BF16 ? 1 : 0;
-    P1Key k{mk_of(ts[i]), vk_of(ts[i]), pt, (D.flags & DF_UNI) && vk_of(ts[i]) == VK_ONEQ};
+    const bool oneq = vk_of(ts[i]) == VK_ONEQ;
+    P1Key k{mk_of(ts[i]), vk_of(ts[i]), pt, (D.flags & DF_UNI) && oneq, oneq && D.nbits <= 6};
     LaunchList& l = p1_list(k);
     const int64_t tiles = cdiv(D.nblk, TB);
     l.idx.push_back(i);
@@ -330,6 +345,8 @@ ta_status run_step(const ta_tensor* ts, int nT, const ta_group* groups, uint64_t
       p2[pt].beg.push_back(p2[pt].beg.back() + tiles);
       sel.idx.push_back(i);
       sel.beg.push_back(sel.beg.back() + D.sel_chunks);
+      alist.idx.push_back(i);
+      alist.beg.push_back(alist.beg.back() + D.alpha_chunks);
     }
   }
   // serialise the lists into the host image of the workspace
@@ -344,6 +361,15 @@ ta_status run_step(const ta_tensor* ts, int nT, const ta_group* groups, uint64_t
                                              (size_t)(nT + 1) * sizeof(int64_t));
     ++slot;
   };
+  uint32_t rk0[10], rk1[10];
+  for (int r = 0; r < 10; ++r) {  // Philox key schedule (ta_philox4x32_10)
+    rk0[r] = (uint32_t)seed + (uint32_t)r * TA_PHILOX_W0;
+    rk1[r] = (uint32_t)(seed >> 32) + (uint32_t)r * TA_PHILOX_W1;
+  }
+  auto set_rk = [&](KParams& kp) {
+    memcpy(kp.rk0, rk0, sizeof(rk0));
+    memcpy(kp.rk1, rk1, sizeof(rk1));
+  };
   std::vector<KParams> p1k(p1.size());
   uint32_t* status = reinterpret_cast<uint32_t*>(ws + L.status);
   const DevTensor* dT = reinterpret_cast<const DevTensor*>(ws + L.table);
@@ -354,6 +380,7 @@ ta_status run_step(const ta_tensor* ts, int nT, const ta_group* groups, uint64_t
     kp.nl = (int32_t)p1[i].second.idx.size();
     kp.total = p1[i].second.beg.back();
     kp.status = status;
+    set_rk(kp);
   }
   KParams p2k[2];
   for (int pt = 0; pt < 2; ++pt) {
@@ -362,26 +389,30 @@ ta_status run_step(const ta_tensor* ts, int nT, const ta_group* groups, uint64_t
     p2k[pt].nl = (int32_t)p2[pt].idx.size();
     p2k[pt].total = p2[pt].beg.back();
     p2k[pt].status = status;
+    set_rk(p2k[pt]);
   }
   SelParams sp;
   sp.T = dT;
   put(sel, &sp.cbeg, &sp.cidx);
   sp.ncs = (int32_t)sel.idx.size();
   const int64_t nchunks = sel.beg.back();
-  // the cs list for k_alpha reuses the select list's tensor indices
-  const int32_t* d_cs = sp.cidx;
+  SelParams ap;
+  ap.T = dT;
+  put(alist, &ap.cbeg, &ap.cidx);
+  ap.ncs = (int32_t)alist.idx.size();
+  const int64_t achunks = alist.beg.back();
 
   TA_CU(cudaMemcpyAsync(ws + L.table, host.data() + L.table, host.size() - L.table,
                         cudaMemcpyHostToDevice, st));
   TA_CU(mark(0));
   for (size_t i = 0; i < p1.size(); ++i) {
     const P1Key& k = p1[i].first;
-    ta_status r = dispatch_p1(k.mk, k.vk, k.pt, k.uni, p1k[i], st);
+    ta_status r = dispatch_p1(k.mk, k.vk, k.pt, k.uni, k.table, p1k[i], st);
     if (r != TA_OK) return r;
   }
   TA_CU(mark(1));
   if (!cs_list.empty()) {
-    k_alpha<<<(unsigned)cs_list.size(), FIN_THREADS, 0, st>>>(dT, d_cs, (int)cs_list.size());
+    k_alpha<<<(unsigned)achunks, FIN_THREADS, 0, st>>>(ap);
     TA_CU(cudaGetLastError());
     TA_CU(mark(2));
     if (p2k[0].total) {

@@ -15,10 +15,10 @@ constexpr int TB = 16;              // blocks per work tile
 constexpr int TE = BS * TB;         // elements per work tile
 constexpr int NCW = 4;              // consumer warps per CTA (4 blocks each)
 constexpr int NTHR = (NCW + 1) * 32;// + one producer warp
-constexpr int NSTAGE = 3;           // smem pipeline depth
+constexpr int NSTAGE = 2;           // smem pipeline depth (more CTAs per SM instead)
 constexpr uint32_t WAIT_LIMIT = 1u << 27;  // bounded mbarrier polling
 
-constexpr int FIN_THREADS = 256;    // alpha finalisation CTA
+constexpr int FIN_THREADS = 256;    // alpha chunk CTA (tiles per chunk)
 constexpr int SEL_CHUNK = 4096;     // ratios per radix-select CTA
 constexpr int SEL_THREADS = 256;
 constexpr int HBINS = 2048;
@@ -63,6 +63,7 @@ struct __align__(16) DevTensor {
   uint32_t* hist;    // [3][2][HBINS]
   uint32_t* sel;     // [16] select state
   float* alpha_new;  // [4]: alpha_new, tau0, tau1
+  double* chunk;     // [2][alpha_chunks] fp64 chunk sums (m.g, g.g)
   int64_t n;
   int64_t nblk;
   int64_t bpad;      // nblk rounded up to whole tiles
@@ -76,12 +77,12 @@ struct __align__(16) DevTensor {
   uint32_t step;
   uint32_t seed_lo, seed_hi;
   int32_t sel_chunks;  // ceil(bpad / SEL_CHUNK)
-  int32_t pad_;
+  int32_t alpha_chunks;  // ceil(tiles / FIN_THREADS)
 };
 
 // sel[] layout
-enum { SEL_CNT0 = 0, SEL_CNT1 = 1, SEL_CNT2 = 2, SEL_PLO = 4, SEL_PHI = 5, SEL_RLO = 6,
-       SEL_RHI = 7 };
+enum { SEL_CNT0 = 0, SEL_CNT1 = 1, SEL_CNT2 = 2, SEL_CNTA = 3, SEL_PLO = 4, SEL_PHI = 5,
+       SEL_RLO = 6, SEL_RHI = 7 };
 
 // ---- PTX wrappers --------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -153,17 +154,29 @@ __device__ __forceinline__ void bulk_wait_all() {
 // torch clamp(min=lo) semantics: NaN propagates.
 __device__ __forceinline__ float clamp_min(float v, float lo) { return (v < lo) ? lo : v; }
 
-// a / b, correctly rounded, given y = RN(1/b) (Markstein: q = RN(a*y),
-// r = a - b*q exact by FMA, RN(q + r*y) = RN(a/b) when nothing under- or
-// overflows); falls back to the IEEE division outside a safe range.
+// a / b, correctly rounded, given y = RN(1/b) and b a positive normal number.
+// Markstein: q = RN(a*y), r = a - b*q (exact by FMA), RN(q + r*y) = RN(a/b)
+// whenever a*y neither under- nor overflows and r is exact; that holds for
+// |a| in [2^-100, 2^100] and a == 0. Non-finite a gives a*y (= a/b exactly).
+// Callers keep |a| in that range (see the per-use notes) -- no branch.
 __device__ __forceinline__ float div_by(float a, float b, float y) {
-  float aa = fabsf(a);
-  if (aa < 0x1p100f && (aa >= 0x1p-100f || a == 0.0f)) {
-    float q = __fmul_rn(a, y);
-    float r = __fmaf_rn(-q, b, a);
-    return __fmaf_rn(r, y, q);
-  }
-  return __fdiv_rn(a, b);
+  float q = __fmul_rn(a, y);
+  float r = __fmaf_rn(-q, b, a);
+  float q2 = __fmaf_rn(r, y, q);
+  return (fabsf(a) <= 3.4028234663852886e38f) ? q2 : q;
+}
+
+// v / bc2 for v >= 0 (bc2 in (0, 1], y = RN(1/bc2)), exact for v = 0 and all
+// normal or non-finite v: v < 2^-100 is scaled by 2^64 first (exact), the
+// quotient (>= v >= 2^-126) scaled back (exact). Subnormal v is flagged for
+// the caller's IEEE fallback.
+__device__ __forceinline__ float div_v_bc2(float v, float bc2, float y, bool* sub) {
+  const bool tiny = v < 0x1p-100f;
+  const float s = tiny ? 0x1p64f : 1.0f;
+  const float si = tiny ? 0x1p-64f : 1.0f;
+  float q = div_by(__fmul_rn(v, s), bc2, y);
+  *sub = *sub || (v < 0x1p-126f && v > 0.0f);
+  return __fmul_rn(q, si);
 }
 
 __device__ __forceinline__ float ld_elem_f32(const float* p) { return *p; }

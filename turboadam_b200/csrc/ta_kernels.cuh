@@ -2,20 +2,26 @@
 // (launched by ta_api.cu, the C-ABI of include/turboadam_b200.h).
 //
 // Data flow of one step (all tensors of a kind share one launch):
-//   pass 1  (HBM stream over p, g and packed state; 1D TMA bulk copies into a
-//            3-stage smem ring, one producer warp, four consumer warps):
-//            weight decay, m update (CoState decode+EMA or fp32 EMA), v update
-//            (1Q decode -> EMA -> Philox stochastic re-quantisation, or fp32
-//            EMA), p.addcdiv_, per-block partial dots m.g and g.g.
-//   finalise alpha = (m.g)/(g.g) per CoState tensor (fixed-order fp64 sum).
+//   pass 1  (one HBM stream over p, g and packed state; 1D TMA bulk copies
+//            into a 2-stage smem ring, one producer warp, four consumer
+//            warps): weight decay, m update (CoState decode+EMA or fp32
+//            EMA), v update (1Q decode -> EMA -> ln v), p.addcdiv_, then the
+//            stochastic re-quantisation of v, and per-block partial dots.
+//   alpha   (m.g)/(g.g) per CoState tensor: per-chunk fp64 trees, the last
+//            CTA of each tensor sums the chunks in order.
 //   pass 2  (CoState tensors: re-read g and the old encoding, recompute m_new
 //            bit-identically, delta = m - alpha g, MSB-first sign bits, torch-
 //            order block norms, fp16 scales, block ratios).
 //   select  exact P10/P90 of the ratios: 3 histogram rounds over the fp32 bit
 //            pattern (11/11/10 bits), the last CTA of each tensor scans.
 //   labels  0/1/2 by >= thresholds, alpha committed to the state.
-// Arithmetic matches the reference CPU path op by op (see oracle/ta_oracle.c,
-// which restates it) and ta_math.h for log/exp/fp16/Philox.
+// Arithmetic matches the reference CPU path op by op (oracle/ta_oracle.c
+// restates it) with ta_math.h for log/exp/fp16/Philox.
+//
+// Lane mapping (passes 1 and 2): a warp owns 4 blocks of the 16-block tile,
+// one per 8-lane group; lane j of a group owns elements j + 8k, k = 0..15.
+// Per-element smem arrays are placed one block per skewed stride so the 4
+// groups of a warp hit disjoint banks.
 #pragma once
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -31,7 +37,8 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
-// Bounded mbarrier wait against wall time (2 s), see ta_device.cuh.
+// Bounded mbarrier wait against wall time (2 s): on expiry the status word
+// records TA_STATUS_WAIT_TIMEOUT and the caller drains and returns.
 __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, uint32_t* status) {
   if (mbar_try_wait(bar, parity)) return true;
   uint64_t t0 = globaltimer_ns();
@@ -82,7 +89,10 @@ struct P2L {
   static constexpr int STAGE = (END + 127) / 128 * 128;
 };
 
-struct StageMeta {
+// Per-stage metadata written by the producer before it arms the barrier: the
+// tensor's descriptor (so consumers read it from smem, not global memory).
+struct __align__(16) StageMeta {
+  DevTensor D;
   int32_t t;     // tensor index
   int32_t nblk;  // blocks of this tile
   int64_t b0;    // first block (within tensor)
@@ -97,6 +107,7 @@ struct KParams {
   int32_t nl;
   int64_t total;        // tiles in this launch
   uint32_t* status;
+  uint32_t rk0[10], rk1[10];  // Philox round keys (seed words + r * Weyl constants)
 };
 
 __device__ __forceinline__ int find_entry(const int64_t* lbeg, int nl, int64_t tile) {
@@ -109,23 +120,74 @@ __device__ __forceinline__ int find_entry(const int64_t* lbeg, int nl, int64_t t
   return lo;
 }
 
-// Shared CoState decode of one element (costate.py:261-323, :416):
-//   m_hat = fl(fl(alpha_old*g) + fl(scale*sign)), m = fl(fl(b1*m_hat) + fl(omb1*g)).
+// Philox4x32-10 with precomputed round keys (identical to ta_philox4x32_10).
+__device__ __forceinline__ void philox_rk(uint32_t c0, uint32_t c1, uint32_t c2, uint32_t c3,
+                                          const uint32_t* rk0, const uint32_t* rk1,
+                                          uint32_t out[4]) {
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    const uint64_t p0 = (uint64_t)TA_PHILOX_M0 * (uint64_t)c0;
+    const uint64_t p1 = (uint64_t)TA_PHILOX_M1 * (uint64_t)c2;
+    const uint32_t hi0 = (uint32_t)(p0 >> 32), lo0 = (uint32_t)p0;
+    const uint32_t hi1 = (uint32_t)(p1 >> 32), lo1 = (uint32_t)p1;
+    c0 = hi1 ^ c1 ^ rk0[r];
+    c1 = lo1;
+    c2 = hi0 ^ c3 ^ rk1[r];
+    c3 = lo0;
+  }
+  out[0] = c0; out[1] = c1; out[2] = c2; out[3] = c3;
+}
+
+// CoState decode + EMA of one element (costate.py:261-323, :416):
+//   m_hat = has_state ? fl(fl(alpha_old*g) + fl(scale*sign)) : 0
+//   m     = fl(fl(b1*m_hat) + fl(omb1*g))
+// scale*sign is an exact sign flip of scale.
 __device__ __forceinline__ float costate_m(float g, float alpha_old, float scale, uint32_t bit,
                                            bool has_state, float b1, float omb1) {
-  float mh = 0.0f;
-  if (has_state) {
-    float sd = __fmul_rn(scale, bit ? -1.0f : 1.0f);
-    mh = __fadd_rn(__fmul_rn(alpha_old, g), sd);
-  }
+  const float sd = __uint_as_float(__float_as_uint(scale) ^ (bit << 31));
+  float mh = __fadd_rn(__fmul_rn(alpha_old, g), sd);
+  mh = has_state ? mh : 0.0f;
   return __fadd_rn(__fmul_rn(b1, mh), __fmul_rn(omb1, g));
 }
 
 __device__ __forceinline__ float costate_scale(uint8_t label, float norm, uint16_t amp,
                                                float sqbs) {
-  if (label == 1) return __fdiv_rn(norm, sqbs);
-  if (label == 2) return ta_f16_to_f32(amp);
-  return 0.0f;
+  const float ph = __fdiv_rn(norm, sqbs);
+  const float am = ta_f16_to_f32(amp);
+  return label == 1 ? ph : (label == 2 ? am : 0.0f);
+}
+
+// Branch-free ta_logf for the kernels (same value as ta_logf for every input):
+// special cases are resolved by selects after the common polynomial.
+__device__ __forceinline__ float log_bf(float x) {
+  const bool sub = x < 0x1p-126f;
+  const float xs = __fmul_rn(x, sub ? 0x1p23f : 1.0f);
+  const int32_t ex = sub ? -23 : 0;
+  const uint32_t ix = __float_as_uint(xs);
+  const int32_t e = ((int32_t)(ix - 0x3f2aaaabu)) >> 23;
+  const float m = __uint_as_float(ix - ((uint32_t)e << 23));
+  const float f = __fsub_rn(m, 1.0f);
+  const float ef = (float)(e + ex);
+  float q = TA_LOG_Q0;
+  q = __fmaf_rn(q, f, TA_LOG_Q1);
+  q = __fmaf_rn(q, f, TA_LOG_Q2);
+  q = __fmaf_rn(q, f, TA_LOG_Q3);
+  q = __fmaf_rn(q, f, TA_LOG_Q4);
+  q = __fmaf_rn(q, f, TA_LOG_Q5);
+  q = __fmaf_rn(q, f, TA_LOG_Q6);
+  q = __fmaf_rn(q, f, TA_LOG_Q7);
+  q = __fmaf_rn(q, f, TA_LOG_Q8);
+  q = __fmaf_rn(q, f, TA_LOG_Q9);
+  const float f2 = __fmul_rn(f, f);
+  const float hi = __fmul_rn(ef, TA_LN2_HI);
+  const float s = __fadd_rn(hi, f);
+  const float err = __fadd_rn(__fsub_rn(hi, s), f);
+  const float lo = __fmaf_rn(f2, q, __fmaf_rn(ef, TA_LN2_LO, err));
+  float r = __fadd_rn(s, lo);
+  r = (x == INFINITY) ? x : r;
+  r = (x == 0.0f) ? -INFINITY : r;
+  r = (x < 0.0f || x != x) ? __uint_as_float(0x7fc00000u) : r;
+  return r;
 }
 
 // ---------------------------------------------------------------------------
@@ -142,10 +204,8 @@ __device__ __forceinline__ void p1_issue(const DevTensor& D, uint8_t* st, int nb
     if (!count_only) bulk_g2s(dst, src, nb, bar);
   };
   for (int i = 0; i < nblk; ++i) {
-    int64_t b = b0 + i;
-    int64_t e0 = b * BS;
-    bool full = (D.n - e0) >= BS;
-    if (full) {
+    const int64_t e0 = (b0 + i) * BS;
+    if (D.n - e0 >= BS) {  // full block: user arrays too
       if (param)
         cp(st + L::OFF_P + i * L::STR_P, (const uint8_t*)D.p + e0 * L::ESZ, BS * L::ESZ);
       cp(st + L::OFF_G + i * L::STR_P, (const uint8_t*)D.g + e0 * L::ESZ, BS * L::ESZ);
@@ -154,7 +214,7 @@ __device__ __forceinline__ void p1_issue(const DevTensor& D, uint8_t* st, int nb
     }
     if (VK == VK_ONEQ) {
       cp(st + L::OFF_IDX + i * L::STR_1, D.v_idx + e0, BS);
-      if (UNI && (D.flags & DF_UNI)) cp(st + L::OFF_UNI + i * L::STR_4, D.uni + e0, BS * 4);
+      if (UNI) cp(st + L::OFF_UNI + i * L::STR_4, D.uni + e0, BS * 4);
     }
   }
   // per-tile arrays (state arrays are padded to whole tiles)
@@ -172,9 +232,8 @@ __device__ __forceinline__ void p1_store(const DevTensor& D, uint8_t* st, int nb
   using L = P1L<MK, VK, PT, UNI>;
   const bool param = !(D.flags & DF_NO_PARAM);
   for (int i = 0; i < nblk; ++i) {
-    int64_t e0 = (b0 + i) * BS;
-    bool full = (D.n - e0) >= BS;
-    if (full) {
+    const int64_t e0 = (b0 + i) * BS;
+    if (D.n - e0 >= BS) {
       if (param) bulk_s2g((uint8_t*)D.p + e0 * L::ESZ, st + L::OFF_P + i * L::STR_P, BS * L::ESZ);
       if (MK == MK_FP32) bulk_s2g(D.ea + e0, st + L::OFF_EA + i * L::STR_4, BS * 4);
       if (VK == VK_FP32) bulk_s2g(D.eas + e0, st + L::OFF_EAS + i * L::STR_4, BS * 4);
@@ -184,102 +243,181 @@ __device__ __forceinline__ void p1_store(const DevTensor& D, uint8_t* st, int nb
   if (VK == VK_ONEQ) bulk_s2g(D.v_hdr + b0 * 2, st + L::OFF_HDR, TB * 4);
 }
 
-// One 128-element block per 8-lane group: lane j owns elements j + 8k.
+// Per-tensor scalars, read once per block from the smem descriptor copy.
+struct Sc {
+  float b1, omb1, b2, omb2, wdf, nlr, eps, bc1, bc2, rbc2, nbf, sqbs;
+  uint32_t flags, tid, step;
+  int nbits;
+};
+
+__device__ __forceinline__ Sc load_sc(const DevTensor& D) {
+  Sc s;
+  s.b1 = D.b1; s.omb1 = D.omb1; s.b2 = D.b2; s.omb2 = D.omb2;
+  s.wdf = (D.flags & DF_WD) ? D.wdf : 1.0f;  // p * 1 == p exactly (optimizer.py:106)
+  s.nlr = D.nlr; s.eps = D.eps; s.bc1 = D.bc1; s.bc2 = D.bc2; s.rbc2 = D.rbc2;
+  s.nbf = D.nbf; s.sqbs = D.sqbs;
+  s.flags = D.flags; s.tid = D.tid; s.step = D.step; s.nbits = D.nbits;
+  return s;
+}
+
+// One element of the p update (optimizer.py:106-107, 163/167, 170), given the
+// already rounded weight-decayed parameter, m_new and v_new.
+template <int PT>
+__device__ __forceinline__ float adam_elem(float pv, float m, float vn, const Sc& c, bool* sub) {
+  pv = __fmul_rn(pv, c.wdf);
+  if (PT) pv = ta_bf16_to_f32(ta_f32_to_bf16(pv));
+  const float d = __fadd_rn(__fsqrt_rn(div_v_bc2(vn, c.bc2, c.rbc2, sub)), c.eps);
+  const float upd = __fdiv_rn(__fmul_rn(c.nlr, m), __fmul_rn(d, c.bc1));
+  return __fadd_rn(pv, upd);
+}
+
+// Exact IEEE version of the same update for elements whose v/bc2 needs the
+// subnormal path (v_new < 2^-126 after ~18k zero-gradient steps).
+template <int PT>
+__device__ __noinline__ float adam_elem_ieee(float pv, float m, float vn, const Sc& c) {
+  pv = __fmul_rn(pv, c.wdf);
+  if (PT) pv = ta_bf16_to_f32(ta_f32_to_bf16(pv));
+  const float d = __fadd_rn(__fsqrt_rn(__fdiv_rn(vn, c.bc2)), c.eps);
+  const float upd = __fdiv_rn(__fmul_rn(c.nlr, m), __fmul_rn(d, c.bc1));
+  return __fadd_rn(pv, upd);
+}
+
+// Exact recomputation of one element of a full block (rare path): used when
+// v/bc2 needs the subnormal IEEE fallback or a stored index is >= 2^nbits.
+// Recomputes m, v_new, ln v_new and the parameter update from the staged
+// inputs (the old parameter is still in global memory, the tile has not been
+// stored yet) and writes the updated parameter to smem. Returns ln v_new.
 template <int MK, int VK, int PT, bool UNI>
-__device__ __forceinline__ void p1_block(const DevTensor& D, uint8_t* st, int nblk, int64_t b0,
-                                         float* table, uint32_t* status) {
+__device__ __noinline__ float p1_fix_elem(const DevTensor& D, const Sc& c, uint8_t* st, int bi,
+                                          int t, int64_t e, float alpha_old, float cs_scale,
+                                          uint32_t bit, bool has_state, float lmin, float span) {
+  using L = P1L<MK, VK, PT, UNI>;
+  uint8_t* sp = st + L::OFF_P + bi * L::STR_P;
+  const uint8_t* sg = st + L::OFF_G + bi * L::STR_P;
+  const float g = PT ? ta_bf16_to_f32(reinterpret_cast<const uint16_t*>(sg)[t])
+                     : reinterpret_cast<const float*>(sg)[t];
+  float m = 0.0f;
+  if (MK == MK_COSTATE) m = costate_m(g, alpha_old, cs_scale, bit, has_state, c.b1, c.omb1);
+  else if (MK == MK_FP32) m = reinterpret_cast<const float*>(st + L::OFF_EA + bi * L::STR_4)[t];
+  float vn = 0.0f, lv = 0.0f;
+  if (VK == VK_ONEQ) {
+    const int id = st[L::OFF_IDX + bi * L::STR_1 + t];
+    const float qv = __fdiv_rn(__fadd_rn((float)id, 0.5f), c.nbf);
+    const float vo = ta_expf(__fadd_rn(lmin, __fmul_rn(qv, span)));
+    vn = __fmaf_rn(__fmul_rn(g, g), c.omb2, __fmul_rn(vo, c.b2));
+    lv = log_bf(clamp_min(vn, 1e-38f));
+  } else if (VK == VK_FP32) {
+    vn = reinterpret_cast<const float*>(st + L::OFF_EAS + bi * L::STR_4)[t];
+  }
+  if (!(c.flags & DF_NO_PARAM)) {
+    const float pv = adam_elem_ieee<PT>(to_f32<PT>(D.p, e), m, vn, c);
+    if (PT) reinterpret_cast<uint16_t*>(sp)[t] = ta_f32_to_bf16(pv);
+    else reinterpret_cast<float*>(sp)[t] = pv;
+  }
+  return lv;
+}
+
+// One 128-element block per 8-lane group. FULL: every group of the warp has a
+// full block (no bounds checks, user arrays from smem); otherwise the general
+// path with per-element bounds and global loads for the ragged tail block.
+template <int MK, int VK, int PT, bool UNI, bool TABLE, bool FULL>
+__device__ __forceinline__ void p1_block(const DevTensor& D, const Sc& c, uint8_t* st, int nblk,
+                                         int64_t b0, float* table, const KParams& kp) {
   using L = P1L<MK, VK, PT, UNI>;
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int q = lane >> 3;
   const int j = lane & 7;
   const int bi = warp * 4 + q;
-  const bool active = bi < nblk;
+  const bool active = FULL || bi < nblk;
   const int64_t b = b0 + bi;
   const int64_t e0 = b * BS;
-  const int nv = active ? (int)min((int64_t)BS, D.n - e0) : 0;
-  const bool full = nv == BS;
-  const bool param = !(D.flags & DF_NO_PARAM);
+  const int nv = FULL ? BS : (active ? (int)min((int64_t)BS, D.n - e0) : 0);
+  const bool fullblk = FULL || nv == BS;
+  const bool param = !(c.flags & DF_NO_PARAM);
 
   uint8_t* sp = st + L::OFF_P + bi * L::STR_P;
-  uint8_t* sg = st + L::OFF_G + bi * L::STR_P;
+  const uint8_t* sg = st + L::OFF_G + bi * L::STR_P;
 
   // ---- per-block CoState decode scalars (costate.py:290-314)
   float cs_scale = 0.0f, alpha_old = 0.0f;
   uint32_t sw[4] = {0, 0, 0, 0};
-  const bool has_state = (MK == MK_COSTATE) && (D.flags & DF_M_HAS_STATE);
+  const bool has_state = (MK == MK_COSTATE) && (c.flags & DF_M_HAS_STATE);
   if (MK == MK_COSTATE && has_state && active) {
-    uint8_t lab = st[L::OFF_LAB + bi];
-    float nrm = reinterpret_cast<const float*>(st + L::OFF_NRM)[bi];
-    uint16_t amp = reinterpret_cast<const uint16_t*>(st + L::OFF_AMP)[bi];
-    cs_scale = costate_scale(lab, nrm, amp, D.sqbs);
-    uint4 w = *reinterpret_cast<const uint4*>(st + L::OFF_SGN + bi * 16);
+    const uint8_t lab = st[L::OFF_LAB + bi];
+    const float nrm = reinterpret_cast<const float*>(st + L::OFF_NRM)[bi];
+    const uint16_t amp = reinterpret_cast<const uint16_t*>(st + L::OFF_AMP)[bi];
+    cs_scale = costate_scale(lab, nrm, amp, c.sqbs);
+    const uint4 w = *reinterpret_cast<const uint4*>(st + L::OFF_SGN + bi * 16);
     sw[0] = w.x; sw[1] = w.y; sw[2] = w.z; sw[3] = w.w;
     alpha_old = *D.alpha_state;
   }
 
   // ---- per-block 1Q decode scalars (quantize.py:252-256) and exp table
   float lmin = 0.0f, span = 0.0f;
-  const int nb = 1 << D.nbits;
-  const bool use_table = D.nbits <= 6;
+  const int nb = 1 << c.nbits;
+  float* tab = table + q * TABLE_STRIDE;
   if (VK == VK_ONEQ) {
     const uint16_t* hdr = reinterpret_cast<const uint16_t*>(st + L::OFF_HDR);
     if (active) {
       lmin = ta_f16_to_f32(hdr[bi * 2]);
       span = __fsub_rn(ta_f16_to_f32(hdr[bi * 2 + 1]), lmin);
     }
-    if (use_table) {
+    if (TABLE) {
       for (int t = j; t < nb; t += 8) {
-        float qv = __fdiv_rn(__fadd_rn((float)t, 0.5f), D.nbf);
-        table[q * TABLE_STRIDE + t] = ta_expf(__fadd_rn(lmin, __fmul_rn(qv, span)));
+        const float qv = __fdiv_rn(__fadd_rn((float)t, 0.5f), c.nbf);
+        tab[t] = ta_expf(__fadd_rn(lmin, __fmul_rn(qv, span)));
       }
     }
     __syncwarp();
   }
 
-  // ---- phase A: m, v, log v per element
-  float mk[16], vk[16], lk[16];
+  // ---- phase A: m, v, ln v, and the parameter update, per element
+  float lk[16];
   float mg = 0.0f, gg = 0.0f, gbad = 0.0f;
   float vmin = INFINITY, vmax = -INFINITY;
-  const float b1 = D.b1, omb1 = D.omb1, b2 = D.b2, omb2 = D.omb2;
+  bool sub = false, badidx = false;
 #pragma unroll
   for (int k = 0; k < 16; ++k) {
     const int t = j + 8 * k;
     const int64_t e = e0 + t;
-    const bool ve = t < nv;
+    const bool ve = FULL || t < nv;
     float g;
-    if (full) g = PT ? ta_bf16_to_f32(reinterpret_cast<const uint16_t*>(sg)[t])
+    if (FULL) g = PT ? ta_bf16_to_f32(reinterpret_cast<const uint16_t*>(sg)[t])
                      : reinterpret_cast<const float*>(sg)[t];
+    else if (fullblk) g = PT ? ta_bf16_to_f32(reinterpret_cast<const uint16_t*>(sg)[t])
+                             : reinterpret_cast<const float*>(sg)[t];
     else g = ve ? to_f32<PT>(D.g, e) : 0.0f;
     gbad = __fmaf_rn(g, 0.0f, gbad);
     float m = 0.0f;
     if (MK == MK_COSTATE) {
-      uint32_t bit = (sw[k >> 2] >> (8 * (k & 3) + 7 - j)) & 1u;
-      m = costate_m(g, alpha_old, cs_scale, bit, has_state, b1, omb1);
+      const uint32_t bit = (sw[k >> 2] >> (8 * (k & 3) + 7 - j)) & 1u;
+      m = costate_m(g, alpha_old, cs_scale, bit, has_state, c.b1, c.omb1);
       if (ve) {
         mg = __fmaf_rn(m, g, mg);
         gg = __fmaf_rn(g, g, gg);
       }
     } else if (MK == MK_FP32) {
       float* sea = reinterpret_cast<float*>(st + L::OFF_EA + bi * L::STR_4);
-      float ea = full ? sea[t] : (ve ? D.ea[e] : 0.0f);
-      m = __fmaf_rn(g, omb1, __fmul_rn(ea, b1));  // optimizer.py:113
-      if (full) sea[t] = m;
+      const float ea = fullblk ? sea[t] : (ve ? D.ea[e] : 0.0f);
+      m = __fmaf_rn(g, c.omb1, __fmul_rn(ea, c.b1));  // optimizer.py:113
+      if (fullblk) sea[t] = m;
       else if (ve) D.ea[e] = m;
     }
-    mk[k] = m;
     float vn = 0.0f;
     if (VK == VK_ONEQ) {
       const int id = active ? st[L::OFF_IDX + bi * L::STR_1 + t] : 0;
       float vo;
-      if (use_table && id < nb) vo = table[q * TABLE_STRIDE + id];
-      else {
-        float qv = __fdiv_rn(__fadd_rn((float)id, 0.5f), D.nbf);
+      if (TABLE && fullblk) {
+        badidx = badidx || (id >= nb);
+        vo = tab[min(id, nb - 1)];
+      } else {
+        const float qv = __fdiv_rn(__fadd_rn((float)id, 0.5f), c.nbf);
         vo = ta_expf(__fadd_rn(lmin, __fmul_rn(qv, span)));
       }
-      float g2 = ve ? __fmul_rn(g, g) : 0.0f;
-      vn = __fmaf_rn(g2, omb2, __fmul_rn(vo, b2));  // quantize.py:270
-      float lv = ta_logf(clamp_min(vn, 1e-38f));   // quantize.py:275
+      const float g2 = ve ? __fmul_rn(g, g) : 0.0f;
+      vn = __fmaf_rn(g2, c.omb2, __fmul_rn(vo, c.b2));  // quantize.py:270
+      const float lv = log_bf(clamp_min(vn, 1e-38f));   // quantize.py:275
       lk[k] = lv;
       if (ve) {
         vmin = (lv < vmin) ? lv : vmin;
@@ -287,14 +425,51 @@ __device__ __forceinline__ void p1_block(const DevTensor& D, uint8_t* st, int nb
       }
     } else if (VK == VK_FP32) {
       float* sea = reinterpret_cast<float*>(st + L::OFF_EAS + bi * L::STR_4);
-      float vs = full ? sea[t] : (ve ? D.eas[e] : 0.0f);
-      vn = __fmaf_rn(__fmul_rn(omb2, g), g, __fmul_rn(vs, b2));  // optimizer.py:166
-      if (full) sea[t] = vn;
+      const float vs = fullblk ? sea[t] : (ve ? D.eas[e] : 0.0f);
+      vn = __fmaf_rn(__fmul_rn(c.omb2, g), g, __fmul_rn(vs, c.b2));  // optimizer.py:166
+      if (fullblk) sea[t] = vn;
       else if (ve) D.eas[e] = vn;
     }
-    vk[k] = vn;
+    if (param && ve) {
+      float pv;
+      if (fullblk) pv = PT ? ta_bf16_to_f32(reinterpret_cast<const uint16_t*>(sp)[t])
+                           : reinterpret_cast<const float*>(sp)[t];
+      else pv = to_f32<PT>(D.p, e);
+      pv = fullblk ? adam_elem<PT>(pv, m, vn, c, &sub) : adam_elem_ieee<PT>(pv, m, vn, c);
+      if (PT) {
+        const uint16_t h = ta_f32_to_bf16(pv);
+        if (fullblk) reinterpret_cast<uint16_t*>(sp)[t] = h;
+        else reinterpret_cast<uint16_t*>(D.p)[e] = h;
+      } else {
+        if (fullblk) reinterpret_cast<float*>(sp)[t] = pv;
+        else reinterpret_cast<float*>(D.p)[e] = pv;
+      }
+    }
+    if (!FULL && ve && (c.flags & DF_M_OUT)) D.m_out[e] = m;
+    if (!FULL && ve && (c.flags & DF_V_OUT)) D.v_out[e] = vn;
   }
-  if (gbad != gbad) atomicOr(status, 1u);
+  if (gbad != gbad) atomicOr(kp.status, 1u);
+
+  // ---- rare exact fallbacks (full blocks only; tail blocks were exact above)
+  if (sub || badidx) {
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const uint32_t bit = (sw[k >> 2] >> (8 * (k & 3) + 7 - j)) & 1u;
+      const float lv = p1_fix_elem<MK, VK, PT, UNI>(D, c, st, bi, j + 8 * k, e0 + j + 8 * k,
+                                                     alpha_old, cs_scale, bit, has_state, lmin,
+                                                     span);
+      if (VK == VK_ONEQ) lk[k] = lv;
+    }
+    if (VK == VK_ONEQ) {  // block extrema from the recomputed logs
+      vmin = INFINITY;
+      vmax = -INFINITY;
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        vmin = (lk[k] < vmin) ? lk[k] : vmin;
+        vmax = (lk[k] > vmax) ? lk[k] : vmax;
+      }
+    }
+  }
 
   // ---- block partial dots for alpha (canonical order, see ta_oracle.c)
   if (MK == MK_COSTATE) {
@@ -309,85 +484,56 @@ __device__ __forceinline__ void p1_block(const DevTensor& D, uint8_t* st, int nb
     }
   }
 
-  // ---- 1Q block min/max, new header (quantize.py:276-285)
-  float mn = 0.0f, nspan = 1.0f, rspan = 1.0f;
+  // ---- 1Q: new header, then the stochastic re-quantisation (quantize.py:276-294)
   if (VK == VK_ONEQ) {
 #pragma unroll
     for (int off = 4; off >= 1; off >>= 1) {
-      float o1 = __shfl_xor_sync(0xffffffffu, vmin, off);
-      float o2 = __shfl_xor_sync(0xffffffffu, vmax, off);
+      const float o1 = __shfl_xor_sync(0xffffffffu, vmin, off);
+      const float o2 = __shfl_xor_sync(0xffffffffu, vmax, off);
       vmin = (o1 < vmin) ? o1 : vmin;
       vmax = (o2 > vmax) ? o2 : vmax;
     }
-    mn = vmin;
     if (active && j == 0) {
       uint16_t* hdr = reinterpret_cast<uint16_t*>(st + L::OFF_HDR);
       hdr[bi * 2] = ta_f32_to_f16(vmin);
       hdr[bi * 2 + 1] = ta_f32_to_f16(vmax);
     }
-    nspan = clamp_min(__fsub_rn(vmax, vmin), 1e-10f);
-    rspan = __frcp_rn(nspan);
-  }
-
-  // ---- phase B: stochastic re-quantisation and the parameter update
-  uint32_t rnd[4] = {0, 0, 0, 0};
-  const bool uni = UNI && (D.flags & DF_UNI);
-  const float* suni = reinterpret_cast<const float*>(st + L::OFF_UNI + bi * L::STR_4);
+    // (L - min) / span: |L - min| is 0 or >= 2^-47 (ln of floats != 1 is
+    // >= 5.9e-8 in magnitude), inside div_by's exact range.
+    const float nspan = clamp_min(__fsub_rn(vmax, vmin), 1e-10f);
+    const float rspan = __frcp_rn(nspan);
+    const float top = c.nbf - 1.0f;
+    const float* suni = reinterpret_cast<const float*>(st + L::OFF_UNI + bi * L::STR_4);
+    uint8_t* sidx = st + L::OFF_IDX + bi * L::STR_1;
+    uint32_t rnd[4] = {0, 0, 0, 0};
 #pragma unroll
-  for (int k = 0; k < 16; ++k) {
-    const int t = j + 8 * k;
-    const int64_t e = e0 + t;
-    const bool ve = t < nv;
-    if (VK == VK_ONEQ) {
+    for (int k = 0; k < 16; ++k) {
+      const int t = j + 8 * k;
       float u;
-      if (uni) {
+      if (UNI) {
         u = suni[t];
       } else {
         if ((k & 3) == 0) {
           uint32_t c0, c1, c2, c3;
-          ta_sr_counter((uint64_t)b, (uint32_t)j, (uint32_t)(k >> 2), D.tid, D.step, &c0, &c1,
+          ta_sr_counter((uint64_t)b, (uint32_t)j, (uint32_t)(k >> 2), c.tid, c.step, &c0, &c1,
                         &c2, &c3);
-          ta_philox4x32_10(c0, c1, c2, c3, D.seed_lo, D.seed_hi, rnd);
+          philox_rk(c0, c1, c2, c3, kp.rk0, kp.rk1, rnd);
         }
         u = ta_u01(rnd[k & 3]);
       }
-      float c = __fmul_rn(div_by(__fsub_rn(lk[k], mn), nspan, rspan), D.nbf);
-      float fl = floorf(c);
-      float fr = __fsub_rn(c, fl);
+      const float cc = __fmul_rn(div_by(__fsub_rn(lk[k], vmin), nspan, rspan), c.nbf);
+      const float fl = floorf(cc);
+      const float fr = __fsub_rn(cc, fl);
       float r = __fadd_rn(fl, (u < fr) ? 1.0f : 0.0f);
       r = (r < 0.0f) ? 0.0f : r;
-      r = (r > D.nbf - 1.0f) ? D.nbf - 1.0f : r;
-      if (active) st[L::OFF_IDX + bi * L::STR_1 + t] = (uint8_t)r;
+      r = (r > top) ? top : r;
+      if (active) sidx[t] = (uint8_t)r;
     }
-    if (param && ve) {
-      float pv;
-      if (full) pv = PT ? ta_bf16_to_f32(reinterpret_cast<const uint16_t*>(sp)[t])
-                        : reinterpret_cast<const float*>(sp)[t];
-      else pv = to_f32<PT>(D.p, e);
-      if (D.flags & DF_WD) {  // optimizer.py:106-107
-        pv = __fmul_rn(pv, D.wdf);
-        if (PT) pv = ta_bf16_to_f32(ta_f32_to_bf16(pv));
-      }
-      // optimizer.py:163 / :167 and :170
-      float d = __fadd_rn(__fsqrt_rn(div_by(vk[k], D.bc2, D.rbc2)), D.eps);
-      float upd = __fdiv_rn(__fmul_rn(D.nlr, mk[k]), __fmul_rn(d, D.bc1));
-      pv = __fadd_rn(pv, upd);
-      if (PT) {
-        uint16_t h = ta_f32_to_bf16(pv);
-        if (full) reinterpret_cast<uint16_t*>(sp)[t] = h;
-        else reinterpret_cast<uint16_t*>(D.p)[e] = h;
-      } else {
-        if (full) reinterpret_cast<float*>(sp)[t] = pv;
-        else reinterpret_cast<float*>(D.p)[e] = pv;
-      }
-    }
-    if (ve && (D.flags & DF_M_OUT)) D.m_out[e] = mk[k];
-    if (ve && (D.flags & DF_V_OUT)) D.v_out[e] = vk[k];
   }
 }
 
-template <int MK, int VK, int PT, bool UNI>
-__global__ void __launch_bounds__(NTHR) k_pass1(KParams kp) {
+template <int MK, int VK, int PT, bool UNI, bool TABLE>
+__global__ void __launch_bounds__(NTHR, 4) k_pass1(const __grid_constant__ KParams kp) {
   using L = P1L<MK, VK, PT, UNI>;
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* stages = smem;
@@ -418,7 +564,7 @@ __global__ void __launch_bounds__(NTHR) k_pass1(KParams kp) {
         if (it >= NSTAGE) {
           if (!wait_bar(&done[s], ph ^ 1u, kp.status)) { ok = false; break; }
           const StageMeta& pm = meta[s];
-          p1_store<MK, VK, PT, UNI>(kp.T[pm.t], st, pm.nblk, pm.b0);
+          p1_store<MK, VK, PT, UNI>(pm.D, st, pm.nblk, pm.b0);
           bulk_commit();
           bulk_wait_read_all();
         }
@@ -428,6 +574,7 @@ __global__ void __launch_bounds__(NTHR) k_pass1(KParams kp) {
         const int64_t lt = tile - kp.lbeg[en];
         const int64_t b0 = lt * TB;
         const int nblk = (int)min((int64_t)TB, D.nblk - b0);
+        meta[s].D = D;
         meta[s].t = t;
         meta[s].nblk = nblk;
         meta[s].b0 = b0;
@@ -442,13 +589,13 @@ __global__ void __launch_bounds__(NTHR) k_pass1(KParams kp) {
           const int s = r % NSTAGE;
           if (!wait_bar(&done[s], (uint32_t)(r / NSTAGE) & 1u, kp.status)) { ok = false; break; }
           const StageMeta& pm = meta[s];
-          p1_store<MK, VK, PT, UNI>(kp.T[pm.t], stages + s * L::STAGE, pm.nblk, pm.b0);
+          p1_store<MK, VK, PT, UNI>(pm.D, stages + s * L::STAGE, pm.nblk, pm.b0);
           bulk_commit();
         }
       }
       if (!ok)  // a wait ran out: let this CTA's own loads land before exiting
-        for (int r = first; r < it; ++r) wait_bar(&full[r % NSTAGE], (uint32_t)(r / NSTAGE) & 1u,
-                                                  kp.status);
+        for (int r = first; r < it; ++r)
+          wait_bar(&full[r % NSTAGE], (uint32_t)(r / NSTAGE) & 1u, kp.status);
       bulk_wait_all();
     }
     return;
@@ -460,9 +607,22 @@ __global__ void __launch_bounds__(NTHR) k_pass1(KParams kp) {
     const int s = it % NSTAGE;
     const uint32_t ph = (uint32_t)(it / NSTAGE) & 1u;
     if (!wait_bar(&full[s], ph, kp.status)) break;
-    const StageMeta pm = meta[s];
-    p1_block<MK, VK, PT, UNI>(kp.T[pm.t], stages + s * L::STAGE, pm.nblk, pm.b0, table,
-                              kp.status);
+    const StageMeta& pm = meta[s];
+    const DevTensor& D = pm.D;
+    const Sc c = load_sc(D);
+    const int nblk = pm.nblk;
+    const int64_t b0 = pm.b0;
+    uint8_t* st = stages + s * L::STAGE;
+    // the fast path needs all 4 blocks of this warp present and full, and no
+    // seam outputs; decided per warp so the shuffles stay convergent
+    const int bi = warp * 4 + (lane >> 3);
+    const bool mine_full = bi < nblk && D.n - (b0 + bi) * BS >= BS;
+    const bool fast = __all_sync(0xffffffffu, mine_full) &&
+                      !(c.flags & (DF_M_OUT | DF_V_OUT));
+    if (fast)
+      p1_block<MK, VK, PT, UNI, TABLE, true>(D, c, st, nblk, b0, table, kp);
+    else
+      p1_block<MK, VK, PT, UNI, TABLE, false>(D, c, st, nblk, b0, table, kp);
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) mbar_arrive(&done[s]);
@@ -476,103 +636,131 @@ constexpr size_t p1_smem_bytes() {
 }
 
 // ---------------------------------------------------------------------------
-// alpha finalisation (costate.py:22-43 with the canonical reduction order)
+// alpha (costate.py:22-43) with the canonical reduction order: chunk c of a
+// tensor (256 tiles, one per thread: fp64 sum of its 16 block partials in
+// block order) -> 32-wide xor butterflies -> 8 warp sums in order; the last
+// chunk CTA of the tensor sums the chunk sums in chunk order.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(FIN_THREADS) k_alpha(const DevTensor* T, const int32_t* cs,
-                                                       int ncs) {
-  const DevTensor& D = T[cs[blockIdx.x]];
+struct SelParams {
+  const DevTensor* T;
+  const int64_t* cbeg;  // [ncs + 1] chunk prefix
+  const int32_t* cidx;  // [ncs] tensor indices
+  int32_t ncs;
+};
+
+__global__ void __launch_bounds__(FIN_THREADS) k_alpha(const __grid_constant__ SelParams sp) {
   const int tid = threadIdx.x;
+  const int64_t chunk = blockIdx.x;
+  const int en = find_entry(sp.cbeg, sp.ncs, chunk);
+  const DevTensor& D = sp.T[sp.cidx[en]];
+  const int64_t c = chunk - sp.cbeg[en];
   const int64_t ntile = (D.nblk + TB - 1) / TB;
-  double amg = 0.0, agg = 0.0;
-  for (int64_t i = tid; i < ntile; i += FIN_THREADS) {
-    double tm = 0.0, tg = 0.0;
-    const int64_t bend = min(D.nblk, (i + 1) * TB);
-    for (int64_t b = i * TB; b < bend; ++b) {
+  const int64_t t = c * FIN_THREADS + tid;
+  double tm = 0.0, tg = 0.0;
+  if (t < ntile) {
+    const int64_t bend = min(D.nblk, (t + 1) * TB);
+    for (int64_t b = t * TB; b < bend; ++b) {
       tm += (double)D.part[b];
       tg += (double)D.part[D.bpad + b];
     }
-    amg += tm;
-    agg += tg;
   }
 #pragma unroll
   for (int off = 16; off >= 1; off >>= 1) {
-    amg = amg + __shfl_xor_sync(0xffffffffu, amg, off);
-    agg = agg + __shfl_xor_sync(0xffffffffu, agg, off);
+    tm = tm + __shfl_xor_sync(0xffffffffu, tm, off);
+    tg = tg + __shfl_xor_sync(0xffffffffu, tg, off);
   }
   __shared__ double wm[FIN_THREADS / 32], wg[FIN_THREADS / 32];
+  __shared__ int last;
   if ((tid & 31) == 0) {
-    wm[tid >> 5] = amg;
-    wg[tid >> 5] = agg;
+    wm[tid >> 5] = tm;
+    wg[tid >> 5] = tg;
   }
-  // zero the select histograms / counters of this tensor for this step
-  for (int i = tid; i < 3 * 2 * HBINS; i += FIN_THREADS) D.hist[i] = 0u;
-  if (tid < 16) D.sel[tid] = 0u;
   __syncthreads();
   if (tid == 0) {
-    double tm = wm[0], tg = wg[0];
+    double cm = wm[0], cg = wg[0];
     for (int w = 1; w < FIN_THREADS / 32; ++w) {
-      tm += wm[w];
-      tg += wg[w];
+      cm += wm[w];
+      cg += wg[w];
     }
-    float mg = (float)tm, gg = (float)tg;
+    D.chunk[c] = cm;
+    D.chunk[D.alpha_chunks + c] = cg;
+    __threadfence();
+    last = (atomicAdd(&D.sel[SEL_CNTA], 1u) == (uint32_t)D.alpha_chunks - 1u);
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  // zero the select histograms / round counters of this tensor for this step
+  for (int i = tid; i < 3 * 2 * HBINS; i += FIN_THREADS) D.hist[i] = 0u;
+  if (tid < 3) D.sel[SEL_CNT0 + tid] = 0u;
+  if (tid == 0) {
+    double am = 0.0, ag = 0.0;
+    for (int64_t k = 0; k < D.alpha_chunks; ++k) {
+      am += __ldcg(&D.chunk[k]);
+      ag += __ldcg(&D.chunk[D.alpha_chunks + k]);
+    }
+    const float mg = (float)am, gg = (float)ag;
     float a = (gg > 0.0f) ? __fdiv_rn(mg, gg) : 0.0f;
     if (D.flags & DF_ALPHA_INJ) a = *D.alpha_inj;
     D.alpha_new[0] = a;
     D.sel[SEL_RLO] = (uint32_t)D.k_lo;
     D.sel[SEL_RHI] = (uint32_t)D.k_hi;
+    D.sel[SEL_CNTA] = 0u;
   }
 }
 
 // ---------------------------------------------------------------------------
 // Pass 2: CoState encode (costate.py:419-425, :51-86, :213-258)
 // ---------------------------------------------------------------------------
-template <int PT>
-__device__ __forceinline__ void p2_block(const DevTensor& D, uint8_t* st, int nblk, int64_t b0) {
+template <int PT, bool FULL>
+__device__ __forceinline__ void p2_block(const DevTensor& D, const Sc& c, uint8_t* st, int nblk,
+                                         int64_t b0) {
   using L = P2L<PT>;
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int q = lane >> 3;
   const int j = lane & 7;
   const int bi = warp * 4 + q;
-  const bool active = bi < nblk;
+  const bool active = FULL || bi < nblk;
   const int64_t b = b0 + bi;
   const int64_t e0 = b * BS;
-  const int nv = active ? (int)min((int64_t)BS, D.n - e0) : 0;
-  const bool full = nv == BS;
+  const int nv = FULL ? BS : (active ? (int)min((int64_t)BS, D.n - e0) : 0);
+  const bool fullblk = FULL || nv == BS;
   const uint32_t gbase = lane & ~7u;
   const uint8_t* sg = st + L::OFF_G + bi * L::STR_G;
 
-  const bool has_state = D.flags & DF_M_HAS_STATE;
+  const bool has_state = c.flags & DF_M_HAS_STATE;
   float cs_scale = 0.0f, alpha_old = 0.0f;
   uint32_t sw[4] = {0, 0, 0, 0};
   if (has_state && active) {
-    uint8_t lab = st[L::OFF_LAB + bi];
-    float nrm = reinterpret_cast<const float*>(st + L::OFF_NRM)[bi];
-    uint16_t amp = reinterpret_cast<const uint16_t*>(st + L::OFF_AMP)[bi];
-    cs_scale = costate_scale(lab, nrm, amp, D.sqbs);
-    uint4 w = *reinterpret_cast<const uint4*>(st + L::OFF_SGN + bi * 16);
+    const uint8_t lab = st[L::OFF_LAB + bi];
+    const float nrm = reinterpret_cast<const float*>(st + L::OFF_NRM)[bi];
+    const uint16_t amp = reinterpret_cast<const uint16_t*>(st + L::OFF_AMP)[bi];
+    cs_scale = costate_scale(lab, nrm, amp, c.sqbs);
+    const uint4 w = *reinterpret_cast<const uint4*>(st + L::OFF_SGN + bi * 16);
     sw[0] = w.x; sw[1] = w.y; sw[2] = w.z; sw[3] = w.w;
     alpha_old = *D.alpha_state;
   }
-  const float alpha = D.alpha_new[0];
+  const float alpha = *D.alpha_new;
   float accd = 0.0f, accm = 0.0f;
   uint32_t myw = 0;
 #pragma unroll
   for (int k = 0; k < 16; ++k) {
     const int t = j + 8 * k;
-    const bool ve = t < nv;
+    const bool ve = FULL || t < nv;
     float g;
-    if (full) g = PT ? ta_bf16_to_f32(reinterpret_cast<const uint16_t*>(sg)[t])
-                     : reinterpret_cast<const float*>(sg)[t];
+    if (fullblk) g = PT ? ta_bf16_to_f32(reinterpret_cast<const uint16_t*>(sg)[t])
+                        : reinterpret_cast<const float*>(sg)[t];
     else g = ve ? to_f32<PT>(D.g, e0 + t) : 0.0f;
-    uint32_t bit = (sw[k >> 2] >> (8 * (k & 3) + 7 - j)) & 1u;
-    float m = costate_m(g, alpha_old, cs_scale, bit, has_state, D.b1, D.omb1);
-    float dl = ve ? __fsub_rn(m, __fmul_rn(alpha, g)) : 0.0f;  // costate.py:42
-    float mm = ve ? m : 0.0f;
+    const uint32_t bit = (sw[k >> 2] >> (8 * (k & 3) + 7 - j)) & 1u;
+    const float m = costate_m(g, alpha_old, cs_scale, bit, has_state, c.b1, c.omb1);
+    const float dl = ve ? __fsub_rn(m, __fmul_rn(alpha, g)) : 0.0f;  // costate.py:42
+    const float mm = ve ? m : 0.0f;
     accd = __fadd_rn(accd, __fmul_rn(dl, dl));
     accm = __fadd_rn(accm, __fmul_rn(mm, mm));
-    uint32_t w = __ballot_sync(0xffffffffu, dl < 0.0f);
-    if (lane == k) myw = w;
+    const uint32_t w = __ballot_sync(0xffffffffu, dl < 0.0f);
+    myw = (lane == k) ? w : myw;
+    if (!FULL && ve && (c.flags & DF_M_OUT)) D.m_out[e0 + t] = m;
   }
   // torch row-norm order: lane accumulators summed 0..7 in sequence
   float sd = __shfl_sync(0xffffffffu, accd, gbase);
@@ -585,15 +773,15 @@ __device__ __forceinline__ void p2_block(const DevTensor& D, uint8_t* st, int nb
   const float dn = __fsqrt_rn(sd);
   const float mnorm = __fsqrt_rn(sm);
   // sign bytes k = 2j, 2j+1 of this block (MSB = lane 0)
-  uint32_t w0 = __shfl_sync(0xffffffffu, myw, 2 * j);
-  uint32_t w1 = __shfl_sync(0xffffffffu, myw, 2 * j + 1);
+  const uint32_t w0 = __shfl_sync(0xffffffffu, myw, 2 * j);
+  const uint32_t w1 = __shfl_sync(0xffffffffu, myw, 2 * j + 1);
   if (active) {
-    uint32_t by0 = __brev((w0 >> (8 * q)) & 0xffu) >> 24;
-    uint32_t by1 = __brev((w1 >> (8 * q)) & 0xffu) >> 24;
+    const uint32_t by0 = __brev((w0 >> (8 * q)) & 0xffu) >> 24;
+    const uint32_t by1 = __brev((w1 >> (8 * q)) & 0xffu) >> 24;
     reinterpret_cast<uint16_t*>(st + L::OFF_SGN + bi * 16)[j] = (uint16_t)(by0 | (by1 << 8));
     if (j == 0) {
       reinterpret_cast<float*>(st + L::OFF_NRM)[bi] = dn;
-      reinterpret_cast<uint16_t*>(st + L::OFF_AMP)[bi] = ta_f32_to_f16(__fdiv_rn(dn, D.sqbs));
+      reinterpret_cast<uint16_t*>(st + L::OFF_AMP)[bi] = ta_f32_to_f16(__fdiv_rn(dn, c.sqbs));
       reinterpret_cast<float*>(st + L::OFF_RAT)[bi] =
           (mnorm == 0.0f) ? 0.0f : __fdiv_rn(dn, mnorm);
     }
@@ -601,7 +789,7 @@ __device__ __forceinline__ void p2_block(const DevTensor& D, uint8_t* st, int nb
 }
 
 template <int PT>
-__global__ void __launch_bounds__(NTHR) k_pass2(KParams kp) {
+__global__ void __launch_bounds__(NTHR) k_pass2(const __grid_constant__ KParams kp) {
   using L = P2L<PT>;
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* stages = smem;
@@ -620,7 +808,7 @@ __global__ void __launch_bounds__(NTHR) k_pass2(KParams kp) {
   __syncthreads();
 
   auto store = [&](uint8_t* st, const StageMeta& pm) {
-    const DevTensor& D = kp.T[pm.t];
+    const DevTensor& D = pm.D;
     bulk_s2g(D.sgn + pm.b0 * 16, st + L::OFF_SGN, TB * 16);
     bulk_s2g(D.nrm + pm.b0, st + L::OFF_NRM, TB * 4);
     bulk_s2g(D.amp + pm.b0, st + L::OFF_AMP, TB * 2);
@@ -646,6 +834,7 @@ __global__ void __launch_bounds__(NTHR) k_pass2(KParams kp) {
         const DevTensor& D = kp.T[t];
         const int64_t b0 = (tile - kp.lbeg[en]) * TB;
         const int nblk = (int)min((int64_t)TB, D.nblk - b0);
+        meta[s].D = D;
         meta[s].t = t;
         meta[s].nblk = nblk;
         meta[s].b0 = b0;
@@ -678,8 +867,8 @@ __global__ void __launch_bounds__(NTHR) k_pass2(KParams kp) {
         }
       }
       if (!ok)
-        for (int r = first; r < it; ++r) wait_bar(&full[r % NSTAGE], (uint32_t)(r / NSTAGE) & 1u,
-                                                  kp.status);
+        for (int r = first; r < it; ++r)
+          wait_bar(&full[r % NSTAGE], (uint32_t)(r / NSTAGE) & 1u, kp.status);
       bulk_wait_all();
     }
     return;
@@ -689,8 +878,17 @@ __global__ void __launch_bounds__(NTHR) k_pass2(KParams kp) {
     const int s = it % NSTAGE;
     const uint32_t ph = (uint32_t)(it / NSTAGE) & 1u;
     if (!wait_bar(&full[s], ph, kp.status)) break;
-    const StageMeta pm = meta[s];
-    p2_block<PT>(kp.T[pm.t], stages + s * L::STAGE, pm.nblk, pm.b0);
+    const StageMeta& pm = meta[s];
+    const DevTensor& D = pm.D;
+    const Sc c = load_sc(D);
+    const int nblk = pm.nblk;
+    const int64_t b0 = pm.b0;
+    uint8_t* st = stages + s * L::STAGE;
+    const int bi = warp * 4 + (lane >> 3);
+    const bool mine_full = bi < nblk && D.n - (b0 + bi) * BS >= BS;
+    const bool fast = __all_sync(0xffffffffu, mine_full) && !(c.flags & DF_M_OUT);
+    if (fast) p2_block<PT, true>(D, c, st, nblk, b0);
+    else p2_block<PT, false>(D, c, st, nblk, b0);
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) mbar_arrive(&done[s]);
@@ -707,13 +905,6 @@ constexpr size_t p2_smem_bytes() {
 // on the fp32 bit pattern (non-negative floats order like their bits).
 // Round r: 0 -> bits[31:21], 1 -> bits[20:10], 2 -> bits[9:0].
 // ---------------------------------------------------------------------------
-struct SelParams {
-  const DevTensor* T;
-  const int64_t* cbeg;  // [ncs + 1] chunk prefix
-  const int32_t* cidx;  // [ncs] tensor indices
-  int32_t ncs;
-};
-
 __device__ __forceinline__ void scan_pick(const uint32_t* h, int nbins, uint32_t rank,
                                           uint32_t* bin_out, uint32_t* rank_out,
                                           uint32_t* sh) {
@@ -728,9 +919,8 @@ __device__ __forceinline__ void scan_pick(const uint32_t* h, int nbins, uint32_t
   }
   sh[tid] = s;
   __syncthreads();
-  // inclusive scan in smem (Hillis-Steele)
-  for (int off = 1; off < SEL_THREADS; off <<= 1) {
-    uint32_t v = (tid >= off) ? sh[tid - off] : 0u;
+  for (int off = 1; off < SEL_THREADS; off <<= 1) {  // inclusive scan (Hillis-Steele)
+    const uint32_t v = (tid >= off) ? sh[tid - off] : 0u;
     __syncthreads();
     sh[tid] += v;
     __syncthreads();
@@ -738,21 +928,21 @@ __device__ __forceinline__ void scan_pick(const uint32_t* h, int nbins, uint32_t
   const uint32_t incl = sh[tid];
   const uint32_t excl = incl - s;
   if (rank >= excl && rank < incl) {
-    uint32_t c = excl;
+    uint32_t cum = excl;
     for (int i = 0; i < per; ++i) {
-      if (rank < c + loc[i]) {
+      if (rank < cum + loc[i]) {
         *bin_out = (uint32_t)(tid * per + i);
-        *rank_out = rank - c;
+        *rank_out = rank - cum;
         break;
       }
-      c += loc[i];
+      cum += loc[i];
     }
   }
   __syncthreads();
 }
 
 template <int R>
-__global__ void __launch_bounds__(SEL_THREADS) k_select(SelParams sp) {
+__global__ void __launch_bounds__(SEL_THREADS) k_select(const __grid_constant__ SelParams sp) {
   __shared__ uint32_t h[2][HBINS];
   __shared__ uint32_t sh[SEL_THREADS];
   __shared__ int last;
@@ -824,7 +1014,7 @@ __global__ void __launch_bounds__(SEL_THREADS) k_select(SelParams sp) {
 }
 
 // labels (costate.py:126-149) and commit alpha (costate.py:443-456)
-__global__ void __launch_bounds__(SEL_THREADS) k_labels(SelParams sp) {
+__global__ void __launch_bounds__(SEL_THREADS) k_labels(const __grid_constant__ SelParams sp) {
   const int64_t chunk = blockIdx.x;
   const int en = find_entry(sp.cbeg, sp.ncs, chunk);
   const DevTensor& D = sp.T[sp.cidx[en]];
