@@ -15,7 +15,8 @@ constexpr int TB = 16;              // blocks per work tile
 constexpr int TE = BS * TB;         // elements per work tile
 constexpr int NCW = 4;              // consumer warps per CTA (4 blocks each)
 constexpr int NTHR = (NCW + 1) * 32;// + one producer warp
-constexpr int NSTAGE = 2;           // smem pipeline depth (more CTAs per SM instead)
+constexpr int NSTAGE = 2;           // pass-1 smem pipeline depth (more CTAs per SM instead)
+constexpr int NSTAGE2 = 4;          // pass-2 depth (small stages, little compute per tile)
 constexpr uint32_t WAIT_LIMIT = 1u << 27;  // bounded mbarrier polling
 
 constexpr int FIN_THREADS = 256;    // alpha chunk CTA (tiles per chunk)

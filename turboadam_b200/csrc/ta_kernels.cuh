@@ -89,16 +89,44 @@ struct P2L {
   static constexpr int STAGE = (END + 127) / 128 * 128;
 };
 
-// Per-stage metadata written by the producer before it arms the barrier: the
-// tensor's descriptor (so consumers read it from smem, not global memory).
+__device__ __forceinline__ int find_entry(const int64_t* lbeg, int nl, int64_t tile) {
+  int lo = 0, hi = nl - 1;
+  while (lo < hi) {
+    int mid = (lo + hi + 1) >> 1;
+    if (lbeg[mid] <= tile) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
+}
+
+// Per-stage metadata written by the producer before it arms the barrier.
+// Consumers read the tensor's descriptor from global memory (L1-cached) once
+// per tile, and the per-tensor scalars into registers.
 struct __align__(16) StageMeta {
-  DevTensor D;
-  int32_t t;     // tensor index
-  int32_t nblk;  // blocks of this tile
-  int64_t b0;    // first block (within tensor)
+  int32_t t;        // tensor index
+  int32_t nblk;     // blocks of this tile
+  int64_t b0;       // first block (within tensor)
+  float alpha_old;  // CoState alpha of the previous step (state)
+  float alpha_new;  // this step's alpha (pass 2)
+};
+
+// Incremental tile -> launch-list entry walk of a producer: tiles of one CTA
+// increase, so the entry only moves forward (one load per tensor change).
+struct EntryWalk {
+  int en = -1;
+  int64_t next = 0;  // first tile of entry en + 1
+  __device__ __forceinline__ int at(const int64_t* lbeg, int nl, int64_t tile) {
+    if (en < 0 || tile >= next) {
+      en = (en < 0) ? find_entry(lbeg, nl, tile) : en;
+      while (en + 1 < nl && lbeg[en + 1] <= tile) ++en;
+      next = (en + 1 < nl) ? lbeg[en + 1] : INT64_MAX;
+    }
+    return en;
+  }
 };
 
 constexpr int TABLE_STRIDE = 65;  // per-group exp table (<= 64 entries), padded
+constexpr int SCR_FLOATS = 16 * 32;  // per-warp scratch: ln v_new of 16 elements x 32 lanes
 
 struct KParams {
   const DevTensor* T;
@@ -109,16 +137,6 @@ struct KParams {
   uint32_t* status;
   uint32_t rk0[10], rk1[10];  // Philox round keys (seed words + r * Weyl constants)
 };
-
-__device__ __forceinline__ int find_entry(const int64_t* lbeg, int nl, int64_t tile) {
-  int lo = 0, hi = nl - 1;
-  while (lo < hi) {
-    int mid = (lo + hi + 1) >> 1;
-    if (lbeg[mid] <= tile) lo = mid;
-    else hi = mid - 1;
-  }
-  return lo;
-}
 
 // Philox4x32-10 with precomputed round keys (identical to ta_philox4x32_10).
 __device__ __forceinline__ void philox_rk(uint32_t c0, uint32_t c1, uint32_t c2, uint32_t c3,
@@ -188,6 +206,37 @@ __device__ __forceinline__ float log_bf(float x) {
   r = (x == 0.0f) ? -INFINITY : r;
   r = (x < 0.0f || x != x) ? __uint_as_float(0x7fc00000u) : r;
   return r;
+}
+
+// ta_logf(clamp_min(v, 1e-38)) (quantize.py:275) for every v: the clamped
+// argument is >= 1e-38 (possibly subnormal), +inf or NaN, so only the
+// subnormal scaling and the non-finite passthrough need selects.
+__device__ __forceinline__ float log_clamped(float v) {
+  const float x = (v < 1e-38f) ? 1e-38f : v;
+  const bool sub = x < 0x1p-126f;
+  const float xs = __fmul_rn(x, sub ? 0x1p23f : 1.0f);
+  const uint32_t ix = __float_as_uint(xs);
+  const int32_t e = ((int32_t)(ix - 0x3f2aaaabu)) >> 23;
+  const float m = __uint_as_float(ix - ((uint32_t)e << 23));
+  const float f = __fsub_rn(m, 1.0f);
+  const float ef = (float)(e + (sub ? -23 : 0));
+  float q = TA_LOG_Q0;
+  q = __fmaf_rn(q, f, TA_LOG_Q1);
+  q = __fmaf_rn(q, f, TA_LOG_Q2);
+  q = __fmaf_rn(q, f, TA_LOG_Q3);
+  q = __fmaf_rn(q, f, TA_LOG_Q4);
+  q = __fmaf_rn(q, f, TA_LOG_Q5);
+  q = __fmaf_rn(q, f, TA_LOG_Q6);
+  q = __fmaf_rn(q, f, TA_LOG_Q7);
+  q = __fmaf_rn(q, f, TA_LOG_Q8);
+  q = __fmaf_rn(q, f, TA_LOG_Q9);
+  const float f2 = __fmul_rn(f, f);
+  const float hi = __fmul_rn(ef, TA_LN2_HI);
+  const float s = __fadd_rn(hi, f);
+  const float err = __fadd_rn(__fsub_rn(hi, s), f);
+  const float lo = __fmaf_rn(f2, q, __fmaf_rn(ef, TA_LN2_LO, err));
+  const float r = __fadd_rn(s, lo);
+  return (__float_as_uint(x) >= 0x7f800000u) ? x : r;  // +inf -> +inf, NaN -> NaN
 }
 
 // ---------------------------------------------------------------------------
@@ -305,7 +354,7 @@ __device__ __noinline__ float p1_fix_elem(const DevTensor& D, const Sc& c, uint8
     const float qv = __fdiv_rn(__fadd_rn((float)id, 0.5f), c.nbf);
     const float vo = ta_expf(__fadd_rn(lmin, __fmul_rn(qv, span)));
     vn = __fmaf_rn(__fmul_rn(g, g), c.omb2, __fmul_rn(vo, c.b2));
-    lv = log_bf(clamp_min(vn, 1e-38f));
+    lv = log_clamped(vn);
   } else if (VK == VK_FP32) {
     vn = reinterpret_cast<const float*>(st + L::OFF_EAS + bi * L::STR_4)[t];
   }
@@ -317,13 +366,19 @@ __device__ __noinline__ float p1_fix_elem(const DevTensor& D, const Sc& c, uint8
   return lv;
 }
 
-// One 128-element block per 8-lane group. FULL: every group of the warp has a
-// full block (no bounds checks, user arrays from smem); otherwise the general
-// path with per-element bounds and global loads for the ragged tail block.
+// One 128-element block per 8-lane group; lane j owns elements j + 8k, k in
+// 0..15, visited as 4 quads (kq) of 4. FULL: every group of the warp has a
+// full block (user arrays staged in smem, no bounds checks); otherwise the
+// general path: per-element bounds, global loads/stores for the ragged tail
+// block, and exact IEEE divisions there. ln v_new goes through a per-lane
+// smem scratch (scr[k*32 + lane]) between phase A and phase B.
 template <int MK, int VK, int PT, bool UNI, bool TABLE, bool FULL>
-__device__ __forceinline__ void p1_block(const DevTensor& D, const Sc& c, uint8_t* st, int nblk,
-                                         int64_t b0, float* table, const KParams& kp) {
+__device__ __forceinline__ void p1_block(const DevTensor& D, const StageMeta& M, const Sc& c,
+                                         uint8_t* st, float* table, float* scr,
+                                         const KParams& kp) {
   using L = P1L<MK, VK, PT, UNI>;
+  const int nblk = M.nblk;
+  const int64_t b0 = M.b0;
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int q = lane >> 3;
@@ -338,19 +393,18 @@ __device__ __forceinline__ void p1_block(const DevTensor& D, const Sc& c, uint8_
 
   uint8_t* sp = st + L::OFF_P + bi * L::STR_P;
   const uint8_t* sg = st + L::OFF_G + bi * L::STR_P;
+  const uint8_t* sidx = st + L::OFF_IDX + bi * L::STR_1;
+  const uint32_t* sgnw = reinterpret_cast<const uint32_t*>(st + L::OFF_SGN + bi * 16);
 
   // ---- per-block CoState decode scalars (costate.py:290-314)
-  float cs_scale = 0.0f, alpha_old = 0.0f;
-  uint32_t sw[4] = {0, 0, 0, 0};
+  float cs_scale = 0.0f;
+  const float alpha_old = M.alpha_old;
   const bool has_state = (MK == MK_COSTATE) && (c.flags & DF_M_HAS_STATE);
   if (MK == MK_COSTATE && has_state && active) {
     const uint8_t lab = st[L::OFF_LAB + bi];
     const float nrm = reinterpret_cast<const float*>(st + L::OFF_NRM)[bi];
     const uint16_t amp = reinterpret_cast<const uint16_t*>(st + L::OFF_AMP)[bi];
     cs_scale = costate_scale(lab, nrm, amp, c.sqbs);
-    const uint4 w = *reinterpret_cast<const uint4*>(st + L::OFF_SGN + bi * 16);
-    sw[0] = w.x; sw[1] = w.y; sw[2] = w.z; sw[3] = w.w;
-    alpha_old = *D.alpha_state;
   }
 
   // ---- per-block 1Q decode scalars (quantize.py:252-256) and exp table
@@ -373,100 +427,111 @@ __device__ __forceinline__ void p1_block(const DevTensor& D, const Sc& c, uint8_
   }
 
   // ---- phase A: m, v, ln v, and the parameter update, per element
-  float lk[16];
   float mg = 0.0f, gg = 0.0f, gbad = 0.0f;
   float vmin = INFINITY, vmax = -INFINITY;
-  bool sub = false, badidx = false;
+  bool sub = false;
+  uint32_t idor = 0;
+#pragma unroll 1
+  for (int kq = 0; kq < 4; ++kq) {
+    const uint32_t sw = (MK == MK_COSTATE && has_state && active) ? sgnw[kq] : 0u;
 #pragma unroll
-  for (int k = 0; k < 16; ++k) {
-    const int t = j + 8 * k;
-    const int64_t e = e0 + t;
-    const bool ve = FULL || t < nv;
-    float g;
-    if (FULL) g = PT ? ta_bf16_to_f32(reinterpret_cast<const uint16_t*>(sg)[t])
-                     : reinterpret_cast<const float*>(sg)[t];
-    else if (fullblk) g = PT ? ta_bf16_to_f32(reinterpret_cast<const uint16_t*>(sg)[t])
-                             : reinterpret_cast<const float*>(sg)[t];
-    else g = ve ? to_f32<PT>(D.g, e) : 0.0f;
-    gbad = __fmaf_rn(g, 0.0f, gbad);
-    float m = 0.0f;
-    if (MK == MK_COSTATE) {
-      const uint32_t bit = (sw[k >> 2] >> (8 * (k & 3) + 7 - j)) & 1u;
-      m = costate_m(g, alpha_old, cs_scale, bit, has_state, c.b1, c.omb1);
-      if (ve) {
-        mg = __fmaf_rn(m, g, mg);
-        gg = __fmaf_rn(g, g, gg);
+    for (int i = 0; i < 4; ++i) {
+      const int k = 4 * kq + i;
+      const int t = j + 8 * k;
+      const int64_t e = e0 + t;
+      const bool ve = FULL || t < nv;
+      float g;
+      if (fullblk) g = PT ? ta_bf16_to_f32(reinterpret_cast<const uint16_t*>(sg)[t])
+                          : reinterpret_cast<const float*>(sg)[t];
+      else g = ve ? to_f32<PT>(D.g, e) : 0.0f;
+      gbad = __fmaf_rn(g, 0.0f, gbad);
+      float m = 0.0f;
+      if (MK == MK_COSTATE) {
+        const uint32_t bit = (sw >> (8 * i + 7 - j)) & 1u;
+        m = costate_m(g, alpha_old, cs_scale, bit, has_state, c.b1, c.omb1);
+        if (ve) {
+          mg = __fmaf_rn(m, g, mg);
+          gg = __fmaf_rn(g, g, gg);
+        }
+      } else if (MK == MK_FP32) {
+        float* sea = reinterpret_cast<float*>(st + L::OFF_EA + bi * L::STR_4);
+        const float ea = fullblk ? sea[t] : (ve ? D.ea[e] : 0.0f);
+        m = __fmaf_rn(g, c.omb1, __fmul_rn(ea, c.b1));  // optimizer.py:113
+        if (fullblk) sea[t] = m;
+        else if (ve) D.ea[e] = m;
       }
-    } else if (MK == MK_FP32) {
-      float* sea = reinterpret_cast<float*>(st + L::OFF_EA + bi * L::STR_4);
-      const float ea = fullblk ? sea[t] : (ve ? D.ea[e] : 0.0f);
-      m = __fmaf_rn(g, c.omb1, __fmul_rn(ea, c.b1));  // optimizer.py:113
-      if (fullblk) sea[t] = m;
-      else if (ve) D.ea[e] = m;
+      float vn = 0.0f;
+      if (VK == VK_ONEQ) {
+        const uint32_t id = active ? sidx[t] : 0u;
+        float vo;
+        if (TABLE && fullblk) {
+          idor |= id;
+          vo = tab[id & (uint32_t)(nb - 1)];
+        } else {
+          const float qv = __fdiv_rn(__fadd_rn((float)id, 0.5f), c.nbf);
+          vo = ta_expf(__fadd_rn(lmin, __fmul_rn(qv, span)));
+        }
+        const float g2 = ve ? __fmul_rn(g, g) : 0.0f;
+        vn = __fmaf_rn(g2, c.omb2, __fmul_rn(vo, c.b2));  // quantize.py:270
+        const float lv = log_clamped(vn);                  // quantize.py:275
+        scr[k * 32 + lane] = lv;
+        if (ve) {  // fminf/fmaxf skip a NaN operand, like the compare-select
+          vmin = fminf(lv, vmin);
+          vmax = fmaxf(lv, vmax);
+        }
+      } else if (VK == VK_FP32) {
+        float* sea = reinterpret_cast<float*>(st + L::OFF_EAS + bi * L::STR_4);
+        const float vs = fullblk ? sea[t] : (ve ? D.eas[e] : 0.0f);
+        vn = __fmaf_rn(__fmul_rn(c.omb2, g), g, __fmul_rn(vs, c.b2));  // optimizer.py:166
+        if (fullblk) sea[t] = vn;
+        else if (ve) D.eas[e] = vn;
+        sub = sub || (vn < 0x1p-126f && vn > 0.0f);
+      }
+      if (param && ve) {
+        float pv;
+        if (fullblk) pv = PT ? ta_bf16_to_f32(reinterpret_cast<const uint16_t*>(sp)[t])
+                             : reinterpret_cast<const float*>(sp)[t];
+        else pv = to_f32<PT>(D.p, e);
+        bool dummy = false;
+        pv = fullblk ? adam_elem<PT>(pv, m, vn, c, &dummy) : adam_elem_ieee<PT>(pv, m, vn, c);
+        if (PT) {
+          const uint16_t h = ta_f32_to_bf16(pv);
+          if (fullblk) reinterpret_cast<uint16_t*>(sp)[t] = h;
+          else reinterpret_cast<uint16_t*>(D.p)[e] = h;
+        } else {
+          if (fullblk) reinterpret_cast<float*>(sp)[t] = pv;
+          else reinterpret_cast<float*>(D.p)[e] = pv;
+        }
+      }
+      if (!FULL && ve && (c.flags & DF_M_OUT)) D.m_out[e] = m;
+      if (!FULL && ve && (c.flags & DF_V_OUT)) D.v_out[e] = vn;
     }
-    float vn = 0.0f;
-    if (VK == VK_ONEQ) {
-      const int id = active ? st[L::OFF_IDX + bi * L::STR_1 + t] : 0;
-      float vo;
-      if (TABLE && fullblk) {
-        badidx = badidx || (id >= nb);
-        vo = tab[min(id, nb - 1)];
-      } else {
-        const float qv = __fdiv_rn(__fadd_rn((float)id, 0.5f), c.nbf);
-        vo = ta_expf(__fadd_rn(lmin, __fmul_rn(qv, span)));
-      }
-      const float g2 = ve ? __fmul_rn(g, g) : 0.0f;
-      vn = __fmaf_rn(g2, c.omb2, __fmul_rn(vo, c.b2));  // quantize.py:270
-      const float lv = log_bf(clamp_min(vn, 1e-38f));   // quantize.py:275
-      lk[k] = lv;
-      if (ve) {
-        vmin = (lv < vmin) ? lv : vmin;
-        vmax = (lv > vmax) ? lv : vmax;
-      }
-    } else if (VK == VK_FP32) {
-      float* sea = reinterpret_cast<float*>(st + L::OFF_EAS + bi * L::STR_4);
-      const float vs = fullblk ? sea[t] : (ve ? D.eas[e] : 0.0f);
-      vn = __fmaf_rn(__fmul_rn(c.omb2, g), g, __fmul_rn(vs, c.b2));  // optimizer.py:166
-      if (fullblk) sea[t] = vn;
-      else if (ve) D.eas[e] = vn;
-    }
-    if (param && ve) {
-      float pv;
-      if (fullblk) pv = PT ? ta_bf16_to_f32(reinterpret_cast<const uint16_t*>(sp)[t])
-                           : reinterpret_cast<const float*>(sp)[t];
-      else pv = to_f32<PT>(D.p, e);
-      pv = fullblk ? adam_elem<PT>(pv, m, vn, c, &sub) : adam_elem_ieee<PT>(pv, m, vn, c);
-      if (PT) {
-        const uint16_t h = ta_f32_to_bf16(pv);
-        if (fullblk) reinterpret_cast<uint16_t*>(sp)[t] = h;
-        else reinterpret_cast<uint16_t*>(D.p)[e] = h;
-      } else {
-        if (fullblk) reinterpret_cast<float*>(sp)[t] = pv;
-        else reinterpret_cast<float*>(D.p)[e] = pv;
-      }
-    }
-    if (!FULL && ve && (c.flags & DF_M_OUT)) D.m_out[e] = m;
-    if (!FULL && ve && (c.flags & DF_V_OUT)) D.v_out[e] = vn;
   }
   if (gbad != gbad) atomicOr(kp.status, 1u);
 
-  // ---- rare exact fallbacks (full blocks only; tail blocks were exact above)
-  if (sub || badidx) {
-#pragma unroll
+  // ---- rare exact fallbacks, full blocks only (tail blocks were exact above):
+  // some v_new < 2^-126 (ln v_new < -87.3365) needs v/bc2 by IEEE division, or
+  // a stored index >= 2^nbits missed the exp table.
+  if (VK == VK_ONEQ) sub = vmin < -87.33f;
+  const bool fix = fullblk && active && (sub || (TABLE && VK == VK_ONEQ && idor >= (uint32_t)nb));
+  if (fix) {
+#pragma unroll 1
     for (int k = 0; k < 16; ++k) {
-      const uint32_t bit = (sw[k >> 2] >> (8 * (k & 3) + 7 - j)) & 1u;
+      const uint32_t sw = (MK == MK_COSTATE && has_state) ? sgnw[k >> 2] : 0u;
+      const uint32_t bit = (sw >> (8 * (k & 3) + 7 - j)) & 1u;
       const float lv = p1_fix_elem<MK, VK, PT, UNI>(D, c, st, bi, j + 8 * k, e0 + j + 8 * k,
                                                      alpha_old, cs_scale, bit, has_state, lmin,
                                                      span);
-      if (VK == VK_ONEQ) lk[k] = lv;
+      if (VK == VK_ONEQ) scr[k * 32 + lane] = lv;
     }
     if (VK == VK_ONEQ) {  // block extrema from the recomputed logs
       vmin = INFINITY;
       vmax = -INFINITY;
-#pragma unroll
+#pragma unroll 1
       for (int k = 0; k < 16; ++k) {
-        vmin = (lk[k] < vmin) ? lk[k] : vmin;
-        vmax = (lk[k] > vmax) ? lk[k] : vmax;
+        const float lv = scr[k * 32 + lane];
+        vmin = fminf(lv, vmin);
+        vmax = fmaxf(lv, vmax);
       }
     }
   }
@@ -488,10 +553,8 @@ __device__ __forceinline__ void p1_block(const DevTensor& D, const Sc& c, uint8_
   if (VK == VK_ONEQ) {
 #pragma unroll
     for (int off = 4; off >= 1; off >>= 1) {
-      const float o1 = __shfl_xor_sync(0xffffffffu, vmin, off);
-      const float o2 = __shfl_xor_sync(0xffffffffu, vmax, off);
-      vmin = (o1 < vmin) ? o1 : vmin;
-      vmax = (o2 > vmax) ? o2 : vmax;
+      vmin = fminf(vmin, __shfl_xor_sync(0xffffffffu, vmin, off));
+      vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, off));
     }
     if (active && j == 0) {
       uint16_t* hdr = reinterpret_cast<uint16_t*>(st + L::OFF_HDR);
@@ -504,32 +567,41 @@ __device__ __forceinline__ void p1_block(const DevTensor& D, const Sc& c, uint8_
     const float rspan = __frcp_rn(nspan);
     const float top = c.nbf - 1.0f;
     const float* suni = reinterpret_cast<const float*>(st + L::OFF_UNI + bi * L::STR_4);
-    uint8_t* sidx = st + L::OFF_IDX + bi * L::STR_1;
-    uint32_t rnd[4] = {0, 0, 0, 0};
-#pragma unroll
-    for (int k = 0; k < 16; ++k) {
-      const int t = j + 8 * k;
-      float u;
-      if (UNI) {
-        u = suni[t];
-      } else {
-        if ((k & 3) == 0) {
-          uint32_t c0, c1, c2, c3;
-          ta_sr_counter((uint64_t)b, (uint32_t)j, (uint32_t)(k >> 2), c.tid, c.step, &c0, &c1,
-                        &c2, &c3);
-          philox_rk(c0, c1, c2, c3, kp.rk0, kp.rk1, rnd);
-        }
-        u = ta_u01(rnd[k & 3]);
+    uint8_t* sidx_w = st + L::OFF_IDX + bi * L::STR_1;
+#pragma unroll 1
+    for (int kq = 0; kq < 4; ++kq) {
+      uint32_t rnd[4] = {0, 0, 0, 0};
+      if (!UNI) {
+        uint32_t c0, c1, c2, c3;
+        ta_sr_counter((uint64_t)b, (uint32_t)j, (uint32_t)kq, c.tid, c.step, &c0, &c1, &c2,
+                      &c3);
+        philox_rk(c0, c1, c2, c3, kp.rk0, kp.rk1, rnd);
       }
-      const float cc = __fmul_rn(div_by(__fsub_rn(lk[k], vmin), nspan, rspan), c.nbf);
-      const float fl = floorf(cc);
-      const float fr = __fsub_rn(cc, fl);
-      float r = __fadd_rn(fl, (u < fr) ? 1.0f : 0.0f);
-      r = (r < 0.0f) ? 0.0f : r;
-      r = (r > top) ? top : r;
-      if (active) sidx[t] = (uint8_t)r;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int k = 4 * kq + i;
+        const int t = j + 8 * k;
+        const float u = UNI ? suni[t] : ta_u01(rnd[i]);
+        const float cc = __fmul_rn(div_by(__fsub_rn(scr[k * 32 + lane], vmin), nspan, rspan),
+                                   c.nbf);
+        const float fl = floorf(cc);
+        const float fr = __fsub_rn(cc, fl);
+        float r = __fadd_rn(fl, (u < fr) ? 1.0f : 0.0f);
+        if (!FULL) r = (r < 0.0f) ? 0.0f : r;  // valid elements have L >= min: r >= 0
+        r = (r > top) ? top : r;
+        if (active) sidx_w[t] = (uint8_t)r;
+      }
     }
   }
+}
+
+// The general (tail) path lives out of line so the hot loop's code stays small.
+template <int MK, int VK, int PT, bool UNI, bool TABLE>
+__device__ __noinline__ void p1_block_general(const StageMeta& M, uint8_t* st, float* table,
+                                              float* scr, const KParams& kp) {
+  const DevTensor& D = kp.T[M.t];
+  const Sc c = load_sc(D);
+  p1_block<MK, VK, PT, UNI, TABLE, false>(D, M, c, st, table, scr, kp);
 }
 
 template <int MK, int VK, int PT, bool UNI, bool TABLE>
@@ -557,6 +629,9 @@ __global__ void __launch_bounds__(NTHR, 4) k_pass1(const __grid_constant__ KPara
     if (lane == 0) {
       int it = 0;
       bool ok = true;
+      EntryWalk walk;
+      int cur_t = -1;
+      float cur_alpha = 0.0f;
       for (int64_t tile = blockIdx.x; tile < kp.total; tile += gridDim.x, ++it) {
         const int s = it % NSTAGE;
         const uint32_t ph = (uint32_t)(it / NSTAGE) & 1u;
@@ -564,20 +639,24 @@ __global__ void __launch_bounds__(NTHR, 4) k_pass1(const __grid_constant__ KPara
         if (it >= NSTAGE) {
           if (!wait_bar(&done[s], ph ^ 1u, kp.status)) { ok = false; break; }
           const StageMeta& pm = meta[s];
-          p1_store<MK, VK, PT, UNI>(pm.D, st, pm.nblk, pm.b0);
+          p1_store<MK, VK, PT, UNI>(kp.T[pm.t], st, pm.nblk, pm.b0);
           bulk_commit();
           bulk_wait_read_all();
         }
-        const int en = find_entry(kp.lbeg, kp.nl, tile);
+        const int en = walk.at(kp.lbeg, kp.nl, tile);
         const int t = kp.lidx[en];
         const DevTensor& D = kp.T[t];
+        if (t != cur_t) {  // per-tensor values, loaded once per tensor change
+          cur_t = t;
+          cur_alpha = (MK == MK_COSTATE && (D.flags & DF_M_HAS_STATE)) ? *D.alpha_state : 0.0f;
+        }
         const int64_t lt = tile - kp.lbeg[en];
         const int64_t b0 = lt * TB;
         const int nblk = (int)min((int64_t)TB, D.nblk - b0);
-        meta[s].D = D;
         meta[s].t = t;
         meta[s].nblk = nblk;
         meta[s].b0 = b0;
+        meta[s].alpha_old = cur_alpha;
         uint32_t bytes;
         p1_issue<MK, VK, PT, UNI>(D, st, nblk, b0, &full[s], true, bytes);
         mbar_arrive_expect_tx(&full[s], bytes);
@@ -589,7 +668,7 @@ __global__ void __launch_bounds__(NTHR, 4) k_pass1(const __grid_constant__ KPara
           const int s = r % NSTAGE;
           if (!wait_bar(&done[s], (uint32_t)(r / NSTAGE) & 1u, kp.status)) { ok = false; break; }
           const StageMeta& pm = meta[s];
-          p1_store<MK, VK, PT, UNI>(pm.D, stages + s * L::STAGE, pm.nblk, pm.b0);
+          p1_store<MK, VK, PT, UNI>(kp.T[pm.t], stages + s * L::STAGE, pm.nblk, pm.b0);
           bulk_commit();
         }
       }
@@ -602,27 +681,27 @@ __global__ void __launch_bounds__(NTHR, 4) k_pass1(const __grid_constant__ KPara
   }
 
   float* table = tables + warp * 4 * TABLE_STRIDE;
+  float* scr = tables + NCW * 4 * TABLE_STRIDE + warp * SCR_FLOATS;
   int it = 0;
   for (int64_t tile = blockIdx.x; tile < kp.total; tile += gridDim.x, ++it) {
     const int s = it % NSTAGE;
     const uint32_t ph = (uint32_t)(it / NSTAGE) & 1u;
     if (!wait_bar(&full[s], ph, kp.status)) break;
     const StageMeta& pm = meta[s];
-    const DevTensor& D = pm.D;
-    const Sc c = load_sc(D);
-    const int nblk = pm.nblk;
-    const int64_t b0 = pm.b0;
+    const DevTensor& D = kp.T[pm.t];
     uint8_t* st = stages + s * L::STAGE;
     // the fast path needs all 4 blocks of this warp present and full, and no
     // seam outputs; decided per warp so the shuffles stay convergent
     const int bi = warp * 4 + (lane >> 3);
-    const bool mine_full = bi < nblk && D.n - (b0 + bi) * BS >= BS;
+    const bool mine_full = bi < pm.nblk && D.n - (pm.b0 + bi) * BS >= BS;
     const bool fast = __all_sync(0xffffffffu, mine_full) &&
-                      !(c.flags & (DF_M_OUT | DF_V_OUT));
-    if (fast)
-      p1_block<MK, VK, PT, UNI, TABLE, true>(D, c, st, nblk, b0, table, kp);
-    else
-      p1_block<MK, VK, PT, UNI, TABLE, false>(D, c, st, nblk, b0, table, kp);
+                      !(D.flags & (DF_M_OUT | DF_V_OUT));
+    if (fast) {
+      const Sc c = load_sc(D);
+      p1_block<MK, VK, PT, UNI, TABLE, true>(D, pm, c, st, table, scr, kp);
+    } else {
+      p1_block_general<MK, VK, PT, UNI, TABLE>(pm, st, table, scr, kp);
+    }
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) mbar_arrive(&done[s]);
@@ -632,7 +711,7 @@ __global__ void __launch_bounds__(NTHR, 4) k_pass1(const __grid_constant__ KPara
 template <int MK, int VK, int PT, bool UNI>
 constexpr size_t p1_smem_bytes() {
   return (size_t)NSTAGE * P1L<MK, VK, PT, UNI>::STAGE + 2 * NSTAGE * 8 +
-         NSTAGE * sizeof(StageMeta) + NCW * 4 * TABLE_STRIDE * 4;
+         NSTAGE * sizeof(StageMeta) + NCW * 4 * TABLE_STRIDE * 4 + NCW * SCR_FLOATS * 4;
 }
 
 // ---------------------------------------------------------------------------
@@ -713,9 +792,11 @@ __global__ void __launch_bounds__(FIN_THREADS) k_alpha(const __grid_constant__ S
 // Pass 2: CoState encode (costate.py:419-425, :51-86, :213-258)
 // ---------------------------------------------------------------------------
 template <int PT, bool FULL>
-__device__ __forceinline__ void p2_block(const DevTensor& D, const Sc& c, uint8_t* st, int nblk,
-                                         int64_t b0) {
+__device__ __forceinline__ void p2_block(const DevTensor& D, const StageMeta& M, const Sc& c,
+                                         uint8_t* st) {
   using L = P2L<PT>;
+  const int nblk = M.nblk;
+  const int64_t b0 = M.b0;
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int q = lane >> 3;
@@ -728,39 +809,42 @@ __device__ __forceinline__ void p2_block(const DevTensor& D, const Sc& c, uint8_
   const bool fullblk = FULL || nv == BS;
   const uint32_t gbase = lane & ~7u;
   const uint8_t* sg = st + L::OFF_G + bi * L::STR_G;
+  const uint32_t* sgnw = reinterpret_cast<const uint32_t*>(st + L::OFF_SGN + bi * 16);
 
   const bool has_state = c.flags & DF_M_HAS_STATE;
-  float cs_scale = 0.0f, alpha_old = 0.0f;
-  uint32_t sw[4] = {0, 0, 0, 0};
+  float cs_scale = 0.0f;
+  const float alpha_old = M.alpha_old;
+  const float alpha = M.alpha_new;
   if (has_state && active) {
     const uint8_t lab = st[L::OFF_LAB + bi];
     const float nrm = reinterpret_cast<const float*>(st + L::OFF_NRM)[bi];
     const uint16_t amp = reinterpret_cast<const uint16_t*>(st + L::OFF_AMP)[bi];
     cs_scale = costate_scale(lab, nrm, amp, c.sqbs);
-    const uint4 w = *reinterpret_cast<const uint4*>(st + L::OFF_SGN + bi * 16);
-    sw[0] = w.x; sw[1] = w.y; sw[2] = w.z; sw[3] = w.w;
-    alpha_old = *D.alpha_state;
   }
-  const float alpha = *D.alpha_new;
   float accd = 0.0f, accm = 0.0f;
   uint32_t myw = 0;
+#pragma unroll 1
+  for (int kq = 0; kq < 4; ++kq) {
+    const uint32_t sw = (has_state && active) ? sgnw[kq] : 0u;
 #pragma unroll
-  for (int k = 0; k < 16; ++k) {
-    const int t = j + 8 * k;
-    const bool ve = FULL || t < nv;
-    float g;
-    if (fullblk) g = PT ? ta_bf16_to_f32(reinterpret_cast<const uint16_t*>(sg)[t])
-                        : reinterpret_cast<const float*>(sg)[t];
-    else g = ve ? to_f32<PT>(D.g, e0 + t) : 0.0f;
-    const uint32_t bit = (sw[k >> 2] >> (8 * (k & 3) + 7 - j)) & 1u;
-    const float m = costate_m(g, alpha_old, cs_scale, bit, has_state, c.b1, c.omb1);
-    const float dl = ve ? __fsub_rn(m, __fmul_rn(alpha, g)) : 0.0f;  // costate.py:42
-    const float mm = ve ? m : 0.0f;
-    accd = __fadd_rn(accd, __fmul_rn(dl, dl));
-    accm = __fadd_rn(accm, __fmul_rn(mm, mm));
-    const uint32_t w = __ballot_sync(0xffffffffu, dl < 0.0f);
-    myw = (lane == k) ? w : myw;
-    if (!FULL && ve && (c.flags & DF_M_OUT)) D.m_out[e0 + t] = m;
+    for (int i = 0; i < 4; ++i) {
+      const int k = 4 * kq + i;
+      const int t = j + 8 * k;
+      const bool ve = FULL || t < nv;
+      float g;
+      if (fullblk) g = PT ? ta_bf16_to_f32(reinterpret_cast<const uint16_t*>(sg)[t])
+                          : reinterpret_cast<const float*>(sg)[t];
+      else g = ve ? to_f32<PT>(D.g, e0 + t) : 0.0f;
+      const uint32_t bit = (sw >> (8 * i + 7 - j)) & 1u;
+      const float m = costate_m(g, alpha_old, cs_scale, bit, has_state, c.b1, c.omb1);
+      const float dl = ve ? __fsub_rn(m, __fmul_rn(alpha, g)) : 0.0f;  // costate.py:42
+      const float mm = ve ? m : 0.0f;
+      accd = __fadd_rn(accd, __fmul_rn(dl, dl));
+      accm = __fadd_rn(accm, __fmul_rn(mm, mm));
+      const uint32_t w = __ballot_sync(0xffffffffu, dl < 0.0f);
+      myw = (lane == k) ? w : myw;
+      if (!FULL && ve && (c.flags & DF_M_OUT)) D.m_out[e0 + t] = m;
+    }
   }
   // torch row-norm order: lane accumulators summed 0..7 in sequence
   float sd = __shfl_sync(0xffffffffu, accd, gbase);
@@ -789,17 +873,25 @@ __device__ __forceinline__ void p2_block(const DevTensor& D, const Sc& c, uint8_
 }
 
 template <int PT>
+__device__ __noinline__ void p2_block_general(const StageMeta& M, uint8_t* st,
+                                              const DevTensor* T) {
+  const DevTensor& D = T[M.t];
+  const Sc c = load_sc(D);
+  p2_block<PT, false>(D, M, c, st);
+}
+
+template <int PT>
 __global__ void __launch_bounds__(NTHR) k_pass2(const __grid_constant__ KParams kp) {
   using L = P2L<PT>;
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* stages = smem;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + NSTAGE * L::STAGE);
-  uint64_t* done = full + NSTAGE;
-  StageMeta* meta = reinterpret_cast<StageMeta*>(done + NSTAGE);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + NSTAGE2 * L::STAGE);
+  uint64_t* done = full + NSTAGE2;
+  StageMeta* meta = reinterpret_cast<StageMeta*>(done + NSTAGE2);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < NSTAGE; ++s) {
+    for (int s = 0; s < NSTAGE2; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&done[s], NCW);
     }
@@ -808,7 +900,7 @@ __global__ void __launch_bounds__(NTHR) k_pass2(const __grid_constant__ KParams 
   __syncthreads();
 
   auto store = [&](uint8_t* st, const StageMeta& pm) {
-    const DevTensor& D = pm.D;
+    const DevTensor& D = kp.T[pm.t];
     bulk_s2g(D.sgn + pm.b0 * 16, st + L::OFF_SGN, TB * 16);
     bulk_s2g(D.nrm + pm.b0, st + L::OFF_NRM, TB * 4);
     bulk_s2g(D.amp + pm.b0, st + L::OFF_AMP, TB * 2);
@@ -819,25 +911,34 @@ __global__ void __launch_bounds__(NTHR) k_pass2(const __grid_constant__ KParams 
     if (lane == 0) {
       int it = 0;
       bool ok = true;
+      EntryWalk walk;
+      int cur_t = -1;
+      float cur_aold = 0.0f, cur_anew = 0.0f;
       for (int64_t tile = blockIdx.x; tile < kp.total; tile += gridDim.x, ++it) {
-        const int s = it % NSTAGE;
-        const uint32_t ph = (uint32_t)(it / NSTAGE) & 1u;
+        const int s = it % NSTAGE2;
+        const uint32_t ph = (uint32_t)(it / NSTAGE2) & 1u;
         uint8_t* st = stages + s * L::STAGE;
-        if (it >= NSTAGE) {
+        if (it >= NSTAGE2) {
           if (!wait_bar(&done[s], ph ^ 1u, kp.status)) { ok = false; break; }
           store(st, meta[s]);
           bulk_commit();
           bulk_wait_read_all();
         }
-        const int en = find_entry(kp.lbeg, kp.nl, tile);
+        const int en = walk.at(kp.lbeg, kp.nl, tile);
         const int t = kp.lidx[en];
         const DevTensor& D = kp.T[t];
+        if (t != cur_t) {
+          cur_t = t;
+          cur_aold = (D.flags & DF_M_HAS_STATE) ? *D.alpha_state : 0.0f;
+          cur_anew = *D.alpha_new;
+        }
         const int64_t b0 = (tile - kp.lbeg[en]) * TB;
         const int nblk = (int)min((int64_t)TB, D.nblk - b0);
-        meta[s].D = D;
         meta[s].t = t;
         meta[s].nblk = nblk;
         meta[s].b0 = b0;
+        meta[s].alpha_old = cur_aold;
+        meta[s].alpha_new = cur_anew;
         uint32_t bytes = 0;
         for (int i = 0; i < nblk; ++i)
           if (D.n - (b0 + i) * BS >= BS) bytes += BS * L::ESZ;
@@ -857,38 +958,39 @@ __global__ void __launch_bounds__(NTHR) k_pass2(const __grid_constant__ KParams 
           bulk_g2s(st + L::OFF_AMP, D.amp + b0, TB * 2, &full[s]);
         }
       }
-      const int first = it > NSTAGE ? it - NSTAGE : 0;
+      const int first = it > NSTAGE2 ? it - NSTAGE2 : 0;
       if (ok) {
         for (int r = first; r < it; ++r) {
-          const int s = r % NSTAGE;
-          if (!wait_bar(&done[s], (uint32_t)(r / NSTAGE) & 1u, kp.status)) { ok = false; break; }
+          const int s = r % NSTAGE2;
+          if (!wait_bar(&done[s], (uint32_t)(r / NSTAGE2) & 1u, kp.status)) { ok = false; break; }
           store(stages + s * L::STAGE, meta[s]);
           bulk_commit();
         }
       }
       if (!ok)
         for (int r = first; r < it; ++r)
-          wait_bar(&full[r % NSTAGE], (uint32_t)(r / NSTAGE) & 1u, kp.status);
+          wait_bar(&full[r % NSTAGE2], (uint32_t)(r / NSTAGE2) & 1u, kp.status);
       bulk_wait_all();
     }
     return;
   }
   int it = 0;
   for (int64_t tile = blockIdx.x; tile < kp.total; tile += gridDim.x, ++it) {
-    const int s = it % NSTAGE;
-    const uint32_t ph = (uint32_t)(it / NSTAGE) & 1u;
+    const int s = it % NSTAGE2;
+    const uint32_t ph = (uint32_t)(it / NSTAGE2) & 1u;
     if (!wait_bar(&full[s], ph, kp.status)) break;
     const StageMeta& pm = meta[s];
-    const DevTensor& D = pm.D;
-    const Sc c = load_sc(D);
-    const int nblk = pm.nblk;
-    const int64_t b0 = pm.b0;
+    const DevTensor& D = kp.T[pm.t];
     uint8_t* st = stages + s * L::STAGE;
     const int bi = warp * 4 + (lane >> 3);
-    const bool mine_full = bi < nblk && D.n - (b0 + bi) * BS >= BS;
-    const bool fast = __all_sync(0xffffffffu, mine_full) && !(c.flags & DF_M_OUT);
-    if (fast) p2_block<PT, true>(D, c, st, nblk, b0);
-    else p2_block<PT, false>(D, c, st, nblk, b0);
+    const bool mine_full = bi < pm.nblk && D.n - (pm.b0 + bi) * BS >= BS;
+    const bool fast = __all_sync(0xffffffffu, mine_full) && !(D.flags & DF_M_OUT);
+    if (fast) {
+      const Sc c = load_sc(D);
+      p2_block<PT, true>(D, pm, c, st);
+    } else {
+      p2_block_general<PT>(pm, st, kp.T);
+    }
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) mbar_arrive(&done[s]);
@@ -897,7 +999,7 @@ __global__ void __launch_bounds__(NTHR) k_pass2(const __grid_constant__ KParams 
 
 template <int PT>
 constexpr size_t p2_smem_bytes() {
-  return (size_t)NSTAGE * P2L<PT>::STAGE + 2 * NSTAGE * 8 + NSTAGE * sizeof(StageMeta);
+  return (size_t)NSTAGE2 * P2L<PT>::STAGE + 2 * NSTAGE2 * 8 + NSTAGE2 * sizeof(StageMeta);
 }
 
 // ---------------------------------------------------------------------------

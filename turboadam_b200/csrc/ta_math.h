@@ -118,12 +118,13 @@ TA_HD float ta_sqrt(float a) {
  * x = 2^e * m with m in [2/3, 4/3); f = m - 1 (exact);
  * log(x) = e*ln2 + f + f^2 Q(f), with e*ln2_hi + f summed by Fast2Sum so the
  * only large rounding is the final one.
- * Special inputs: NaN -> NaN, +inf -> +inf, 0 -> -inf, negative -> NaN.
+ * Special inputs: NaN -> the same NaN, +inf -> +inf, 0 -> -inf, negative -> NaN.
  */
 TA_HD float ta_logf(float x) {
+  if (x != x) return x; /* NaN propagates unchanged */
   if (!(x > 0.0f)) {
     if (x == 0.0f) return -INFINITY;
-    return ta_u2f(0x7fc00000u); /* NaN or negative */
+    return ta_u2f(0x7fc00000u); /* negative */
   }
   if (x == INFINITY) return x;
   int32_t ex = 0;
