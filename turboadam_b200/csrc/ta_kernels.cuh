@@ -2,11 +2,10 @@
 // (launched by ta_api.cu, the C-ABI of include/turboadam_b200.h).
 //
 // Data flow of one step (all tensors of a kind share one launch):
-//   pass 1  (one HBM stream over p, g and packed state; 1D TMA bulk copies
-//            into a 2-stage smem ring, one producer warp, four consumer
-//            warps): weight decay, m update (CoState decode+EMA or fp32
-//            EMA), v update (1Q decode -> EMA -> ln v), p.addcdiv_, then the
-//            stochastic re-quantisation of v, and per-block partial dots.
+//   pass 1  (one HBM stream over p, g and packed state): weight decay, m
+//            update (CoState decode+EMA or fp32 EMA), v update (1Q decode ->
+//            EMA -> ln v), p.addcdiv_, the stochastic re-quantisation of v,
+//            and per-block partial dots for alpha.
 //   alpha   (m.g)/(g.g) per CoState tensor: per-chunk fp64 trees, the last
 //            CTA of each tensor sums the chunks in order.
 //   pass 2  (CoState tensors: re-read g and the old encoding, recompute m_new
@@ -18,10 +17,18 @@
 // Arithmetic matches the reference CPU path op by op (oracle/ta_oracle.c
 // restates it) with ta_math.h for log/exp/fp16/Philox.
 //
-// Lane mapping (passes 1 and 2): a warp owns 4 blocks of the 16-block tile,
-// one per 8-lane group; lane j of a group owns elements j + 8k, k = 0..15.
-// Per-element smem arrays are placed one block per skewed stride so the 4
-// groups of a warp hit disjoint banks.
+// Pipeline of passes 1 and 2: persistent CTAs, one producer thread and four
+// consumer warps. The producer streams the inputs of 16-block tiles into a
+// ring of smem stages with 1D TMA bulk copies (cp.async.bulk, no multicast;
+// one copy per 4 consecutive blocks of each array) and writes the tile's
+// metadata, per-tensor scalars and output pointers beside them. Consumers
+// never modify the staged inputs and write every output straight to global
+// memory, so a stage is refilled as soon as its consumers arrive on its
+// "done" barrier.
+//
+// Lane mapping: warp w, 8-lane group q owns block 4q + w of the tile; lane j
+// owns elements j + 8k, k = 0..15. Copies of 4 blocks sit at a skewed stride
+// so the 4 groups of a warp (4 different copies) read disjoint smem banks.
 #pragma once
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -52,41 +59,109 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, uint32_
 }
 
 // ---------------------------------------------------------------------------
-// Stage layouts
+// Stage layouts. A per-element array holds the tile's 16 blocks as 4 copies
+// of 4 consecutive blocks; copy c starts at c * (4 * block bytes + skew).
 // ---------------------------------------------------------------------------
+template <int ESZ>
+struct Arr {
+  static constexpr int BLK = BS * ESZ;                      // bytes per block
+  static constexpr int SKEW = (8 * ESZ < 16) ? 16 : 8 * ESZ;
+  static constexpr int CSTR = 4 * BLK + SKEW;               // bytes per 4-block copy
+  static constexpr int BYTES = 4 * CSTR;
+  __device__ __forceinline__ static int off(int bi) { return (bi >> 2) * CSTR + (bi & 3) * BLK; }
+};
+
 template <int MK, int VK, int PT, bool UNI>
 struct P1L {
   static constexpr int ESZ = PT ? 2 : 4;
-  static constexpr int STR_P = BS * ESZ + (PT ? 16 : 32);  // skewed block stride
-  static constexpr int STR_4 = BS * 4 + 32;
-  static constexpr int STR_1 = BS + 16;
+  using AP = Arr<ESZ>;
+  using A4 = Arr<4>;
+  using A1 = Arr<1>;
   static constexpr int OFF_P = 0;
-  static constexpr int OFF_G = OFF_P + TB * STR_P;
-  static constexpr int OFF_IDX = OFF_G + TB * STR_P;
-  static constexpr int OFF_HDR = OFF_IDX + (VK == VK_ONEQ ? TB * STR_1 : 0);
+  static constexpr int OFF_G = OFF_P + AP::BYTES;
+  static constexpr int OFF_IDX = OFF_G + AP::BYTES;
+  static constexpr int OFF_HDR = OFF_IDX + (VK == VK_ONEQ ? A1::BYTES : 0);
   static constexpr int OFF_EAS = OFF_HDR + (VK == VK_ONEQ ? TB * 4 : 0);
-  static constexpr int OFF_LAB = OFF_EAS + (VK == VK_FP32 ? TB * STR_4 : 0);
+  static constexpr int OFF_LAB = OFF_EAS + (VK == VK_FP32 ? A4::BYTES : 0);
   static constexpr int OFF_SGN = OFF_LAB + (MK == MK_COSTATE ? 16 : 0);
   static constexpr int OFF_NRM = OFF_SGN + (MK == MK_COSTATE ? TB * 16 : 0);
   static constexpr int OFF_AMP = OFF_NRM + (MK == MK_COSTATE ? TB * 4 : 0);
   static constexpr int OFF_EA = OFF_AMP + (MK == MK_COSTATE ? TB * 2 : 0);
-  static constexpr int OFF_UNI = OFF_EA + (MK == MK_FP32 ? TB * STR_4 : 0);
-  static constexpr int END = OFF_UNI + ((UNI && VK == VK_ONEQ) ? TB * STR_4 : 0);
+  static constexpr int OFF_UNI = OFF_EA + (MK == MK_FP32 ? A4::BYTES : 0);
+  static constexpr int END = OFF_UNI + ((UNI && VK == VK_ONEQ) ? A4::BYTES : 0);
   static constexpr int STAGE = (END + 127) / 128 * 128;
 };
 
 template <int PT>
 struct P2L {
   static constexpr int ESZ = PT ? 2 : 4;
-  static constexpr int STR_G = BS * ESZ + (PT ? 16 : 32);
+  using AG = Arr<ESZ>;
   static constexpr int OFF_G = 0;
-  static constexpr int OFF_LAB = OFF_G + TB * STR_G;
+  static constexpr int OFF_LAB = OFF_G + AG::BYTES;
   static constexpr int OFF_SGN = OFF_LAB + 16;
   static constexpr int OFF_NRM = OFF_SGN + TB * 16;
   static constexpr int OFF_AMP = OFF_NRM + TB * 4;
-  static constexpr int OFF_RAT = OFF_AMP + TB * 2;
-  static constexpr int END = OFF_RAT + TB * 4;
+  static constexpr int END = OFF_AMP + TB * 2;
   static constexpr int STAGE = (END + 127) / 128 * 128;
+};
+
+constexpr int TABLE_STRIDE = 65;     // per-group exp table (<= 64 entries), padded
+constexpr int SCR_FLOATS = 16 * 32;  // per-warp scratch: ln v_new of 16 elements x 32 lanes
+constexpr int OB_STRIDE = BS + 16;   // per-group staging of the new 1Q indices (skewed)
+constexpr int OB_BYTES = 4 * OB_STRIDE;
+
+// Per-tensor scalars (fp32 values of the Python hyper-parameters as torch
+// rounds them), carried in the stage metadata.
+struct __align__(16) Sc {
+  float b1, omb1, b2, omb2;
+  float wdf, nlr, eps, bc1;
+  float bc2, rbc2, nbf, sqbs;
+  uint32_t flags, tid, step;
+  int32_t nbits;
+};
+
+__device__ __forceinline__ Sc load_sc(const DevTensor& D) {
+  Sc s;
+  s.b1 = D.b1; s.omb1 = D.omb1; s.b2 = D.b2; s.omb2 = D.omb2;
+  s.wdf = (D.flags & DF_WD) ? D.wdf : 1.0f;  // p * 1 == p exactly (optimizer.py:106)
+  s.nlr = D.nlr; s.eps = D.eps; s.bc1 = D.bc1; s.bc2 = D.bc2; s.rbc2 = D.rbc2;
+  s.nbf = D.nbf; s.sqbs = D.sqbs;
+  s.flags = D.flags; s.tid = D.tid; s.step = D.step; s.nbits = D.nbits;
+  return s;
+}
+
+// Per-tile metadata written by the producer before it arms the stage.
+struct __align__(16) StageMeta {
+  Sc c;
+  // pass-1 outputs
+  void* p;
+  uint8_t* v_idx;
+  uint16_t* v_hdr;
+  float* ea;
+  float* eas;
+  float* part;      // alpha partials [2][bpad]
+  // pass-2 outputs
+  uint8_t* sgn;
+  float* nrm;
+  uint16_t* amp;
+  float* ratios;
+  int64_t n;
+  int64_t bpad;
+  int64_t b0;       // first block (within tensor)
+  int32_t t;        // tensor index
+  int32_t nblk;     // blocks of this tile
+  float alpha_old;  // CoState alpha of the previous step (state)
+  float alpha_new;  // this step's alpha (pass 2)
+};
+
+struct KParams {
+  const DevTensor* T;
+  const int64_t* lbeg;  // [nl + 1] tile prefix of the launch list
+  const int32_t* lidx;  // [nl] tensor indices
+  int32_t nl;
+  int64_t total;        // tiles in this launch
+  uint32_t* status;
+  uint32_t rk0[10], rk1[10];  // Philox round keys (seed words + r * Weyl constants)
 };
 
 __device__ __forceinline__ int find_entry(const int64_t* lbeg, int nl, int64_t tile) {
@@ -98,17 +173,6 @@ __device__ __forceinline__ int find_entry(const int64_t* lbeg, int nl, int64_t t
   }
   return lo;
 }
-
-// Per-stage metadata written by the producer before it arms the barrier.
-// Consumers read the tensor's descriptor from global memory (L1-cached) once
-// per tile, and the per-tensor scalars into registers.
-struct __align__(16) StageMeta {
-  int32_t t;        // tensor index
-  int32_t nblk;     // blocks of this tile
-  int64_t b0;       // first block (within tensor)
-  float alpha_old;  // CoState alpha of the previous step (state)
-  float alpha_new;  // this step's alpha (pass 2)
-};
 
 // Incremental tile -> launch-list entry walk of a producer: tiles of one CTA
 // increase, so the entry only moves forward (one load per tensor change).
@@ -123,19 +187,6 @@ struct EntryWalk {
     }
     return en;
   }
-};
-
-constexpr int TABLE_STRIDE = 65;  // per-group exp table (<= 64 entries), padded
-constexpr int SCR_FLOATS = 16 * 32;  // per-warp scratch: ln v_new of 16 elements x 32 lanes
-
-struct KParams {
-  const DevTensor* T;
-  const int64_t* lbeg;  // [nl + 1] tile prefix of the launch list
-  const int32_t* lidx;  // [nl] tensor indices
-  int32_t nl;
-  int64_t total;        // tiles in this launch
-  uint32_t* status;
-  uint32_t rk0[10], rk1[10];  // Philox round keys (seed words + r * Weyl constants)
 };
 
 // Philox4x32-10 with precomputed round keys (identical to ta_philox4x32_10).
@@ -175,39 +226,6 @@ __device__ __forceinline__ float costate_scale(uint8_t label, float norm, uint16
   return label == 1 ? ph : (label == 2 ? am : 0.0f);
 }
 
-// Branch-free ta_logf for the kernels (same value as ta_logf for every input):
-// special cases are resolved by selects after the common polynomial.
-__device__ __forceinline__ float log_bf(float x) {
-  const bool sub = x < 0x1p-126f;
-  const float xs = __fmul_rn(x, sub ? 0x1p23f : 1.0f);
-  const int32_t ex = sub ? -23 : 0;
-  const uint32_t ix = __float_as_uint(xs);
-  const int32_t e = ((int32_t)(ix - 0x3f2aaaabu)) >> 23;
-  const float m = __uint_as_float(ix - ((uint32_t)e << 23));
-  const float f = __fsub_rn(m, 1.0f);
-  const float ef = (float)(e + ex);
-  float q = TA_LOG_Q0;
-  q = __fmaf_rn(q, f, TA_LOG_Q1);
-  q = __fmaf_rn(q, f, TA_LOG_Q2);
-  q = __fmaf_rn(q, f, TA_LOG_Q3);
-  q = __fmaf_rn(q, f, TA_LOG_Q4);
-  q = __fmaf_rn(q, f, TA_LOG_Q5);
-  q = __fmaf_rn(q, f, TA_LOG_Q6);
-  q = __fmaf_rn(q, f, TA_LOG_Q7);
-  q = __fmaf_rn(q, f, TA_LOG_Q8);
-  q = __fmaf_rn(q, f, TA_LOG_Q9);
-  const float f2 = __fmul_rn(f, f);
-  const float hi = __fmul_rn(ef, TA_LN2_HI);
-  const float s = __fadd_rn(hi, f);
-  const float err = __fadd_rn(__fsub_rn(hi, s), f);
-  const float lo = __fmaf_rn(f2, q, __fmaf_rn(ef, TA_LN2_LO, err));
-  float r = __fadd_rn(s, lo);
-  r = (x == INFINITY) ? x : r;
-  r = (x == 0.0f) ? -INFINITY : r;
-  r = (x < 0.0f || x != x) ? __uint_as_float(0x7fc00000u) : r;
-  return r;
-}
-
 // ta_logf(clamp_min(v, 1e-38)) (quantize.py:275) for every v: the clamped
 // argument is >= 1e-38 (possibly subnormal), +inf or NaN, so only the
 // subnormal scaling and the non-finite passthrough need selects.
@@ -239,31 +257,83 @@ __device__ __forceinline__ float log_clamped(float v) {
   return (__float_as_uint(x) >= 0x7f800000u) ? x : r;  // +inf -> +inf, NaN -> NaN
 }
 
+template <int PT>
+__device__ __forceinline__ float ld_smem_elem(const uint8_t* base, int t) {
+  return PT ? ta_bf16_to_f32(reinterpret_cast<const uint16_t*>(base)[t])
+            : reinterpret_cast<const float*>(base)[t];
+}
+
+template <int PT>
+__device__ __forceinline__ void st_param(void* p, int64_t e, float v) {
+  if (PT) reinterpret_cast<uint16_t*>(p)[e] = ta_f32_to_bf16(v);
+  else reinterpret_cast<float*>(p)[e] = v;
+}
+
+// One element of the p update (optimizer.py:106-107, 163/167, 170), given the
+// old parameter, m_new and v_new. Exact fast divisions (Markstein) for v_new
+// = 0 or normal; a subnormal v_new is flagged for the IEEE fallback.
+template <int PT>
+__device__ __forceinline__ float adam_elem(float pv, float m, float vn, const Sc& c, bool* sub) {
+  pv = __fmul_rn(pv, c.wdf);
+  if (PT) pv = ta_bf16_to_f32(ta_f32_to_bf16(pv));
+  const float d = __fadd_rn(__fsqrt_rn(div_v_bc2(vn, c.bc2, c.rbc2, sub)), c.eps);
+  const float upd = __fdiv_rn(__fmul_rn(c.nlr, m), __fmul_rn(d, c.bc1));
+  return __fadd_rn(pv, upd);
+}
+
+// The same update with IEEE divisions throughout.
+// (Scalars by value: a struct passed by reference to an out-of-line function
+// would be copied to local memory.)
+template <int PT>
+__device__ __noinline__ float adam_elem_ieee_v(float pv, float m, float vn, float wdf, float bc2,
+                                               float eps, float nlr, float bc1) {
+  pv = __fmul_rn(pv, wdf);
+  if (PT) pv = ta_bf16_to_f32(ta_f32_to_bf16(pv));
+  const float d = __fadd_rn(__fsqrt_rn(__fdiv_rn(vn, bc2)), eps);
+  const float upd = __fdiv_rn(__fmul_rn(nlr, m), __fmul_rn(d, bc1));
+  return __fadd_rn(pv, upd);
+}
+template <int PT>
+__device__ __forceinline__ float adam_elem_ieee(float pv, float m, float vn, const Sc& c) {
+  return adam_elem_ieee_v<PT>(pv, m, vn, c.wdf, c.bc2, c.eps, c.nlr, c.bc1);
+}
+
 // ---------------------------------------------------------------------------
 // Pass 1
 // ---------------------------------------------------------------------------
+// Producer: bulk copies of one tile's inputs. Per-element arrays go as one
+// copy per run of up to 4 consecutive full blocks; the ragged tail block of
+// p/g/ea/eas is read by the consumers from global memory. Padded state (1Q
+// indices, uniforms) is copied for every present block.
 template <int MK, int VK, int PT, bool UNI>
-__device__ __forceinline__ void p1_issue(const DevTensor& D, uint8_t* st, int nblk, int64_t b0,
-                                         uint64_t* bar, bool count_only, uint32_t& bytes) {
+__device__ __forceinline__ uint32_t p1_issue(const DevTensor& D, uint8_t* st, int nblk,
+                                             int64_t b0, uint64_t* bar, bool count_only) {
   using L = P1L<MK, VK, PT, UNI>;
+  using AP = typename L::AP;
+  using A4 = typename L::A4;
+  using A1 = typename L::A1;
   const bool param = !(D.flags & DF_NO_PARAM);
-  bytes = 0;
+  uint32_t bytes = 0;
   auto cp = [&](void* dst, const void* src, uint32_t nb) {
     bytes += nb;
     if (!count_only) bulk_g2s(dst, src, nb, bar);
   };
-  for (int i = 0; i < nblk; ++i) {
-    const int64_t e0 = (b0 + i) * BS;
-    if (D.n - e0 >= BS) {  // full block: user arrays too
+  const int64_t nfull = min((int64_t)nblk, (D.n - b0 * BS) / BS);
+#pragma unroll 1
+  for (int c = 0; c < 4; ++c) {
+    const int cnt = (int)max((int64_t)0, min((int64_t)4, nfull - 4 * c));
+    const int cnt_all = max(0, min(4, nblk - 4 * c));
+    const int64_t e0 = (b0 + 4 * c) * BS;
+    if (cnt > 0) {
       if (param)
-        cp(st + L::OFF_P + i * L::STR_P, (const uint8_t*)D.p + e0 * L::ESZ, BS * L::ESZ);
-      cp(st + L::OFF_G + i * L::STR_P, (const uint8_t*)D.g + e0 * L::ESZ, BS * L::ESZ);
-      if (MK == MK_FP32) cp(st + L::OFF_EA + i * L::STR_4, D.ea + e0, BS * 4);
-      if (VK == VK_FP32) cp(st + L::OFF_EAS + i * L::STR_4, D.eas + e0, BS * 4);
+        cp(st + L::OFF_P + c * AP::CSTR, (const uint8_t*)D.p + e0 * L::ESZ, cnt * AP::BLK);
+      cp(st + L::OFF_G + c * AP::CSTR, (const uint8_t*)D.g + e0 * L::ESZ, cnt * AP::BLK);
+      if (MK == MK_FP32) cp(st + L::OFF_EA + c * A4::CSTR, D.ea + e0, cnt * A4::BLK);
+      if (VK == VK_FP32) cp(st + L::OFF_EAS + c * A4::CSTR, D.eas + e0, cnt * A4::BLK);
     }
-    if (VK == VK_ONEQ) {
-      cp(st + L::OFF_IDX + i * L::STR_1, D.v_idx + e0, BS);
-      if (UNI) cp(st + L::OFF_UNI + i * L::STR_4, D.uni + e0, BS * 4);
+    if (VK == VK_ONEQ && cnt_all > 0) {
+      cp(st + L::OFF_IDX + c * A1::CSTR, D.v_idx + e0, cnt_all * A1::BLK);
+      if (UNI) cp(st + L::OFF_UNI + c * A4::CSTR, D.uni + e0, cnt_all * A4::BLK);
     }
   }
   // per-tile arrays (state arrays are padded to whole tiles)
@@ -274,127 +344,79 @@ __device__ __forceinline__ void p1_issue(const DevTensor& D, uint8_t* st, int nb
     cp(st + L::OFF_NRM, D.nrm + b0, TB * 4);
     cp(st + L::OFF_AMP, D.amp + b0, TB * 2);
   }
-}
-
-template <int MK, int VK, int PT, bool UNI>
-__device__ __forceinline__ void p1_store(const DevTensor& D, uint8_t* st, int nblk, int64_t b0) {
-  using L = P1L<MK, VK, PT, UNI>;
-  const bool param = !(D.flags & DF_NO_PARAM);
-  for (int i = 0; i < nblk; ++i) {
-    const int64_t e0 = (b0 + i) * BS;
-    if (D.n - e0 >= BS) {
-      if (param) bulk_s2g((uint8_t*)D.p + e0 * L::ESZ, st + L::OFF_P + i * L::STR_P, BS * L::ESZ);
-      if (MK == MK_FP32) bulk_s2g(D.ea + e0, st + L::OFF_EA + i * L::STR_4, BS * 4);
-      if (VK == VK_FP32) bulk_s2g(D.eas + e0, st + L::OFF_EAS + i * L::STR_4, BS * 4);
-    }
-    if (VK == VK_ONEQ) bulk_s2g(D.v_idx + e0, st + L::OFF_IDX + i * L::STR_1, BS);
-  }
-  if (VK == VK_ONEQ) bulk_s2g(D.v_hdr + b0 * 2, st + L::OFF_HDR, TB * 4);
-}
-
-// Per-tensor scalars, read once per block from the smem descriptor copy.
-struct Sc {
-  float b1, omb1, b2, omb2, wdf, nlr, eps, bc1, bc2, rbc2, nbf, sqbs;
-  uint32_t flags, tid, step;
-  int nbits;
-};
-
-__device__ __forceinline__ Sc load_sc(const DevTensor& D) {
-  Sc s;
-  s.b1 = D.b1; s.omb1 = D.omb1; s.b2 = D.b2; s.omb2 = D.omb2;
-  s.wdf = (D.flags & DF_WD) ? D.wdf : 1.0f;  // p * 1 == p exactly (optimizer.py:106)
-  s.nlr = D.nlr; s.eps = D.eps; s.bc1 = D.bc1; s.bc2 = D.bc2; s.rbc2 = D.rbc2;
-  s.nbf = D.nbf; s.sqbs = D.sqbs;
-  s.flags = D.flags; s.tid = D.tid; s.step = D.step; s.nbits = D.nbits;
-  return s;
-}
-
-// One element of the p update (optimizer.py:106-107, 163/167, 170), given the
-// already rounded weight-decayed parameter, m_new and v_new.
-template <int PT>
-__device__ __forceinline__ float adam_elem(float pv, float m, float vn, const Sc& c, bool* sub) {
-  pv = __fmul_rn(pv, c.wdf);
-  if (PT) pv = ta_bf16_to_f32(ta_f32_to_bf16(pv));
-  const float d = __fadd_rn(__fsqrt_rn(div_v_bc2(vn, c.bc2, c.rbc2, sub)), c.eps);
-  const float upd = __fdiv_rn(__fmul_rn(c.nlr, m), __fmul_rn(d, c.bc1));
-  return __fadd_rn(pv, upd);
-}
-
-// Exact IEEE version of the same update for elements whose v/bc2 needs the
-// subnormal path (v_new < 2^-126 after ~18k zero-gradient steps).
-template <int PT>
-__device__ __noinline__ float adam_elem_ieee(float pv, float m, float vn, const Sc& c) {
-  pv = __fmul_rn(pv, c.wdf);
-  if (PT) pv = ta_bf16_to_f32(ta_f32_to_bf16(pv));
-  const float d = __fadd_rn(__fsqrt_rn(__fdiv_rn(vn, c.bc2)), c.eps);
-  const float upd = __fdiv_rn(__fmul_rn(c.nlr, m), __fmul_rn(d, c.bc1));
-  return __fadd_rn(pv, upd);
+  return bytes;
 }
 
 // Exact recomputation of one element of a full block (rare path): used when
 // v/bc2 needs the subnormal IEEE fallback or a stored index is >= 2^nbits.
 // Recomputes m, v_new, ln v_new and the parameter update from the staged
-// inputs (the old parameter is still in global memory, the tile has not been
-// stored yet) and writes the updated parameter to smem. Returns ln v_new.
+// (unmodified) inputs and stores the parameter. Returns ln v_new.
 template <int MK, int VK, int PT, bool UNI>
-__device__ __noinline__ float p1_fix_elem(const DevTensor& D, const Sc& c, uint8_t* st, int bi,
-                                          int t, int64_t e, float alpha_old, float cs_scale,
-                                          uint32_t bit, bool has_state, float lmin, float span) {
+__device__ __noinline__ float p1_fix_elem(const StageMeta& M, const uint8_t* st, int bi, int t,
+                                          int64_t e, float cs_scale, uint32_t bit,
+                                          bool has_state, float lmin, float span) {
   using L = P1L<MK, VK, PT, UNI>;
-  uint8_t* sp = st + L::OFF_P + bi * L::STR_P;
-  const uint8_t* sg = st + L::OFF_G + bi * L::STR_P;
-  const float g = PT ? ta_bf16_to_f32(reinterpret_cast<const uint16_t*>(sg)[t])
-                     : reinterpret_cast<const float*>(sg)[t];
+  const Sc c = M.c;
+  const float g = ld_smem_elem<PT>(st + L::OFF_G + L::AP::off(bi), t);
   float m = 0.0f;
-  if (MK == MK_COSTATE) m = costate_m(g, alpha_old, cs_scale, bit, has_state, c.b1, c.omb1);
-  else if (MK == MK_FP32) m = reinterpret_cast<const float*>(st + L::OFF_EA + bi * L::STR_4)[t];
+  if (MK == MK_COSTATE) {
+    m = costate_m(g, M.alpha_old, cs_scale, bit, has_state, c.b1, c.omb1);
+  } else if (MK == MK_FP32) {
+    const float ea = reinterpret_cast<const float*>(st + L::OFF_EA + L::A4::off(bi))[t];
+    m = __fmaf_rn(g, c.omb1, __fmul_rn(ea, c.b1));
+  }
   float vn = 0.0f, lv = 0.0f;
   if (VK == VK_ONEQ) {
-    const int id = st[L::OFF_IDX + bi * L::STR_1 + t];
+    const int id = st[L::OFF_IDX + L::A1::off(bi) + t];
     const float qv = __fdiv_rn(__fadd_rn((float)id, 0.5f), c.nbf);
     const float vo = ta_expf(__fadd_rn(lmin, __fmul_rn(qv, span)));
     vn = __fmaf_rn(__fmul_rn(g, g), c.omb2, __fmul_rn(vo, c.b2));
     lv = log_clamped(vn);
   } else if (VK == VK_FP32) {
-    vn = reinterpret_cast<const float*>(st + L::OFF_EAS + bi * L::STR_4)[t];
+    const float vs = reinterpret_cast<const float*>(st + L::OFF_EAS + L::A4::off(bi))[t];
+    vn = __fmaf_rn(__fmul_rn(c.omb2, g), g, __fmul_rn(vs, c.b2));
   }
   if (!(c.flags & DF_NO_PARAM)) {
-    const float pv = adam_elem_ieee<PT>(to_f32<PT>(D.p, e), m, vn, c);
-    if (PT) reinterpret_cast<uint16_t*>(sp)[t] = ta_f32_to_bf16(pv);
-    else reinterpret_cast<float*>(sp)[t] = pv;
+    const float pv = ld_smem_elem<PT>(st + L::OFF_P + L::AP::off(bi), t);
+    st_param<PT>(M.p, e, adam_elem_ieee<PT>(pv, m, vn, c));
   }
   return lv;
 }
 
-// One 128-element block per 8-lane group; lane j owns elements j + 8k, k in
-// 0..15, visited as 4 quads (kq) of 4. FULL: every group of the warp has a
-// full block (user arrays staged in smem, no bounds checks); otherwise the
-// general path: per-element bounds, global loads/stores for the ragged tail
-// block, and exact IEEE divisions there. ln v_new goes through a per-lane
-// smem scratch (scr[k*32 + lane]) between phase A and phase B.
+// One 128-element block per 8-lane group; elements visited as 4 quads of 4.
+// FULL: every group of the warp has a full block (inputs from smem, no bounds
+// checks); otherwise the general path: per-element bounds, global loads for
+// the ragged tail block and IEEE divisions there. ln v_new goes through a
+// per-lane smem scratch (scr[k*32 + lane]) between phase A and phase B, the
+// new indices through a per-group byte buffer (ob) for 16-byte stores.
 template <int MK, int VK, int PT, bool UNI, bool TABLE, bool FULL>
-__device__ __forceinline__ void p1_block(const DevTensor& D, const StageMeta& M, const Sc& c,
-                                         uint8_t* st, float* table, float* scr,
-                                         const KParams& kp) {
+__device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
+                                         const uint8_t* st, float* table, float* scr,
+                                         uint8_t* ob, const KParams& kp) {
   using L = P1L<MK, VK, PT, UNI>;
-  const int nblk = M.nblk;
-  const int64_t b0 = M.b0;
+  const Sc c = M.c;
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int q = lane >> 3;
   const int j = lane & 7;
-  const int bi = warp * 4 + q;
-  const bool active = FULL || bi < nblk;
-  const int64_t b = b0 + bi;
+  const int bi = 4 * q + warp;
+  const bool active = FULL || bi < M.nblk;
+  const int64_t b = M.b0 + bi;
   const int64_t e0 = b * BS;
-  const int nv = FULL ? BS : (active ? (int)min((int64_t)BS, D.n - e0) : 0);
+  const int nv = FULL ? BS : (active ? (int)min((int64_t)BS, M.n - e0) : 0);
   const bool fullblk = FULL || nv == BS;
   const bool param = !(c.flags & DF_NO_PARAM);
+  void* const gp = M.p;
+  float* const gea = M.ea;
+  float* const geas = M.eas;
 
-  uint8_t* sp = st + L::OFF_P + bi * L::STR_P;
-  const uint8_t* sg = st + L::OFF_G + bi * L::STR_P;
-  const uint8_t* sidx = st + L::OFF_IDX + bi * L::STR_1;
+  const uint8_t* sp = st + L::OFF_P + L::AP::off(bi);
+  const uint8_t* sg = st + L::OFF_G + L::AP::off(bi);
+  const uint8_t* sidx = st + L::OFF_IDX + L::A1::off(bi);
+  const float* sea = reinterpret_cast<const float*>(st + L::OFF_EA + L::A4::off(bi));
+  const float* seas = reinterpret_cast<const float*>(st + L::OFF_EAS + L::A4::off(bi));
   const uint32_t* sgnw = reinterpret_cast<const uint32_t*>(st + L::OFF_SGN + bi * 16);
+  const DevTensor* D = FULL ? nullptr : &T[M.t];  // tail loads and seam outputs only
 
   // ---- per-block CoState decode scalars (costate.py:290-314)
   float cs_scale = 0.0f;
@@ -441,9 +463,8 @@ __device__ __forceinline__ void p1_block(const DevTensor& D, const StageMeta& M,
       const int64_t e = e0 + t;
       const bool ve = FULL || t < nv;
       float g;
-      if (fullblk) g = PT ? ta_bf16_to_f32(reinterpret_cast<const uint16_t*>(sg)[t])
-                          : reinterpret_cast<const float*>(sg)[t];
-      else g = ve ? to_f32<PT>(D.g, e) : 0.0f;
+      if (fullblk) g = ld_smem_elem<PT>(sg, t);
+      else g = ve ? to_f32<PT>(D->g, e) : 0.0f;
       gbad = __fmaf_rn(g, 0.0f, gbad);
       float m = 0.0f;
       if (MK == MK_COSTATE) {
@@ -454,11 +475,9 @@ __device__ __forceinline__ void p1_block(const DevTensor& D, const StageMeta& M,
           gg = __fmaf_rn(g, g, gg);
         }
       } else if (MK == MK_FP32) {
-        float* sea = reinterpret_cast<float*>(st + L::OFF_EA + bi * L::STR_4);
-        const float ea = fullblk ? sea[t] : (ve ? D.ea[e] : 0.0f);
+        const float ea = fullblk ? sea[t] : (ve ? D->ea[e] : 0.0f);
         m = __fmaf_rn(g, c.omb1, __fmul_rn(ea, c.b1));  // optimizer.py:113
-        if (fullblk) sea[t] = m;
-        else if (ve) D.ea[e] = m;
+        if (ve) gea[e] = m;
       }
       float vn = 0.0f;
       if (VK == VK_ONEQ) {
@@ -480,31 +499,23 @@ __device__ __forceinline__ void p1_block(const DevTensor& D, const StageMeta& M,
           vmax = fmaxf(lv, vmax);
         }
       } else if (VK == VK_FP32) {
-        float* sea = reinterpret_cast<float*>(st + L::OFF_EAS + bi * L::STR_4);
-        const float vs = fullblk ? sea[t] : (ve ? D.eas[e] : 0.0f);
+        const float vs = fullblk ? seas[t] : (ve ? D->eas[e] : 0.0f);
         vn = __fmaf_rn(__fmul_rn(c.omb2, g), g, __fmul_rn(vs, c.b2));  // optimizer.py:166
-        if (fullblk) sea[t] = vn;
-        else if (ve) D.eas[e] = vn;
+        if (ve) geas[e] = vn;
         sub = sub || (vn < 0x1p-126f && vn > 0.0f);
       }
       if (param && ve) {
         float pv;
-        if (fullblk) pv = PT ? ta_bf16_to_f32(reinterpret_cast<const uint16_t*>(sp)[t])
-                             : reinterpret_cast<const float*>(sp)[t];
-        else pv = to_f32<PT>(D.p, e);
-        bool dummy = false;
-        pv = fullblk ? adam_elem<PT>(pv, m, vn, c, &dummy) : adam_elem_ieee<PT>(pv, m, vn, c);
-        if (PT) {
-          const uint16_t h = ta_f32_to_bf16(pv);
-          if (fullblk) reinterpret_cast<uint16_t*>(sp)[t] = h;
-          else reinterpret_cast<uint16_t*>(D.p)[e] = h;
+        if (fullblk) {
+          bool s2 = false;
+          pv = adam_elem<PT>(ld_smem_elem<PT>(sp, t), m, vn, c, &s2);
         } else {
-          if (fullblk) reinterpret_cast<float*>(sp)[t] = pv;
-          else reinterpret_cast<float*>(D.p)[e] = pv;
+          pv = adam_elem_ieee<PT>(to_f32<PT>(D->p, e), m, vn, c);
         }
+        st_param<PT>(gp, e, pv);
       }
-      if (!FULL && ve && (c.flags & DF_M_OUT)) D.m_out[e] = m;
-      if (!FULL && ve && (c.flags & DF_V_OUT)) D.v_out[e] = vn;
+      if (!FULL && ve && (c.flags & DF_M_OUT)) D->m_out[e] = m;
+      if (!FULL && ve && (c.flags & DF_V_OUT)) D->v_out[e] = vn;
     }
   }
   if (gbad != gbad) atomicOr(kp.status, 1u);
@@ -519,9 +530,8 @@ __device__ __forceinline__ void p1_block(const DevTensor& D, const StageMeta& M,
     for (int k = 0; k < 16; ++k) {
       const uint32_t sw = (MK == MK_COSTATE && has_state) ? sgnw[k >> 2] : 0u;
       const uint32_t bit = (sw >> (8 * (k & 3) + 7 - j)) & 1u;
-      const float lv = p1_fix_elem<MK, VK, PT, UNI>(D, c, st, bi, j + 8 * k, e0 + j + 8 * k,
-                                                     alpha_old, cs_scale, bit, has_state, lmin,
-                                                     span);
+      const float lv = p1_fix_elem<MK, VK, PT, UNI>(M, st, bi, j + 8 * k, e0 + j + 8 * k,
+                                                     cs_scale, bit, has_state, lmin, span);
       if (VK == VK_ONEQ) scr[k * 32 + lane] = lv;
     }
     if (VK == VK_ONEQ) {  // block extrema from the recomputed logs
@@ -544,8 +554,8 @@ __device__ __forceinline__ void p1_block(const DevTensor& D, const StageMeta& M,
       gg = __fadd_rn(gg, __shfl_xor_sync(0xffffffffu, gg, off));
     }
     if (active && j == 0) {
-      D.part[b] = mg;
-      D.part[D.bpad + b] = gg;
+      M.part[b] = mg;
+      M.part[M.bpad + b] = gg;
     }
   }
 
@@ -556,18 +566,16 @@ __device__ __forceinline__ void p1_block(const DevTensor& D, const StageMeta& M,
       vmin = fminf(vmin, __shfl_xor_sync(0xffffffffu, vmin, off));
       vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, off));
     }
-    if (active && j == 0) {
-      uint16_t* hdr = reinterpret_cast<uint16_t*>(st + L::OFF_HDR);
-      hdr[bi * 2] = ta_f32_to_f16(vmin);
-      hdr[bi * 2 + 1] = ta_f32_to_f16(vmax);
-    }
+    if (active && j == 0)
+      reinterpret_cast<uint32_t*>(M.v_hdr)[b] =
+          (uint32_t)ta_f32_to_f16(vmin) | ((uint32_t)ta_f32_to_f16(vmax) << 16);
     // (L - min) / span: |L - min| is 0 or >= 2^-47 (ln of floats != 1 is
     // >= 5.9e-8 in magnitude), inside div_by's exact range.
     const float nspan = clamp_min(__fsub_rn(vmax, vmin), 1e-10f);
     const float rspan = __frcp_rn(nspan);
     const float top = c.nbf - 1.0f;
-    const float* suni = reinterpret_cast<const float*>(st + L::OFF_UNI + bi * L::STR_4);
-    uint8_t* sidx_w = st + L::OFF_IDX + bi * L::STR_1;
+    const float* suni = reinterpret_cast<const float*>(st + L::OFF_UNI + L::A4::off(bi));
+    uint8_t* obq = ob + q * OB_STRIDE;
 #pragma unroll 1
     for (int kq = 0; kq < 4; ++kq) {
       uint32_t rnd[4] = {0, 0, 0, 0};
@@ -589,19 +597,32 @@ __device__ __forceinline__ void p1_block(const DevTensor& D, const StageMeta& M,
         float r = __fadd_rn(fl, (u < fr) ? 1.0f : 0.0f);
         if (!FULL) r = (r < 0.0f) ? 0.0f : r;  // valid elements have L >= min: r >= 0
         r = (r > top) ? top : r;
-        if (active) sidx_w[t] = (uint8_t)r;
+        obq[t] = (uint8_t)r;
       }
     }
+    __syncwarp();
+    if (active)
+      reinterpret_cast<uint4*>(M.v_idx + e0)[j] = reinterpret_cast<const uint4*>(obq)[j];
   }
 }
 
 // The general (tail) path lives out of line so the hot loop's code stays small.
 template <int MK, int VK, int PT, bool UNI, bool TABLE>
-__device__ __noinline__ void p1_block_general(const StageMeta& M, uint8_t* st, float* table,
-                                              float* scr, const KParams& kp) {
-  const DevTensor& D = kp.T[M.t];
-  const Sc c = load_sc(D);
-  p1_block<MK, VK, PT, UNI, TABLE, false>(D, M, c, st, table, scr, kp);
+__device__ __noinline__ void p1_block_general(const DevTensor* T, const StageMeta& M,
+                                              const uint8_t* st, float* table, float* scr,
+                                              uint8_t* ob, const KParams& kp) {
+  p1_block<MK, VK, PT, UNI, TABLE, false>(T, M, st, table, scr, ob, kp);
+}
+
+__device__ __forceinline__ void fill_meta_common(StageMeta& m, const DevTensor& D, const Sc& c,
+                                                 int t, int nblk, int64_t b0, float aold) {
+  m.c = c;
+  m.n = D.n;
+  m.bpad = D.bpad;
+  m.b0 = b0;
+  m.t = t;
+  m.nblk = nblk;
+  m.alpha_old = aold;
 }
 
 template <int MK, int VK, int PT, bool UNI, bool TABLE>
@@ -613,6 +634,7 @@ __global__ void __launch_bounds__(NTHR, 4) k_pass1(const __grid_constant__ KPara
   uint64_t* done = full + NSTAGE;
   StageMeta* meta = reinterpret_cast<StageMeta*>(done + NSTAGE);
   float* tables = reinterpret_cast<float*>(meta + NSTAGE);
+  uint8_t* obufs = reinterpret_cast<uint8_t*>(tables + NCW * 4 * TABLE_STRIDE + NCW * SCR_FLOATS);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -625,84 +647,67 @@ __global__ void __launch_bounds__(NTHR, 4) k_pass1(const __grid_constant__ KPara
   }
   __syncthreads();
 
-  if (warp == NCW) {  // producer / storer
+  if (warp == NCW) {  // producer
     if (lane == 0) {
       int it = 0;
-      bool ok = true;
       EntryWalk walk;
       int cur_t = -1;
       float cur_alpha = 0.0f;
+      Sc cur_c;
       for (int64_t tile = blockIdx.x; tile < kp.total; tile += gridDim.x, ++it) {
         const int s = it % NSTAGE;
         const uint32_t ph = (uint32_t)(it / NSTAGE) & 1u;
         uint8_t* st = stages + s * L::STAGE;
-        if (it >= NSTAGE) {
-          if (!wait_bar(&done[s], ph ^ 1u, kp.status)) { ok = false; break; }
-          const StageMeta& pm = meta[s];
-          p1_store<MK, VK, PT, UNI>(kp.T[pm.t], st, pm.nblk, pm.b0);
-          bulk_commit();
-          bulk_wait_read_all();
-        }
         const int en = walk.at(kp.lbeg, kp.nl, tile);
         const int t = kp.lidx[en];
         const DevTensor& D = kp.T[t];
         if (t != cur_t) {  // per-tensor values, loaded once per tensor change
           cur_t = t;
+          cur_c = load_sc(D);
           cur_alpha = (MK == MK_COSTATE && (D.flags & DF_M_HAS_STATE)) ? *D.alpha_state : 0.0f;
         }
-        const int64_t lt = tile - kp.lbeg[en];
-        const int64_t b0 = lt * TB;
+        const int64_t b0 = (tile - kp.lbeg[en]) * TB;
         const int nblk = (int)min((int64_t)TB, D.nblk - b0);
-        meta[s].t = t;
-        meta[s].nblk = nblk;
-        meta[s].b0 = b0;
-        meta[s].alpha_old = cur_alpha;
-        uint32_t bytes;
-        p1_issue<MK, VK, PT, UNI>(D, st, nblk, b0, &full[s], true, bytes);
-        mbar_arrive_expect_tx(&full[s], bytes);
-        p1_issue<MK, VK, PT, UNI>(D, st, nblk, b0, &full[s], false, bytes);
+        if (it >= NSTAGE && !wait_bar(&done[s], ph ^ 1u, kp.status)) break;
+        StageMeta& m = meta[s];
+        fill_meta_common(m, D, cur_c, t, nblk, b0, cur_alpha);
+        m.p = D.p;
+        m.v_idx = D.v_idx;
+        m.v_hdr = D.v_hdr;
+        m.ea = D.ea;
+        m.eas = D.eas;
+        m.part = D.part;
+        mbar_arrive_expect_tx(&full[s], p1_issue<MK, VK, PT, UNI>(D, st, nblk, b0, &full[s], true));
+        p1_issue<MK, VK, PT, UNI>(D, st, nblk, b0, &full[s], false);
       }
+      // let every load this CTA issued land before the CTA can exit
       const int first = it > NSTAGE ? it - NSTAGE : 0;
-      if (ok) {
-        for (int r = first; r < it; ++r) {
-          const int s = r % NSTAGE;
-          if (!wait_bar(&done[s], (uint32_t)(r / NSTAGE) & 1u, kp.status)) { ok = false; break; }
-          const StageMeta& pm = meta[s];
-          p1_store<MK, VK, PT, UNI>(kp.T[pm.t], stages + s * L::STAGE, pm.nblk, pm.b0);
-          bulk_commit();
-        }
-      }
-      if (!ok)  // a wait ran out: let this CTA's own loads land before exiting
-        for (int r = first; r < it; ++r)
-          wait_bar(&full[r % NSTAGE], (uint32_t)(r / NSTAGE) & 1u, kp.status);
-      bulk_wait_all();
+      for (int r = first; r < it; ++r)
+        wait_bar(&full[r % NSTAGE], (uint32_t)(r / NSTAGE) & 1u, kp.status);
     }
     return;
   }
 
   float* table = tables + warp * 4 * TABLE_STRIDE;
   float* scr = tables + NCW * 4 * TABLE_STRIDE + warp * SCR_FLOATS;
+  uint8_t* ob = obufs + warp * OB_BYTES;
   int it = 0;
   for (int64_t tile = blockIdx.x; tile < kp.total; tile += gridDim.x, ++it) {
     const int s = it % NSTAGE;
     const uint32_t ph = (uint32_t)(it / NSTAGE) & 1u;
     if (!wait_bar(&full[s], ph, kp.status)) break;
     const StageMeta& pm = meta[s];
-    const DevTensor& D = kp.T[pm.t];
-    uint8_t* st = stages + s * L::STAGE;
+    const uint8_t* st = stages + s * L::STAGE;
     // the fast path needs all 4 blocks of this warp present and full, and no
     // seam outputs; decided per warp so the shuffles stay convergent
-    const int bi = warp * 4 + (lane >> 3);
-    const bool mine_full = bi < pm.nblk && D.n - (pm.b0 + bi) * BS >= BS;
-    const bool fast = __all_sync(0xffffffffu, mine_full) &&
-                      !(D.flags & (DF_M_OUT | DF_V_OUT));
-    if (fast) {
-      const Sc c = load_sc(D);
-      p1_block<MK, VK, PT, UNI, TABLE, true>(D, pm, c, st, table, scr, kp);
-    } else {
-      p1_block_general<MK, VK, PT, UNI, TABLE>(pm, st, table, scr, kp);
-    }
-    fence_proxy_async_smem();
+    const int bi = 4 * (lane >> 3) + warp;
+    const bool mine_full = bi < pm.nblk && pm.n - (pm.b0 + bi) * BS >= BS;
+    const bool fast =
+        __all_sync(0xffffffffu, mine_full) && !(pm.c.flags & (DF_M_OUT | DF_V_OUT));
+    if (fast)
+      p1_block<MK, VK, PT, UNI, TABLE, true>(kp.T, pm, st, table, scr, ob, kp);
+    else
+      p1_block_general<MK, VK, PT, UNI, TABLE>(kp.T, pm, st, table, scr, ob, kp);
     __syncwarp();
     if (lane == 0) mbar_arrive(&done[s]);
   }
@@ -711,7 +716,8 @@ __global__ void __launch_bounds__(NTHR, 4) k_pass1(const __grid_constant__ KPara
 template <int MK, int VK, int PT, bool UNI>
 constexpr size_t p1_smem_bytes() {
   return (size_t)NSTAGE * P1L<MK, VK, PT, UNI>::STAGE + 2 * NSTAGE * 8 +
-         NSTAGE * sizeof(StageMeta) + NCW * 4 * TABLE_STRIDE * 4 + NCW * SCR_FLOATS * 4;
+         NSTAGE * sizeof(StageMeta) + NCW * 4 * TABLE_STRIDE * 4 + NCW * SCR_FLOATS * 4 +
+         NCW * OB_BYTES;
 }
 
 // ---------------------------------------------------------------------------
@@ -792,26 +798,27 @@ __global__ void __launch_bounds__(FIN_THREADS) k_alpha(const __grid_constant__ S
 // Pass 2: CoState encode (costate.py:419-425, :51-86, :213-258)
 // ---------------------------------------------------------------------------
 template <int PT, bool FULL>
-__device__ __forceinline__ void p2_block(const DevTensor& D, const StageMeta& M, const Sc& c,
-                                         uint8_t* st) {
+__device__ __forceinline__ void p2_block(const DevTensor* T, const StageMeta& M,
+                                         const uint8_t* st) {
   using L = P2L<PT>;
-  const int nblk = M.nblk;
-  const int64_t b0 = M.b0;
+  const float b1 = M.c.b1, omb1 = M.c.omb1, sqbs = M.c.sqbs;
+  const uint32_t flags = M.c.flags;
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int q = lane >> 3;
   const int j = lane & 7;
-  const int bi = warp * 4 + q;
-  const bool active = FULL || bi < nblk;
-  const int64_t b = b0 + bi;
+  const int bi = 4 * q + warp;
+  const bool active = FULL || bi < M.nblk;
+  const int64_t b = M.b0 + bi;
   const int64_t e0 = b * BS;
-  const int nv = FULL ? BS : (active ? (int)min((int64_t)BS, D.n - e0) : 0);
+  const int nv = FULL ? BS : (active ? (int)min((int64_t)BS, M.n - e0) : 0);
   const bool fullblk = FULL || nv == BS;
   const uint32_t gbase = lane & ~7u;
-  const uint8_t* sg = st + L::OFF_G + bi * L::STR_G;
+  const uint8_t* sg = st + L::OFF_G + L::AG::off(bi);
   const uint32_t* sgnw = reinterpret_cast<const uint32_t*>(st + L::OFF_SGN + bi * 16);
+  const DevTensor* D = FULL ? nullptr : &T[M.t];  // tail loads and seam outputs only
 
-  const bool has_state = c.flags & DF_M_HAS_STATE;
+  const bool has_state = flags & DF_M_HAS_STATE;
   float cs_scale = 0.0f;
   const float alpha_old = M.alpha_old;
   const float alpha = M.alpha_new;
@@ -819,7 +826,7 @@ __device__ __forceinline__ void p2_block(const DevTensor& D, const StageMeta& M,
     const uint8_t lab = st[L::OFF_LAB + bi];
     const float nrm = reinterpret_cast<const float*>(st + L::OFF_NRM)[bi];
     const uint16_t amp = reinterpret_cast<const uint16_t*>(st + L::OFF_AMP)[bi];
-    cs_scale = costate_scale(lab, nrm, amp, c.sqbs);
+    cs_scale = costate_scale(lab, nrm, amp, sqbs);
   }
   float accd = 0.0f, accm = 0.0f;
   uint32_t myw = 0;
@@ -832,18 +839,17 @@ __device__ __forceinline__ void p2_block(const DevTensor& D, const StageMeta& M,
       const int t = j + 8 * k;
       const bool ve = FULL || t < nv;
       float g;
-      if (fullblk) g = PT ? ta_bf16_to_f32(reinterpret_cast<const uint16_t*>(sg)[t])
-                          : reinterpret_cast<const float*>(sg)[t];
-      else g = ve ? to_f32<PT>(D.g, e0 + t) : 0.0f;
+      if (fullblk) g = ld_smem_elem<PT>(sg, t);
+      else g = ve ? to_f32<PT>(D->g, e0 + t) : 0.0f;
       const uint32_t bit = (sw >> (8 * i + 7 - j)) & 1u;
-      const float m = costate_m(g, alpha_old, cs_scale, bit, has_state, c.b1, c.omb1);
+      const float m = costate_m(g, alpha_old, cs_scale, bit, has_state, b1, omb1);
       const float dl = ve ? __fsub_rn(m, __fmul_rn(alpha, g)) : 0.0f;  // costate.py:42
       const float mm = ve ? m : 0.0f;
       accd = __fadd_rn(accd, __fmul_rn(dl, dl));
       accm = __fadd_rn(accm, __fmul_rn(mm, mm));
       const uint32_t w = __ballot_sync(0xffffffffu, dl < 0.0f);
       myw = (lane == k) ? w : myw;
-      if (!FULL && ve && (c.flags & DF_M_OUT)) D.m_out[e0 + t] = m;
+      if (!FULL && ve && (flags & DF_M_OUT)) D->m_out[e0 + t] = m;
     }
   }
   // torch row-norm order: lane accumulators summed 0..7 in sequence
@@ -862,27 +868,25 @@ __device__ __forceinline__ void p2_block(const DevTensor& D, const StageMeta& M,
   if (active) {
     const uint32_t by0 = __brev((w0 >> (8 * q)) & 0xffu) >> 24;
     const uint32_t by1 = __brev((w1 >> (8 * q)) & 0xffu) >> 24;
-    reinterpret_cast<uint16_t*>(st + L::OFF_SGN + bi * 16)[j] = (uint16_t)(by0 | (by1 << 8));
+    reinterpret_cast<uint16_t*>(M.sgn + b * 16)[j] = (uint16_t)(by0 | (by1 << 8));
     if (j == 0) {
-      reinterpret_cast<float*>(st + L::OFF_NRM)[bi] = dn;
-      reinterpret_cast<uint16_t*>(st + L::OFF_AMP)[bi] = ta_f32_to_f16(__fdiv_rn(dn, c.sqbs));
-      reinterpret_cast<float*>(st + L::OFF_RAT)[bi] =
-          (mnorm == 0.0f) ? 0.0f : __fdiv_rn(dn, mnorm);
+      M.nrm[b] = dn;
+      M.amp[b] = ta_f32_to_f16(__fdiv_rn(dn, sqbs));
+      M.ratios[b] = (mnorm == 0.0f) ? 0.0f : __fdiv_rn(dn, mnorm);
     }
   }
 }
 
 template <int PT>
-__device__ __noinline__ void p2_block_general(const StageMeta& M, uint8_t* st,
-                                              const DevTensor* T) {
-  const DevTensor& D = T[M.t];
-  const Sc c = load_sc(D);
-  p2_block<PT, false>(D, M, c, st);
+__device__ __noinline__ void p2_block_general(const DevTensor* T, const StageMeta& M,
+                                              const uint8_t* st) {
+  p2_block<PT, false>(T, M, st);
 }
 
 template <int PT>
 __global__ void __launch_bounds__(NTHR) k_pass2(const __grid_constant__ KParams kp) {
   using L = P2L<PT>;
+  using AG = typename L::AG;
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* stages = smem;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + NSTAGE2 * L::STAGE);
@@ -899,57 +903,46 @@ __global__ void __launch_bounds__(NTHR) k_pass2(const __grid_constant__ KParams 
   }
   __syncthreads();
 
-  auto store = [&](uint8_t* st, const StageMeta& pm) {
-    const DevTensor& D = kp.T[pm.t];
-    bulk_s2g(D.sgn + pm.b0 * 16, st + L::OFF_SGN, TB * 16);
-    bulk_s2g(D.nrm + pm.b0, st + L::OFF_NRM, TB * 4);
-    bulk_s2g(D.amp + pm.b0, st + L::OFF_AMP, TB * 2);
-    bulk_s2g(D.ratios + pm.b0, st + L::OFF_RAT, TB * 4);
-  };
-
-  if (warp == NCW) {
+  if (warp == NCW) {  // producer
     if (lane == 0) {
       int it = 0;
-      bool ok = true;
       EntryWalk walk;
       int cur_t = -1;
       float cur_aold = 0.0f, cur_anew = 0.0f;
+      Sc cur_c;
       for (int64_t tile = blockIdx.x; tile < kp.total; tile += gridDim.x, ++it) {
         const int s = it % NSTAGE2;
         const uint32_t ph = (uint32_t)(it / NSTAGE2) & 1u;
         uint8_t* st = stages + s * L::STAGE;
-        if (it >= NSTAGE2) {
-          if (!wait_bar(&done[s], ph ^ 1u, kp.status)) { ok = false; break; }
-          store(st, meta[s]);
-          bulk_commit();
-          bulk_wait_read_all();
-        }
         const int en = walk.at(kp.lbeg, kp.nl, tile);
         const int t = kp.lidx[en];
         const DevTensor& D = kp.T[t];
         if (t != cur_t) {
           cur_t = t;
+          cur_c = load_sc(D);
           cur_aold = (D.flags & DF_M_HAS_STATE) ? *D.alpha_state : 0.0f;
           cur_anew = *D.alpha_new;
         }
         const int64_t b0 = (tile - kp.lbeg[en]) * TB;
         const int nblk = (int)min((int64_t)TB, D.nblk - b0);
-        meta[s].t = t;
-        meta[s].nblk = nblk;
-        meta[s].b0 = b0;
-        meta[s].alpha_old = cur_aold;
-        meta[s].alpha_new = cur_anew;
-        uint32_t bytes = 0;
-        for (int i = 0; i < nblk; ++i)
-          if (D.n - (b0 + i) * BS >= BS) bytes += BS * L::ESZ;
         const bool hs = D.flags & DF_M_HAS_STATE;
-        if (hs) bytes += 16 + TB * 16 + TB * 4 + TB * 2;
+        const int64_t nfull = min((int64_t)nblk, (D.n - b0 * BS) / BS);
+        const uint32_t bytes =
+            (uint32_t)nfull * AG::BLK + (hs ? 16 + TB * 16 + TB * 4 + TB * 2 : 0);
+        if (it >= NSTAGE2 && !wait_bar(&done[s], ph ^ 1u, kp.status)) break;
+        StageMeta& m = meta[s];
+        fill_meta_common(m, D, cur_c, t, nblk, b0, cur_aold);
+        m.alpha_new = cur_anew;
+        m.sgn = D.sgn;
+        m.nrm = D.nrm;
+        m.amp = D.amp;
+        m.ratios = D.ratios;
         mbar_arrive_expect_tx(&full[s], bytes);
-        for (int i = 0; i < nblk; ++i) {
-          const int64_t e0 = (b0 + i) * BS;
-          if (D.n - e0 >= BS)
-            bulk_g2s(st + L::OFF_G + i * L::STR_G, (const uint8_t*)D.g + e0 * L::ESZ,
-                     BS * L::ESZ, &full[s]);
+        for (int cb = 0; cb < 4; ++cb) {
+          const int cnt = (int)max((int64_t)0, min((int64_t)4, nfull - 4 * cb));
+          if (cnt > 0)
+            bulk_g2s(st + L::OFF_G + cb * AG::CSTR,
+                     (const uint8_t*)D.g + (b0 + 4 * cb) * BS * L::ESZ, cnt * AG::BLK, &full[s]);
         }
         if (hs) {
           bulk_g2s(st + L::OFF_LAB, D.lab + b0, 16, &full[s]);
@@ -959,18 +952,8 @@ __global__ void __launch_bounds__(NTHR) k_pass2(const __grid_constant__ KParams 
         }
       }
       const int first = it > NSTAGE2 ? it - NSTAGE2 : 0;
-      if (ok) {
-        for (int r = first; r < it; ++r) {
-          const int s = r % NSTAGE2;
-          if (!wait_bar(&done[s], (uint32_t)(r / NSTAGE2) & 1u, kp.status)) { ok = false; break; }
-          store(stages + s * L::STAGE, meta[s]);
-          bulk_commit();
-        }
-      }
-      if (!ok)
-        for (int r = first; r < it; ++r)
-          wait_bar(&full[r % NSTAGE2], (uint32_t)(r / NSTAGE2) & 1u, kp.status);
-      bulk_wait_all();
+      for (int r = first; r < it; ++r)
+        wait_bar(&full[r % NSTAGE2], (uint32_t)(r / NSTAGE2) & 1u, kp.status);
     }
     return;
   }
@@ -980,18 +963,12 @@ __global__ void __launch_bounds__(NTHR) k_pass2(const __grid_constant__ KParams 
     const uint32_t ph = (uint32_t)(it / NSTAGE2) & 1u;
     if (!wait_bar(&full[s], ph, kp.status)) break;
     const StageMeta& pm = meta[s];
-    const DevTensor& D = kp.T[pm.t];
-    uint8_t* st = stages + s * L::STAGE;
-    const int bi = warp * 4 + (lane >> 3);
-    const bool mine_full = bi < pm.nblk && D.n - (pm.b0 + bi) * BS >= BS;
-    const bool fast = __all_sync(0xffffffffu, mine_full) && !(D.flags & DF_M_OUT);
-    if (fast) {
-      const Sc c = load_sc(D);
-      p2_block<PT, true>(D, pm, c, st);
-    } else {
-      p2_block_general<PT>(pm, st, kp.T);
-    }
-    fence_proxy_async_smem();
+    const uint8_t* st = stages + s * L::STAGE;
+    const int bi = 4 * (lane >> 3) + warp;
+    const bool mine_full = bi < pm.nblk && pm.n - (pm.b0 + bi) * BS >= BS;
+    const bool fast = __all_sync(0xffffffffu, mine_full) && !(pm.c.flags & DF_M_OUT);
+    if (fast) p2_block<PT, true>(kp.T, pm, st);
+    else p2_block_general<PT>(kp.T, pm, st);
     __syncwarp();
     if (lane == 0) mbar_arrive(&done[s]);
   }
