@@ -120,7 +120,7 @@ def pass1_bytes(n, kw, psize=4):
 
 
 def step_bytes(n, kw, psize=4):
-    """Single-touch algorithmic bytes of the whole step (SURVEY 8d figures:
+    """Single-touch algorithmic bytes of the whole step (figures:
     14.42 B/param for 4-bit + CoState fp32, 22.06 v-only fp32)."""
     costate, oneq = kind_of(n, kw)
     B = (n + 127) // 128
@@ -292,8 +292,10 @@ def measured_peak():
 
 
 def profiled_traffic(config):
-    """Per-param DRAM bytes of pass 1 from the committed ncu summary, if any."""
-    p = os.path.join(ROOT, "profiles", "k_pass1_ncu.txt")
+    """Per-param DRAM bytes of pass 1 from the committed ncu summary (a
+    GPT-2 124M capture; the traffic per element does not depend on the tensor
+    count, so it scales to a full launch by the elements processed)."""
+    p = os.path.join(ROOT, "profiles", "k_pass1_gpt2-124m.txt")
     if not os.path.exists(p):
         return None
     for line in open(p):

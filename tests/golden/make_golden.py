@@ -287,9 +287,12 @@ def gen_optimizer_runs(mods, out_dir):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("TURBOADAM_REF", "/root/reference"))
+    ap.add_argument("--ref", default=os.environ.get("TURBOADAM_REF"),
+                    help="checkout of the reference repository (or set TURBOADAM_REF)")
     ap.add_argument("--out", default=os.path.dirname(os.path.abspath(__file__)))
     a = ap.parse_args()
+    if not a.ref:
+        ap.error("--ref (or TURBOADAM_REF) must name the reference checkout")
     torch.set_num_threads(1)
     mods = _import_reference(a.ref)
     gen_v_cases(mods, a.out)

@@ -28,7 +28,7 @@ def p_close(ours, ref, update_scale, rtol=1e-6):
     """Parameter agreement: |ours - ref| <= rtol * (|ref| + update_scale).
 
     ``update_scale`` is the largest per-element update the reference applied
-    so far, so elements where p crosses zero are judged against the update
+    so far, so elements where p crosses zero are compared against the update
     size, not against |p| ~ 0.
     """
     ours = np.asarray(ours, np.float64)
