@@ -166,6 +166,29 @@ TA_API ta_status ta_v_update(const uint8_t* idx_dev, const uint16_t* hdr_dev, co
                       uint16_t* out_hdr_dev, float* v_out_dev, void* workspace_dev,
                       size_t workspace_bytes, void* stream);
 
+/*
+ * ta_v_update without a caller workspace. No counterpart in the reference:
+ * the scratch that ta_v_update carves from workspace_dev lives in a
+ * file-scope static device array of TA_V_UPDATE_NOALLOC_SCRATCH_BYTES per
+ * device, so the call allocates no device memory. n above
+ * TA_V_UPDATE_NOALLOC_MAX_N is rejected with TA_ERR_UNSUPPORTED.
+ * The first call on a device (with that device current) looks up the array
+ * and zeroes it on `stream`; make it before any stream capture. The status
+ * word at the start of the array starts at zero that way; every other
+ * scratch byte is written by the call before it is read.
+ * All calls on one device share the array: calls that can overlap (other
+ * streams, other host threads, without ordering) race; serialise them.
+ * Arguments and results as ta_v_update.
+ */
+#define TA_V_UPDATE_NOALLOC_MAX_N ((int64_t)1 << 20)
+#define TA_V_UPDATE_NOALLOC_SCRATCH_BYTES ((size_t)5 << 18) /* 1.25 MiB */
+TA_API ta_status ta_v_update_noalloc(const uint8_t* idx_dev, const uint16_t* hdr_dev,
+                                     const void* grad_dev, int32_t grad_dtype, int64_t n,
+                                     int32_t block_size, int32_t v_bits, double beta2,
+                                     const float* uniforms_dev, uint64_t seed,
+                                     uint32_t tensor_id, uint32_t step, uint8_t* out_idx_dev,
+                                     uint16_t* out_hdr_dev, float* v_out_dev, void* stream);
+
 /* 1Q state of a fresh tensor: compress_v_logscale(full(1e-30)) as done at
  * optimizer.py:273-280 (all indices 0, both headers fp16(ln 1e-30)). */
 TA_API ta_status ta_v_init(int64_t n, int32_t block_size, uint8_t* idx_dev, uint16_t* hdr_dev,

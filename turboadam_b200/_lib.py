@@ -43,6 +43,7 @@ EXPORTED = (
     "ta_step_profiled",
     "ta_read_status",
     "ta_v_update",
+    "ta_v_update_noalloc",
     "ta_v_init",
     "ta_v_decode",
     "ta_costate_decode",
@@ -139,6 +140,10 @@ _SIG = {
                                    ctypes.c_int32, ctypes.c_double, _P, ctypes.c_uint64,
                                    ctypes.c_uint32, ctypes.c_uint32, _P, _P, _P, _P,
                                    ctypes.c_size_t, _P]),
+    "ta_v_update_noalloc": (ctypes.c_int, [_P, _P, _P, ctypes.c_int32, ctypes.c_int64,
+                                           ctypes.c_int32, ctypes.c_int32, ctypes.c_double, _P,
+                                           ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32,
+                                           _P, _P, _P, _P]),
     "ta_v_init": (ctypes.c_int, [ctypes.c_int64, ctypes.c_int32, _P, _P, _P]),
     "ta_v_decode": (ctypes.c_int, [_P, _P, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, _P,
                                    _P]),

@@ -681,3 +681,65 @@ ta_status ta_thresholds(const float* ratios_dev, int64_t n_blocks, double null_p
 }
 
 }  // extern "C"
+
+// ---- ta_v_update_noalloc: ta_v_update's scratch in a static device array --
+// One instance per device (module globals are per context). The pointer is
+// looked up once per device, with that device current, and cached.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[TA_V_UPDATE_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+// Set-up on the first call per device: symbol address (return code checked)
+// and one zeroing of the array on the caller's stream.
+ta_status noalloc_scratch(cudaStream_t st, void** out) {
+  int dev = -1;
+  TA_CU(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kNoAllocMaxDevices)
+    return fail(TA_ERR_UNSUPPORTED, "device ordinal " + std::to_string(dev) +
+                                        " above the static scratch table");
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      return fail(TA_ERR_CUDA, std::string("cudaGetSymbolAddress(static scratch): ") +
+                                   cudaGetErrorString(e));
+    TA_CU(cudaMemsetAsync(p, 0, TA_V_UPDATE_NOALLOC_SCRATCH_BYTES, st));
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return TA_OK;
+}
+}  // namespace
+
+extern "C" {
+
+ta_status ta_v_update_noalloc(const uint8_t* idx_dev, const uint16_t* hdr_dev,
+                              const void* grad_dev, int32_t grad_dtype, int64_t n,
+                              int32_t block_size, int32_t v_bits, double beta2,
+                              const float* uniforms_dev, uint64_t seed, uint32_t tensor_id,
+                              uint32_t step, uint8_t* out_idx_dev, uint16_t* out_hdr_dev,
+                              float* v_out_dev, void* stream) {
+  g_err.clear();
+  if (n > TA_V_UPDATE_NOALLOC_MAX_N)
+    return fail(TA_ERR_UNSUPPORTED,
+                "n = " + std::to_string(n) + " exceeds the static scratch limit of " +
+                    std::to_string(TA_V_UPDATE_NOALLOC_MAX_N) +
+                    " elements (TA_V_UPDATE_NOALLOC_MAX_N); use ta_v_update with a workspace");
+  if (n > 0 && ta_aux_workspace_size(n) > TA_V_UPDATE_NOALLOC_SCRATCH_BYTES)
+    return fail(TA_ERR_UNSUPPORTED, "n = " + std::to_string(n) +
+                                        " needs more scratch than the static array holds");
+  void* scratch = nullptr;
+  if (n > 0) {
+    const ta_status r = noalloc_scratch((cudaStream_t)stream, &scratch);
+    if (r != TA_OK) return r;
+  }
+  return ta_v_update(idx_dev, hdr_dev, grad_dev, grad_dtype, n, block_size, v_bits, beta2,
+                     uniforms_dev, seed, tensor_id, step, out_idx_dev, out_hdr_dev, v_out_dev,
+                     scratch, TA_V_UPDATE_NOALLOC_SCRATCH_BYTES, stream);
+}
+
+}  // extern "C"
