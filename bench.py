@@ -92,14 +92,9 @@ def numel(shape):
 
 
 def lpt_assign(shapes, world):
-    order = sorted(range(len(shapes)), key=lambda i: -numel(shapes[i][1]))
-    load = [0] * world
-    owner = [0] * len(shapes)
-    for i in order:
-        r = min(range(world), key=lambda k: load[k])
-        owner[i] = r
-        load[r] += numel(shapes[i][1])
-    return owner
+    from turboadam_b200.sharding import lpt_owners
+
+    return lpt_owners([numel(s) for _, s in shapes], world)
 
 
 def kind_of(n, kw):
@@ -320,19 +315,20 @@ def run_ours(args, rank, world, local_rank):
     if args.v_bits:
         kw["v_bits"] = args.v_bits
     owner = lpt_assign(shapes, world)
-    mine = [s for i, s in enumerate(shapes) if owner[i] == rank]
+    my_ids = [i for i in range(len(shapes)) if owner[i] == rank]
+    mine = [shapes[i] for i in my_ids]
     total_params = sum(numel(s) for _, s in shapes)
     my_params = sum(numel(s) for _, s in mine)
     gen = torch.Generator(device=dev)
-    gen.manual_seed(1234 + rank)
     params = []
-    for _, shp in mine:
-        p = torch.empty(shp, dtype=torch.float32, device=dev)
+    for i in my_ids:  # data keyed by the global tensor index: same at every world size
+        gen.manual_seed(1234 + i)
+        p = torch.empty(shapes[i][1], dtype=torch.float32, device=dev)
         p.normal_(0.0, 0.02, generator=gen)
         p = torch.nn.Parameter(p)
         p.grad = torch.empty_like(p).normal_(0.0, cfg["grad_std"], generator=gen)
         params.append(p)
-    opt = TurboAdam(params, betas=(0.9, 0.999), seed=2024, **kw)
+    opt = TurboAdam(params, betas=(0.9, 0.999), seed=2024, tensor_ids=my_ids, **kw)
     stream = torch.cuda.current_stream(dev)
 
     def barrier():

@@ -1,0 +1,187 @@
+"""By-tensor sharding over data-parallel ranks (the multi-GPU path of the step).
+
+* the LPT owner assignment is a deterministic pure function of the sizes and
+  balances the Llama-3-8B-shaped set;
+* world_size-2 ``gloo`` ranks on CPU: each rank replays the step (checker)
+  on its own shard with global tensor ids, and the gathered packed state is
+  bit-identical to the unsharded replay; the max-over-ranks timing reduction
+  behaves as the bench uses it;
+* on a GPU: ``TurboAdam(shard, tensor_ids=global ids)`` reproduces the
+  unsharded optimizer's state for those tensors bit for bit.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from turboadam_b200.sharding import lpt_owners, rank_loads, shard_by_tensor
+
+SHAPES = [(768,), (768, 2304), (2304,), (768, 768), (3072, 768), (768, 3072), (3072,),
+          (50, 768), (4096,), (1000, 129), (777,), (96, 70)]
+
+
+def llama3_8b_numels():
+    d, kv, ffn, vocab = 4096, 1024, 14336, 128256
+    layer = [d * d, kv * d, kv * d, d * d, ffn * d, ffn * d, d * ffn, d, d]
+    return [vocab * d] + layer * 32 + [d, vocab * d]
+
+
+def test_lpt_owners_deterministic_and_balanced():
+    n = llama3_8b_numels()
+    for world in (1, 2, 4, 8):
+        own = lpt_owners(n, world)
+        assert own == lpt_owners(list(n), world)
+        assert set(own) == set(range(world))
+        loads = rank_loads(n, world)
+        assert sum(loads) == sum(n)
+        # LPT: no rank exceeds the mean by more than the largest tensor
+        assert max(loads) - sum(n) / world <= max(n)
+        assert max(loads) / (sum(n) / world) < 1.02
+    with pytest.raises(ValueError):
+        lpt_owners(n, 0)
+
+
+def test_shard_by_tensor_partitions():
+    ts = [torch.empty(s) for s in SHAPES]
+    seen = []
+    for r in range(3):
+        local, ids = shard_by_tensor(ts, 3, r)
+        assert [t.shape for t in local] == [ts[i].shape for i in ids]
+        seen += ids
+    assert sorted(seen) == list(range(len(ts)))
+    with pytest.raises(ValueError):
+        shard_by_tensor(ts, 2, 2)
+
+
+def _replay(oracle, ids, nsteps, seed=77):
+    """Checker replay of the step over the tensors ``ids`` (global indices),
+    4-bit v + CoState, Philox draws keyed by the global index."""
+    params = []
+    for i in ids:
+        rng = np.random.default_rng(1000 + i)
+        params.append(oracle.OracleParam(
+            (rng.standard_normal(int(np.prod(SHAPES[i]))) * 0.02).astype(np.float32)))
+    opt = oracle.OracleTurboAdam([oracle.OracleTurboAdam.make_group(
+        params, lr=6e-4, weight_decay=0.01, v_bits=4)])
+    for s in range(nsteps):
+        for i, p in zip(ids, params):
+            rng = np.random.default_rng(10_000 * (s + 1) + i)
+            p.grad = (rng.standard_normal(p.n) * 1e-3).astype(np.float32)
+        opt.step(uniforms=lambda oi, st, npad: oracle.sr_uniforms(params[oi].n, ids[oi], st,
+                                                                   seed))
+    out = {}
+    for i, p in zip(ids, params):
+        st = opt.state[id(p)]
+        rec = {"p": p.data.copy(), "idx": st.v_idx.copy(), "hdr": st.v_hdr.copy()}
+        if st.compress_m:
+            m = st.mgr
+            rec.update(alpha=np.array([m.alpha], np.float32), labels=m.labels.copy(),
+                       signs=m.signs.copy(), norms=m.norms.copy(), amp=m.amp.copy())
+        else:
+            rec["exp_avg"] = st.exp_avg.copy()
+        out[i] = rec
+    return out
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, q):
+    import sys
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.abspath(__file__)), ".."))
+    from oracle import oracle as O
+
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        own = lpt_owners([int(np.prod(s)) for s in SHAPES], world)
+        mine = [i for i, o in enumerate(own) if o == rank]
+        # every rank computes the same owners without communication
+        allown = [None] * world
+        dist.all_gather_object(allown, own)
+        assert all(a == own for a in allown)
+        res = _replay(O, mine, nsteps=3)
+        gathered = [None] * world
+        dist.all_gather_object(gathered, res)
+        # max-over-ranks timing as the bench reduces it
+        t = torch.tensor([1.5 + rank])
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        if rank == 0:
+            merged = {}
+            for g in gathered:
+                merged.update(g)
+            q.put((sorted(merged), merged, float(t[0])))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gloo_two_ranks_match_unsharded(oracle):
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    keys, merged, tmax = q.get(timeout=240)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert keys == list(range(len(SHAPES)))
+    assert tmax == 2.5
+    ref = _replay(oracle, list(range(len(SHAPES))), nsteps=3)
+    for i in keys:
+        for k, v in ref[i].items():
+            np.testing.assert_array_equal(np.asarray(merged[i][k]).view(np.uint8),
+                                          np.asarray(v).view(np.uint8), err_msg=f"{i} {k}")
+
+
+@pytest.mark.gpu
+def test_turboadam_shard_with_global_ids_matches_unsharded():
+    from turboadam_b200 import TurboAdam
+
+    def make(ids):
+        ps = []
+        for i in ids:
+            g = torch.Generator().manual_seed(500 + i)
+            ps.append(torch.nn.Parameter((torch.randn(SHAPES[i], generator=g) * 0.02).cuda()))
+        return ps
+
+    def run(opt, ps, ids):
+        for s in range(3):
+            for i, p in zip(ids, ps):
+                g = torch.Generator().manual_seed(9000 * (s + 1) + i)
+                p.grad = (torch.randn(SHAPES[i], generator=g) * 1e-3).cuda()
+            opt.step()
+        torch.cuda.synchronize()
+
+    all_ids = list(range(len(SHAPES)))
+    full = make(all_ids)
+    ofull = TurboAdam(full, lr=6e-4, weight_decay=0.01, seed=5)
+    run(ofull, full, all_ids)
+    for rank in range(2):
+        _, ids = shard_by_tensor(full, 2, rank)
+        part = make(ids)
+        opart = TurboAdam(part, lr=6e-4, weight_decay=0.01, seed=5, tensor_ids=ids)
+        run(opart, part, ids)
+        for p, i in zip(part, ids):
+            q = full[i]
+            assert torch.equal(p.data.view(torch.int32), q.data.view(torch.int32)), i
+            a, b = opart.state[p], ofull.state[q]
+            assert torch.equal(a["compressed_v"]["indices"], b["compressed_v"]["indices"]), i
+            if "m_mgr" in a:
+                ea, eb = a["m_mgr"]._encoded, b["m_mgr"]._encoded
+                for k in ("labels", "sign_packed"):
+                    assert torch.equal(ea[k], eb[k]), (i, k)
+    with pytest.raises(ValueError):
+        TurboAdam(full, tensor_ids=[0])

@@ -30,8 +30,14 @@ _DTYPES = {torch.float32: _lib.TA_F32, torch.bfloat16: _lib.TA_BF16}
 class TurboAdam(Optimizer):
     """Adam with CoState-compressed m and 1Q log-scale v (reference API).
 
-    Args mirror the reference (optimizer.py:44-81). ``seed`` (keyword-only,
-    extra) keys the stochastic-rounding generator; default torch.initial_seed().
+    Args mirror the reference (optimizer.py:44-81). Keyword-only extras:
+    ``seed`` keys the stochastic-rounding generator (default
+    torch.initial_seed()); ``tensor_ids`` gives each parameter (in the order
+    the constructor's param groups list them) the id that keys its rounding
+    stream -- by default its position in that order. A rank that steps a
+    shard of a larger parameter set passes the shard's global indices
+    (``turboadam_b200.sharding.shard_by_tensor``) so its packed state matches
+    the unsharded run bit for bit.
     """
 
     def __init__(
@@ -52,6 +58,7 @@ class TurboAdam(Optimizer):
         min_m_compress_elements: int = 4096,
         *,
         seed: int | None = None,
+        tensor_ids=None,
     ):
         if v_bits not in (2, 3, 4, 6, 8):
             raise ValueError(f"v_bits must be one of {{2, 3, 4, 6, 8}}, got {v_bits}")
@@ -75,6 +82,16 @@ class TurboAdam(Optimizer):
         super().__init__(params, defaults)
         self._group_step_tensors = {}
         self._seed = (torch.initial_seed() if seed is None else int(seed)) & 0xFFFFFFFFFFFFFFFF
+        self._tid_override = None
+        if tensor_ids is not None:
+            flat = [p for g in self.param_groups for p in g["params"]]
+            tensor_ids = [int(t) for t in tensor_ids]
+            if len(tensor_ids) != len(flat):
+                raise ValueError(f"tensor_ids has {len(tensor_ids)} entries for "
+                                 f"{len(flat)} parameters")
+            if any(t < 0 or t > 0xFFFFFFFF for t in tensor_ids):
+                raise ValueError("tensor_ids must be 32-bit unsigned integers")
+            self._tid_override = {id(p): t for p, t in zip(flat, tensor_ids)}
         self._plans = None
         self._ws = {}
         # test hook: {"uniforms": {param: fp32 [B*128] cuda}, "alpha": {param: fp32 [1] cuda}}
@@ -205,9 +222,10 @@ class TurboAdam(Optimizer):
     def _tensor_ids(self):
         ids = {}
         i = 0
+        over = self._tid_override or {}
         for group in self.param_groups:
             for p in group["params"]:
-                ids.setdefault(id(p), i)
+                ids.setdefault(id(p), over.get(id(p), i))
                 i += 1
         return ids
 
