@@ -199,10 +199,11 @@ def cpu_sample(cfg_name, target_s=15.0):
     from oracle import oracle as O
 
     O.build()
+    threads = len(os.sched_getaffinity(0))
+    O.set_threads(threads)
     cfg = CONFIGS[cfg_name]
     shapes = cfg["shapes"]()
     kw = cfg["kw"]
-    threads = os.cpu_count() or 1
     rng = np.random.default_rng(0)
     # sample: one transformer layer for llama, the whole set for small configs
     pick = _cpu_pick(cfg_name, shapes)
@@ -243,6 +244,7 @@ def run_reference(args, rank, world):
     from oracle import oracle as O
 
     O.build()
+    O.set_threads(len(os.sched_getaffinity(0)))  # all host cores (torchrun sets 1)
     shapes = cfg["shapes"]()
     pick = _cpu_pick(args.config, shapes)
     rng = np.random.default_rng(0)

@@ -76,6 +76,7 @@ def _declare(L):
         "orc_scan_log": (_D, [_U32, _U32, _P]),
         "orc_scan_exp": (_D, [_U32, _U32, _P]),
         "orc_threads": (_I, []),
+        "orc_set_threads": (None, [_I]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -154,6 +155,10 @@ def sr_uniforms(n: int, tensor_id: int, step: int, seed: int, bs: int = BLOCK_SI
 
 def threads() -> int:
     return int(lib().orc_threads())
+
+
+def set_threads(n: int) -> None:
+    lib().orc_set_threads(int(n))
 
 
 def philox(ctr, key):
