@@ -71,6 +71,7 @@ def _declare(L):
         "orc_sr_uniforms": (None, [_I64, _I, _U32, _U32, _U64, _P]),
         "orc_philox": (None, [_U32, _U32, _U32, _U32, _U32, _U32, _P]),
         "orc_logf_array": (None, [_P, _I64, _P]),
+        "orc_logf_fast_array": (None, [_P, _I64, _P]),
         "orc_expf_array": (None, [_P, _I64, _P]),
         "orc_f32_to_f16_array": (None, [_P, _I64, _P]),
         "orc_scan_log": (_D, [_U32, _U32, _P]),
@@ -171,6 +172,13 @@ def logf(x):
     x = np.ascontiguousarray(x, np.float32)
     y = np.empty_like(x)
     lib().orc_logf_array(_ptr(x), x.size, _ptr(y))
+    return y
+
+
+def logf_fast(x):
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.empty_like(x)
+    lib().orc_logf_fast_array(_ptr(x), x.size, _ptr(y))
     return y
 
 

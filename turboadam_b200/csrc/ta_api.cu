@@ -274,6 +274,7 @@ DevTensor make_dev(const ta_tensor& t, const ta_group& g, uint64_t seed) {
   D.seed_hi = (uint32_t)(seed >> 32);
   D.sel_chunks = (int32_t)cdiv(D.bpad, SEL_CHUNK);
   D.alpha_chunks = (int32_t)cdiv(D.bpad / TB, FIN_THREADS);
+  D.one = 1.0f;
   return D;
 }
 

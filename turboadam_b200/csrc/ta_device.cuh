@@ -79,6 +79,7 @@ struct __align__(16) DevTensor {
   uint32_t seed_lo, seed_hi;
   int32_t sel_chunks;  // ceil(bpad / SEL_CHUNK)
   int32_t alpha_chunks;  // ceil(tiles / FIN_THREADS)
+  float one;           // 1.0f, stored by the host (a runtime identity operand)
 };
 
 // sel[] layout

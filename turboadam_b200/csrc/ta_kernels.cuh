@@ -60,23 +60,27 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, uint32_
 
 // ---------------------------------------------------------------------------
 // Stage layouts. A per-element array holds the tile's 16 blocks as 4 copies
-// of 4 consecutive blocks; copy c starts at c * (4 * block bytes + skew).
+// of 4 consecutive blocks; copy c starts at c * (4 * block bytes + SKEW).
+// The skews keep the 4 groups of a warp (4 different copies) on disjoint
+// banks for each pass's access width: pass 1 reads 4 consecutive elements per
+// lane (16-byte fp32 / 8-byte bf16 / 4-byte index loads), pass 2 one element.
 // ---------------------------------------------------------------------------
-template <int ESZ>
+template <int ESZ, int SKEW_>
 struct Arr {
   static constexpr int BLK = BS * ESZ;                      // bytes per block
-  static constexpr int SKEW = (8 * ESZ < 16) ? 16 : 8 * ESZ;
+  static constexpr int SKEW = SKEW_;
   static constexpr int CSTR = 4 * BLK + SKEW;               // bytes per 4-block copy
   static constexpr int BYTES = 4 * CSTR;
+  static_assert(CSTR % 16 == 0, "bulk copies need 16-byte aligned destinations");
   __device__ __forceinline__ static int off(int bi) { return (bi >> 2) * CSTR + (bi & 3) * BLK; }
 };
 
 template <int MK, int VK, int PT, bool UNI>
 struct P1L {
   static constexpr int ESZ = PT ? 2 : 4;
-  using AP = Arr<ESZ>;
-  using A4 = Arr<4>;
-  using A1 = Arr<1>;
+  using AP = Arr<ESZ, PT ? 64 : 32>;
+  using A4 = Arr<4, 32>;
+  using A1 = Arr<1, 32>;
   static constexpr int OFF_P = 0;
   static constexpr int OFF_G = OFF_P + AP::BYTES;
   static constexpr int OFF_IDX = OFF_G + AP::BYTES;
@@ -95,7 +99,7 @@ struct P1L {
 template <int PT>
 struct P2L {
   static constexpr int ESZ = PT ? 2 : 4;
-  using AG = Arr<ESZ>;
+  using AG = Arr<ESZ, PT ? 16 : 32>;
   static constexpr int OFF_G = 0;
   static constexpr int OFF_LAB = OFF_G + AG::BYTES;
   static constexpr int OFF_SGN = OFF_LAB + 16;
@@ -106,9 +110,7 @@ struct P2L {
 };
 
 constexpr int TABLE_STRIDE = 65;     // per-group exp table (<= 64 entries), padded
-constexpr int SCR_FLOATS = 16 * 32;  // per-warp scratch: ln v_new of 16 elements x 32 lanes
-constexpr int OB_STRIDE = BS + 16;   // per-group staging of the new 1Q indices (skewed)
-constexpr int OB_BYTES = 4 * OB_STRIDE;
+constexpr int SCR_FLOATS = 16 * 32;  // per-warp scratch: ln v_new, 4 quads x 32 lanes x 4
 
 // Per-tensor scalars (fp32 values of the Python hyper-parameters as torch
 // rounds them), carried in the stage metadata.
@@ -118,6 +120,9 @@ struct __align__(16) Sc {
   float bc2, rbc2, nbf, sqbs;
   uint32_t flags, tid, step;
   int32_t nbits;
+  float rnbf;   // 2^-nbits (exact)
+  float one;    // 1 and -0 as runtime values: the identity operands of PK
+  float nzero;
 };
 
 __device__ __forceinline__ Sc load_sc(const DevTensor& D) {
@@ -127,6 +132,9 @@ __device__ __forceinline__ Sc load_sc(const DevTensor& D) {
   s.nlr = D.nlr; s.eps = D.eps; s.bc1 = D.bc1; s.bc2 = D.bc2; s.rbc2 = D.rbc2;
   s.nbf = D.nbf; s.sqbs = D.sqbs;
   s.flags = D.flags; s.tid = D.tid; s.step = D.step; s.nbits = D.nbits;
+  s.rnbf = __uint_as_float((uint32_t)(127 - D.nbits) << 23);
+  s.one = D.one;
+  s.nzero = -0.0f * D.one;
   return s;
 }
 
@@ -299,6 +307,112 @@ __device__ __forceinline__ float adam_elem_ieee(float pv, float m, float vn, con
 }
 
 // ---------------------------------------------------------------------------
+// Packed fp32 pairs: the sm_100 fma.rn.f32x2 instruction does two IEEE
+// single-precision fmas per instruction, each rounded exactly like the scalar
+// fma, so pairing never changes a result -- it halves the issue slots of the
+// arithmetic. ptxas contracts a packed multiply followed by a packed add into
+// one fma (even with -fmad=false and .rn), which would drop a rounding, so
+// every pair operation here is issued as an fma whose identity operand (1, -1
+// or -0) is a runtime value it cannot see through (PK).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ unsigned long long pk2(float2 v) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(v.x), "f"(v.y));
+  return r;
+}
+__device__ __forceinline__ float2 upk2(unsigned long long r) {
+  float2 v;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(v.x), "=f"(v.y) : "l"(r));
+  return v;
+}
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  unsigned long long d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(pk2(a)), "l"(pk2(b)), "l"(pk2(c)));
+  return upk2(d);
+}
+// a + b = fma(a, 1, b); a - b = fma(b, -1, a); a * b = fma(a, b, -0): each is
+// the correctly rounded sum / difference / product, signed zeros included.
+struct PK {
+  float2 one, mone, nz;
+  __device__ __forceinline__ PK(float one_, float nzero_)
+      : one(make_float2(one_, one_)), mone(make_float2(-one_, -one_)),
+        nz(make_float2(nzero_, nzero_)) {}
+  __device__ __forceinline__ float2 add(float2 a, float2 b) const { return fma2(a, one, b); }
+  __device__ __forceinline__ float2 sub(float2 a, float2 b) const { return fma2(b, mone, a); }
+  __device__ __forceinline__ float2 mul(float2 a, float2 b) const { return fma2(a, b, nz); }
+};
+__device__ __forceinline__ float2 dup2(float a) { return make_float2(a, a); }
+__device__ __forceinline__ float2 lo2(float4 v) { return make_float2(v.x, v.y); }
+__device__ __forceinline__ float2 hi2(float4 v) { return make_float2(v.z, v.w); }
+__device__ __forceinline__ float4 cat4(float2 a, float2 b) { return make_float4(a.x, a.y, b.x, b.y); }
+
+// ta_logf for x in [2^-126, FLT_MAX], two at a time: the same operations as
+// log_clamped without the clamp and the special-case selects. For x = 0 or a
+// subnormal x the result is below -69.3 (checked exhaustively by the tests),
+// which the caller's range flag catches; other inputs never reach it unflagged.
+__device__ __forceinline__ float2 log_fast2(float2 x, const PK& P) {
+  const uint32_t ix0 = __float_as_uint(x.x), ix1 = __float_as_uint(x.y);
+  const int32_t e0 = ((int32_t)(ix0 - 0x3f2aaaabu)) >> 23;
+  const int32_t e1 = ((int32_t)(ix1 - 0x3f2aaaabu)) >> 23;
+  const float2 m = make_float2(__uint_as_float(ix0 - ((uint32_t)e0 << 23)),
+                               __uint_as_float(ix1 - ((uint32_t)e1 << 23)));
+  const float2 f = P.sub(m, dup2(1.0f));
+  const float2 ef = make_float2((float)e0, (float)e1);
+  float2 q = dup2(TA_LOG_Q0);
+  q = fma2(q, f, dup2(TA_LOG_Q1));
+  q = fma2(q, f, dup2(TA_LOG_Q2));
+  q = fma2(q, f, dup2(TA_LOG_Q3));
+  q = fma2(q, f, dup2(TA_LOG_Q4));
+  q = fma2(q, f, dup2(TA_LOG_Q5));
+  q = fma2(q, f, dup2(TA_LOG_Q6));
+  q = fma2(q, f, dup2(TA_LOG_Q7));
+  q = fma2(q, f, dup2(TA_LOG_Q8));
+  q = fma2(q, f, dup2(TA_LOG_Q9));
+  const float2 f2 = P.mul(f, f);
+  const float2 hi = P.mul(ef, dup2(TA_LN2_HI));
+  const float2 s = P.add(hi, f);
+  const float2 err = P.add(P.sub(hi, s), f);
+  const float2 lo = fma2(f2, q, fma2(ef, dup2(TA_LN2_LO), err));
+  return P.add(s, lo);
+}
+
+// Range flag thresholds of the fast path: ln v_new below -69.3 (v_new below
+// ~8.9e-31, incl. every v_new < 2^-100, zero and subnormal) takes the exact
+// path, where v / bc2 needs the scaled or IEEE division and the log its
+// subnormal and zero handling.
+constexpr float FAST_LN_MIN = -69.3f;
+
+template <int PT>
+__device__ __forceinline__ float4 ld_quad(const uint8_t* base, int t0) {
+  if (PT) {
+    const uint2 w = *reinterpret_cast<const uint2*>(base + 2 * t0);
+    return make_float4(__uint_as_float(w.x << 16), __uint_as_float(w.x & 0xffff0000u),
+                       __uint_as_float(w.y << 16), __uint_as_float(w.y & 0xffff0000u));
+  }
+  return *reinterpret_cast<const float4*>(base + 4 * t0);
+}
+
+template <int PT>
+__device__ __forceinline__ void st_quad(void* p, int64_t e, float4 v) {
+  if (PT) {
+    uint2 w;
+    w.x = (uint32_t)ta_f32_to_bf16(v.x) | ((uint32_t)ta_f32_to_bf16(v.y) << 16);
+    w.y = (uint32_t)ta_f32_to_bf16(v.z) | ((uint32_t)ta_f32_to_bf16(v.w) << 16);
+    *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(p) + e) = w;
+  } else {
+    *reinterpret_cast<float4*>(reinterpret_cast<float*>(p) + e) = v;
+  }
+}
+
+// bf16 parameters: p * (1 - lr*wd) is rounded to bf16 before the update
+// (torch computes the in-place op in fp32 and stores bf16).
+template <int PT>
+__device__ __forceinline__ float2 round_param2(float2 v) {
+  if (PT) return make_float2(ta_bf16_to_f32(ta_f32_to_bf16(v.x)), ta_bf16_to_f32(ta_f32_to_bf16(v.y)));
+  return v;
+}
+
+// ---------------------------------------------------------------------------
 // Pass 1
 // ---------------------------------------------------------------------------
 // Producer: bulk copies of one tile's inputs. Per-element arrays go as one
@@ -347,19 +461,31 @@ __device__ __forceinline__ uint32_t p1_issue(const DevTensor& D, uint8_t* st, in
   return bytes;
 }
 
+// Element layout inside a 128-element block: lane j of the block's 8-lane
+// group owns the quads Q = j + 8k (k = 0..3), i.e. elements 4Q + i, i = 0..3.
+// The stochastic-rounding draws of quad Q of block b are the 4 words of
+// Philox(b*32 + Q, tensor_id, step, b >> 27) (ta_sr_counter); the alpha
+// partial of a lane accumulates its elements with i even and i odd in two
+// chains (k ascending) that are added at the end, then the 8 lanes are
+// combined ((l0+l4)+(l2+l6))+((l1+l5)+(l3+l7)).
+
 // Exact recomputation of one element of a full block (rare path): used when
-// v/bc2 needs the subnormal IEEE fallback or a stored index is >= 2^nbits.
-// Recomputes m, v_new, ln v_new and the parameter update from the staged
-// (unmodified) inputs and stores the parameter. Returns ln v_new.
+// a range flag (tiny or non-finite v_new, v / bc2 overflow) or an index
+// >= 2^nbits was seen. Recomputes m, v_new, ln v_new and the parameter
+// update from the staged (unmodified) inputs with exact special-case
+// handling, stores the parameter, records a non-finite gradient in the status
+// word and returns ln v_new.
 template <int MK, int VK, int PT, bool UNI>
 __device__ __noinline__ float p1_fix_elem(const StageMeta& M, const uint8_t* st, int bi, int t,
-                                          int64_t e, float cs_scale, uint32_t bit,
-                                          bool has_state, float lmin, float span) {
+                                          int64_t e, float cs_scale, bool has_state, float lmin,
+                                          float span, uint32_t* status) {
   using L = P1L<MK, VK, PT, UNI>;
   const Sc c = M.c;
   const float g = ld_smem_elem<PT>(st + L::OFF_G + L::AP::off(bi), t);
+  if (!(fabsf(g) <= 3.4028234663852886e38f)) atomicOr(status, 1u);
   float m = 0.0f;
   if (MK == MK_COSTATE) {
+    const uint32_t bit = (st[L::OFF_SGN + bi * 16 + (t >> 3)] >> (7 - (t & 7))) & 1u;
     m = costate_m(g, M.alpha_old, cs_scale, bit, has_state, c.b1, c.omb1);
   } else if (MK == MK_FP32) {
     const float ea = reinterpret_cast<const float*>(st + L::OFF_EA + L::A4::off(bi))[t];
@@ -368,7 +494,7 @@ __device__ __noinline__ float p1_fix_elem(const StageMeta& M, const uint8_t* st,
   float vn = 0.0f, lv = 0.0f;
   if (VK == VK_ONEQ) {
     const int id = st[L::OFF_IDX + L::A1::off(bi) + t];
-    const float qv = __fdiv_rn(__fadd_rn((float)id, 0.5f), c.nbf);
+    const float qv = __fmul_rn(__fadd_rn((float)id, 0.5f), c.rnbf);
     const float vo = ta_expf(__fadd_rn(lmin, __fmul_rn(qv, span)));
     vn = __fmaf_rn(__fmul_rn(g, g), c.omb2, __fmul_rn(vo, c.b2));
     lv = log_clamped(vn);
@@ -383,18 +509,78 @@ __device__ __noinline__ float p1_fix_elem(const StageMeta& M, const uint8_t* st,
   return lv;
 }
 
-// One 128-element block per 8-lane group; elements visited as 4 quads of 4.
-// FULL: every group of the warp has a full block (inputs from smem, no bounds
-// checks); otherwise the general path: per-element bounds, global loads for
-// the ragged tail block and IEEE divisions there. ln v_new goes through a
-// per-lane smem scratch (scr[k*32 + lane]) between phase A and phase B, the
-// new indices through a per-group byte buffer (ob) for 16-byte stores.
+// Exact stochastic re-quantisation of one lane's 16 elements (quantize.py:
+// 276-294) for blocks that took a slow path: handles non-finite logs and
+// partial blocks (elements past n read as 0 -> clamped to index 0).
+template <bool UNI>
+__device__ __noinline__ void p1_requant_exact(const float4* scr4, const float* suni,
+                                              uint8_t* gidx, uint64_t b, int j, int lane,
+                                              float vmin, float nspan, float rspan, float nbf,
+                                              uint32_t tid, uint32_t step, const uint32_t* rk0,
+                                              const uint32_t* rk1) {
+  const float top = nbf - 1.0f;
+#pragma unroll 1
+  for (int k = 0; k < 4; ++k) {
+    const int t0 = 4 * j + 32 * k;
+    uint32_t rnd[4] = {0, 0, 0, 0};
+    if (!UNI) {
+      uint32_t c0, c1, c2, c3;
+      ta_sr_counter(b, (uint32_t)(j + 8 * k), tid, step, &c0, &c1, &c2, &c3);
+      philox_rk(c0, c1, c2, c3, rk0, rk1, rnd);
+    }
+    const float4 lq = scr4[k * 32 + lane];
+    const float l4[4] = {lq.x, lq.y, lq.z, lq.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float u = UNI ? suni[t0 + i] : ta_u01(rnd[i]);
+      const float cc = __fmul_rn(div_by(__fsub_rn(l4[i], vmin), nspan, rspan), nbf);
+      const float fl = floorf(cc);
+      const float fr = __fsub_rn(cc, fl);
+      float r = __fadd_rn(fl, (u < fr) ? 1.0f : 0.0f);
+      r = (r < 0.0f) ? 0.0f : r;
+      r = (r > top) ? top : r;
+      gidx[t0 + i] = (uint8_t)r;
+    }
+  }
+}
+
+// Stochastic re-quantisation of 4 finite logs of a fast block: the same
+// operations as p1_requant_exact, paired, with the 4 indices packed into one
+// word (index + 2^23 carries the integer in its low byte).
+__device__ __forceinline__ uint32_t requant_quad(float4 l, float4 u, float2 vmin2, float2 nspan2n,
+                                                 float2 rspan2, float2 nbf2, float top,
+                                                 const PK& P) {
+  float2 a0 = P.sub(lo2(l), vmin2), a1 = P.sub(hi2(l), vmin2);
+  float2 q0 = P.mul(a0, rspan2), q1 = P.mul(a1, rspan2);
+  q0 = fma2(fma2(q0, nspan2n, a0), rspan2, q0);  // Markstein: RN((L - min) / span)
+  q1 = fma2(fma2(q1, nspan2n, a1), rspan2, q1);
+  const float2 c0 = P.mul(q0, nbf2), c1 = P.mul(q1, nbf2);
+  const float2 f0 = make_float2(floorf(c0.x), floorf(c0.y));
+  const float2 f1 = make_float2(floorf(c1.x), floorf(c1.y));
+  const float2 r0 = P.sub(c0, f0), r1 = P.sub(c1, f1);
+  float2 k0 = P.add(f0, make_float2(u.x < r0.x ? 1.0f : 0.0f, u.y < r0.y ? 1.0f : 0.0f));
+  float2 k1 = P.add(f1, make_float2(u.z < r1.x ? 1.0f : 0.0f, u.w < r1.y ? 1.0f : 0.0f));
+  k0 = P.add(make_float2(fminf(k0.x, top), fminf(k0.y, top)), dup2(8388608.0f));
+  k1 = P.add(make_float2(fminf(k1.x, top), fminf(k1.y, top)), dup2(8388608.0f));
+  const uint32_t w01 = __byte_perm(__float_as_uint(k0.x), __float_as_uint(k0.y), 0x0040);
+  const uint32_t w23 = __byte_perm(__float_as_uint(k1.x), __float_as_uint(k1.y), 0x0040);
+  return __byte_perm(w01, w23, 0x5410);
+}
+
+// One 128-element block per 8-lane group (quad layout above).
+// FULL: every group of the warp has a full block -- inputs from smem, paired
+// arithmetic, 16-byte loads and stores, range flags instead of per-element
+// special cases (a flagged block is recomputed exactly). Otherwise the
+// general path: per-element bounds, global loads for the ragged tail block,
+// IEEE divisions and exact special cases everywhere. ln v_new goes through a
+// per-lane smem scratch between the v update and the re-quantisation.
 template <int MK, int VK, int PT, bool UNI, bool TABLE, bool FULL>
 __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
                                          const uint8_t* st, float* table, float* scr,
-                                         uint8_t* ob, const KParams& kp) {
+                                         const KParams& kp) {
   using L = P1L<MK, VK, PT, UNI>;
   const Sc c = M.c;
+  const PK P(c.one, c.nzero);
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int q = lane >> 3;
@@ -409,25 +595,31 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
   void* const gp = M.p;
   float* const gea = M.ea;
   float* const geas = M.eas;
+  float4* scr4 = reinterpret_cast<float4*>(scr);
 
   const uint8_t* sp = st + L::OFF_P + L::AP::off(bi);
   const uint8_t* sg = st + L::OFF_G + L::AP::off(bi);
   const uint8_t* sidx = st + L::OFF_IDX + L::A1::off(bi);
   const float* sea = reinterpret_cast<const float*>(st + L::OFF_EA + L::A4::off(bi));
   const float* seas = reinterpret_cast<const float*>(st + L::OFF_EAS + L::A4::off(bi));
-  const uint32_t* sgnw = reinterpret_cast<const uint32_t*>(st + L::OFF_SGN + bi * 16);
   const DevTensor* D = FULL ? nullptr : &T[M.t];  // tail loads and seam outputs only
 
   // ---- per-block CoState decode scalars (costate.py:290-314)
   float cs_scale = 0.0f;
   const float alpha_old = M.alpha_old;
   const bool has_state = (MK == MK_COSTATE) && (c.flags & DF_M_HAS_STATE);
+  uint4 sgn4 = make_uint4(0, 0, 0, 0);
   if (MK == MK_COSTATE && has_state && active) {
     const uint8_t lab = st[L::OFF_LAB + bi];
     const float nrm = reinterpret_cast<const float*>(st + L::OFF_NRM)[bi];
     const uint16_t amp = reinterpret_cast<const uint16_t*>(st + L::OFF_AMP)[bi];
     cs_scale = costate_scale(lab, nrm, amp, c.sqbs);
+    sgn4 = *reinterpret_cast<const uint4*>(st + L::OFF_SGN + bi * 16);
   }
+  uint32_t sw0 = sgn4.x, sw1 = sgn4.y, sw2 = sgn4.z, sw3 = sgn4.w;  // rotated per quad
+  // the sign byte of quad k is byte (j >> 1) of word k, element i's bit is
+  // bit 7 - 4 (j & 1) - i of that byte; the shift moves it to bit 31 - i
+  const int sshift = 24 + 4 * (j & 1) - 8 * (j >> 1);
 
   // ---- per-block 1Q decode scalars (quantize.py:252-256) and exp table
   float lmin = 0.0f, span = 0.0f;
@@ -441,105 +633,205 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
     }
     if (TABLE) {
       for (int t = j; t < nb; t += 8) {
-        const float qv = __fdiv_rn(__fadd_rn((float)t, 0.5f), c.nbf);
+        const float qv = __fmul_rn(__fadd_rn((float)t, 0.5f), c.rnbf);
         tab[t] = ta_expf(__fadd_rn(lmin, __fmul_rn(qv, span)));
       }
     }
     __syncwarp();
   }
 
-  // ---- phase A: m, v, ln v, and the parameter update, per element
-  float mg = 0.0f, gg = 0.0f, gbad = 0.0f;
+  // ---- phase A: m, v, ln v and the parameter update
   float vmin = INFINITY, vmax = -INFINITY;
-  bool sub = false;
-  uint32_t idor = 0;
+  float mgs = 0.0f, ggs = 0.0f;  // lane partials of m.g and g.g
+  bool fix = false;              // FULL: this group's block needs the exact path
+  if (FULL) {
+    float2 am = dup2(0.0f), ag = dup2(0.0f), nanacc = dup2(0.0f);
+    float vmin_fp = INFINITY;  // VK_FP32: smallest v_new
+    uint32_t idor = 0;
+    const float2 zero2 = dup2(0.0f);
 #pragma unroll 1
-  for (int kq = 0; kq < 4; ++kq) {
-    const uint32_t sw = (MK == MK_COSTATE && has_state && active) ? sgnw[kq] : 0u;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int k = 4 * kq + i;
-      const int t = j + 8 * k;
-      const int64_t e = e0 + t;
-      const bool ve = FULL || t < nv;
-      float g;
-      if (fullblk) g = ld_smem_elem<PT>(sg, t);
-      else g = ve ? to_f32<PT>(D->g, e) : 0.0f;
-      gbad = __fmaf_rn(g, 0.0f, gbad);
-      float m = 0.0f;
+    for (int k = 0; k < 4; ++k) {
+      const int t0 = 4 * j + 32 * k;
+      const int64_t e = e0 + t0;
+      const float4 g4 = ld_quad<PT>(sg, t0);
+      const float2 g01 = lo2(g4), g23 = hi2(g4);
+      float2 m01 = zero2, m23 = zero2;
       if (MK == MK_COSTATE) {
-        const uint32_t bit = (sw >> (8 * i + 7 - j)) & 1u;
-        m = costate_m(g, alpha_old, cs_scale, bit, has_state, c.b1, c.omb1);
-        if (ve) {
-          mg = __fmaf_rn(m, g, mg);
-          gg = __fmaf_rn(g, g, gg);
+        const uint32_t sb = sw0 << sshift;
+        sw0 = sw1;
+        sw1 = sw2;
+        sw2 = sw3;
+        const uint32_t sc = __float_as_uint(cs_scale);
+        const float2 sd01 = make_float2(__uint_as_float(sc ^ (sb & 0x80000000u)),
+                                        __uint_as_float(sc ^ ((sb << 1) & 0x80000000u)));
+        const float2 sd23 = make_float2(__uint_as_float(sc ^ ((sb << 2) & 0x80000000u)),
+                                        __uint_as_float(sc ^ ((sb << 3) & 0x80000000u)));
+        float2 mh01 = P.add(P.mul(dup2(alpha_old), g01), sd01);
+        float2 mh23 = P.add(P.mul(dup2(alpha_old), g23), sd23);
+        if (!has_state) {
+          mh01 = zero2;
+          mh23 = zero2;
         }
+        m01 = P.add(P.mul(dup2(c.b1), mh01), P.mul(dup2(c.omb1), g01));
+        m23 = P.add(P.mul(dup2(c.b1), mh23), P.mul(dup2(c.omb1), g23));
+        am = fma2(m01, g01, am);
+        am = fma2(m23, g23, am);
+        ag = fma2(g01, g01, ag);
+        ag = fma2(g23, g23, ag);
       } else if (MK == MK_FP32) {
-        const float ea = fullblk ? sea[t] : (ve ? D->ea[e] : 0.0f);
-        m = __fmaf_rn(g, c.omb1, __fmul_rn(ea, c.b1));  // optimizer.py:113
-        if (ve) gea[e] = m;
+        const float4 ea4 = *reinterpret_cast<const float4*>(sea + t0);
+        m01 = fma2(g01, dup2(c.omb1), P.mul(lo2(ea4), dup2(c.b1)));  // optimizer.py:113
+        m23 = fma2(g23, dup2(c.omb1), P.mul(hi2(ea4), dup2(c.b1)));
+        *reinterpret_cast<float4*>(gea + e) = cat4(m01, m23);
       }
-      float vn = 0.0f;
+      if (VK == VK_NONE) nanacc = fma2(g01, zero2, fma2(g23, zero2, nanacc));  // status only
+      float2 v01 = zero2, v23 = zero2;
       if (VK == VK_ONEQ) {
-        const uint32_t id = active ? sidx[t] : 0u;
-        float vo;
-        if (TABLE && fullblk) {
-          idor |= id;
-          vo = tab[id & (uint32_t)(nb - 1)];
+        const uint32_t w = *reinterpret_cast<const uint32_t*>(sidx + t0);
+        float vo[4];
+        if (TABLE) {
+          idor |= w;
+          vo[0] = tab[w & (uint32_t)(nb - 1)];
+          vo[1] = tab[(w >> 8) & (uint32_t)(nb - 1)];
+          vo[2] = tab[(w >> 16) & (uint32_t)(nb - 1)];
+          vo[3] = tab[(w >> 24) & (uint32_t)(nb - 1)];
         } else {
-          const float qv = __fdiv_rn(__fadd_rn((float)id, 0.5f), c.nbf);
-          vo = ta_expf(__fadd_rn(lmin, __fmul_rn(qv, span)));
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float qv = __fmul_rn(__fadd_rn((float)((w >> (8 * i)) & 0xffu), 0.5f), c.rnbf);
+            vo[i] = ta_expf(__fadd_rn(lmin, __fmul_rn(qv, span)));
+          }
         }
-        const float g2 = ve ? __fmul_rn(g, g) : 0.0f;
-        vn = __fmaf_rn(g2, c.omb2, __fmul_rn(vo, c.b2));  // quantize.py:270
-        const float lv = log_clamped(vn);                  // quantize.py:275
-        scr[k * 32 + lane] = lv;
-        if (ve) {  // fminf/fmaxf skip a NaN operand, like the compare-select
-          vmin = fminf(lv, vmin);
-          vmax = fmaxf(lv, vmax);
-        }
+        // quantize.py:270: v = b2 * v_old + (1 - b2) * g^2
+        v01 = fma2(P.mul(g01, g01), dup2(c.omb2), P.mul(make_float2(vo[0], vo[1]), dup2(c.b2)));
+        v23 = fma2(P.mul(g23, g23), dup2(c.omb2), P.mul(make_float2(vo[2], vo[3]), dup2(c.b2)));
+        const float2 l01 = log_fast2(v01, P), l23 = log_fast2(v23, P);  // quantize.py:275
+        scr4[k * 32 + lane] = cat4(l01, l23);
+        vmin = fminf(fminf(l01.x, l01.y), fminf(fminf(l23.x, l23.y), vmin));
+        vmax = fmaxf(fmaxf(l01.x, l01.y), fmaxf(fmaxf(l23.x, l23.y), vmax));
       } else if (VK == VK_FP32) {
-        const float vs = fullblk ? seas[t] : (ve ? D->eas[e] : 0.0f);
-        vn = __fmaf_rn(__fmul_rn(c.omb2, g), g, __fmul_rn(vs, c.b2));  // optimizer.py:166
-        if (ve) geas[e] = vn;
-        sub = sub || (vn < 0x1p-126f && vn > 0.0f);
+        const float4 s4 = *reinterpret_cast<const float4*>(seas + t0);
+        v01 = fma2(P.mul(dup2(c.omb2), g01), g01, P.mul(lo2(s4), dup2(c.b2)));  // optimizer.py:166
+        v23 = fma2(P.mul(dup2(c.omb2), g23), g23, P.mul(hi2(s4), dup2(c.b2)));
+        *reinterpret_cast<float4*>(geas + e) = cat4(v01, v23);
+        vmin_fp = fminf(fminf(v01.x, v01.y), fminf(fminf(v23.x, v23.y), vmin_fp));
       }
-      if (param && ve) {
-        float pv;
-        if (fullblk) {
-          bool s2 = false;
-          pv = adam_elem<PT>(ld_smem_elem<PT>(sp, t), m, vn, c, &s2);
-        } else {
-          pv = adam_elem_ieee<PT>(to_f32<PT>(D->p, e), m, vn, c);
-        }
-        st_param<PT>(gp, e, pv);
+      if (VK != VK_NONE && !param) nanacc = fma2(v01, zero2, fma2(v23, zero2, nanacc));
+      if (param) {
+        // optimizer.py:106-107, 163/167, 170:
+        // p = fl(p * (1 - lr wd)); d = sqrt(v / bc2) + eps; p += fl(-lr m) / fl(d bc1)
+        const float4 p4 = ld_quad<PT>(sp, t0);
+        const float2 w01 = round_param2<PT>(P.mul(lo2(p4), dup2(c.wdf)));
+        const float2 w23 = round_param2<PT>(P.mul(hi2(p4), dup2(c.wdf)));
+        // v / bc2 by Markstein with y = RN(1/bc2): exact for v in the unflagged range
+        float2 x01 = P.mul(v01, dup2(c.rbc2)), x23 = P.mul(v23, dup2(c.rbc2));
+        nanacc = fma2(x01, zero2, fma2(x23, zero2, nanacc));  // v or v / bc2 not finite
+        x01 = fma2(fma2(x01, dup2(-c.bc2), v01), dup2(c.rbc2), x01);
+        x23 = fma2(fma2(x23, dup2(-c.bc2), v23), dup2(c.rbc2), x23);
+        const float2 d01 = P.add(make_float2(__fsqrt_rn(x01.x), __fsqrt_rn(x01.y)), dup2(c.eps));
+        const float2 d23 = P.add(make_float2(__fsqrt_rn(x23.x), __fsqrt_rn(x23.y)), dup2(c.eps));
+        const float2 n01 = P.mul(dup2(c.nlr), m01), n23 = P.mul(dup2(c.nlr), m23);
+        const float2 den01 = P.mul(d01, dup2(c.bc1)), den23 = P.mul(d23, dup2(c.bc1));
+        const float2 p01 = P.add(w01, make_float2(__fdiv_rn(n01.x, den01.x), __fdiv_rn(n01.y, den01.y)));
+        const float2 p23 = P.add(w23, make_float2(__fdiv_rn(n23.x, den23.x), __fdiv_rn(n23.y, den23.y)));
+        st_quad<PT>(gp, e, cat4(p01, p23));
       }
-      if (!FULL && ve && (c.flags & DF_M_OUT)) D->m_out[e] = m;
-      if (!FULL && ve && (c.flags & DF_V_OUT)) D->v_out[e] = vn;
     }
-  }
-  if (gbad != gbad) atomicOr(kp.status, 1u);
-
-  // ---- rare exact fallbacks, full blocks only (tail blocks were exact above):
-  // some v_new < 2^-126 (ln v_new < -87.3365) needs v/bc2 by IEEE division, or
-  // a stored index >= 2^nbits missed the exp table.
-  if (VK == VK_ONEQ) sub = vmin < -87.33f;
-  const bool fix = fullblk && active && (sub || (TABLE && VK == VK_ONEQ && idor >= (uint32_t)nb));
-  if (fix) {
+    if (MK == MK_COSTATE) {
+      mgs = __fadd_rn(am.x, am.y);
+      ggs = __fadd_rn(ag.x, ag.y);
+    }
+    const bool bad = (nanacc.x != nanacc.x) || (nanacc.y != nanacc.y);
+    if (VK == VK_ONEQ)
+      fix = bad || vmin < FAST_LN_MIN || (TABLE && (idor & (0x01010101u * (uint32_t)(0xff & ~(nb - 1)))) != 0);
+    else if (VK == VK_FP32)
+      fix = bad || !(vmin_fp >= 0x1p-100f);
+    else if (bad)
+      atomicOr(kp.status, 1u);  // m-only kernel: a non-finite gradient
+  } else {
+    // general path: per-element bounds and exact special cases
+    float am0 = 0.0f, am1 = 0.0f, ag0 = 0.0f, ag1 = 0.0f, gbad = 0.0f;
 #pragma unroll 1
-    for (int k = 0; k < 16; ++k) {
-      const uint32_t sw = (MK == MK_COSTATE && has_state) ? sgnw[k >> 2] : 0u;
-      const uint32_t bit = (sw >> (8 * (k & 3) + 7 - j)) & 1u;
-      const float lv = p1_fix_elem<MK, VK, PT, UNI>(M, st, bi, j + 8 * k, e0 + j + 8 * k,
-                                                     cs_scale, bit, has_state, lmin, span);
-      if (VK == VK_ONEQ) scr[k * 32 + lane] = lv;
+    for (int k = 0; k < 4; ++k) {
+      const int t0 = 4 * j + 32 * k;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int t = t0 + i;
+        const int64_t e = e0 + t;
+        const bool ve = t < nv;
+        float g;
+        if (fullblk) g = ld_smem_elem<PT>(sg, t);
+        else g = ve ? to_f32<PT>(D->g, e) : 0.0f;
+        gbad = __fmaf_rn(g, 0.0f, gbad);
+        float m = 0.0f;
+        if (MK == MK_COSTATE) {
+          const uint32_t bit = has_state && active
+                                   ? (st[L::OFF_SGN + bi * 16 + (t >> 3)] >> (7 - (t & 7))) & 1u
+                                   : 0u;
+          m = costate_m(g, alpha_old, cs_scale, bit, has_state, c.b1, c.omb1);
+          if (ve) {
+            if (i & 1) {
+              am1 = __fmaf_rn(m, g, am1);
+              ag1 = __fmaf_rn(g, g, ag1);
+            } else {
+              am0 = __fmaf_rn(m, g, am0);
+              ag0 = __fmaf_rn(g, g, ag0);
+            }
+          }
+        } else if (MK == MK_FP32) {
+          const float ea = fullblk ? sea[t] : (ve ? D->ea[e] : 0.0f);
+          m = __fmaf_rn(g, c.omb1, __fmul_rn(ea, c.b1));
+          if (ve) gea[e] = m;
+        }
+        float vn = 0.0f;
+        if (VK == VK_ONEQ) {
+          const uint32_t id = active ? sidx[t] : 0u;
+          const float qv = __fmul_rn(__fadd_rn((float)id, 0.5f), c.rnbf);
+          const float vo = ta_expf(__fadd_rn(lmin, __fmul_rn(qv, span)));
+          const float g2 = ve ? __fmul_rn(g, g) : 0.0f;
+          vn = __fmaf_rn(g2, c.omb2, __fmul_rn(vo, c.b2));
+          const float lv = log_clamped(vn);
+          reinterpret_cast<float*>(scr4 + k * 32 + lane)[i] = lv;
+          if (ve) {  // fminf/fmaxf skip a NaN operand, like the compare-select
+            vmin = fminf(lv, vmin);
+            vmax = fmaxf(lv, vmax);
+          }
+        } else if (VK == VK_FP32) {
+          const float vs = fullblk ? seas[t] : (ve ? D->eas[e] : 0.0f);
+          vn = __fmaf_rn(__fmul_rn(c.omb2, g), g, __fmul_rn(vs, c.b2));
+          if (ve) geas[e] = vn;
+        }
+        if (param && ve) {
+          const float pv = fullblk ? ld_smem_elem<PT>(sp, t) : to_f32<PT>(D->p, e);
+          st_param<PT>(gp, e, adam_elem_ieee<PT>(pv, m, vn, c));
+        }
+        if (ve && (c.flags & DF_M_OUT)) D->m_out[e] = m;
+        if (ve && (c.flags & DF_V_OUT)) D->v_out[e] = vn;
+      }
+    }
+    if (gbad != gbad) atomicOr(kp.status, 1u);
+    mgs = __fadd_rn(am0, am1);
+    ggs = __fadd_rn(ag0, ag1);
+  }
+
+  // ---- exact recomputation of a flagged full block
+  if (FULL && fix) {
+#pragma unroll 1
+    for (int k = 0; k < 4; ++k) {
+#pragma unroll 1
+      for (int i = 0; i < 4; ++i) {
+        const int t = 4 * j + 32 * k + i;
+        const float lv = p1_fix_elem<MK, VK, PT, UNI>(M, st, bi, t, e0 + t, cs_scale, has_state,
+                                                      lmin, span, kp.status);
+        if (VK == VK_ONEQ) reinterpret_cast<float*>(scr4 + k * 32 + lane)[i] = lv;
+      }
     }
     if (VK == VK_ONEQ) {  // block extrema from the recomputed logs
       vmin = INFINITY;
       vmax = -INFINITY;
 #pragma unroll 1
       for (int k = 0; k < 16; ++k) {
-        const float lv = scr[k * 32 + lane];
+        const float lv = reinterpret_cast<const float*>(scr4 + (k >> 2) * 32 + lane)[k & 3];
         vmin = fminf(lv, vmin);
         vmax = fmaxf(lv, vmax);
       }
@@ -550,12 +842,12 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
   if (MK == MK_COSTATE) {
 #pragma unroll
     for (int off = 4; off >= 1; off >>= 1) {
-      mg = __fadd_rn(mg, __shfl_xor_sync(0xffffffffu, mg, off));
-      gg = __fadd_rn(gg, __shfl_xor_sync(0xffffffffu, gg, off));
+      mgs = __fadd_rn(mgs, __shfl_xor_sync(0xffffffffu, mgs, off));
+      ggs = __fadd_rn(ggs, __shfl_xor_sync(0xffffffffu, ggs, off));
     }
     if (active && j == 0) {
-      M.part[b] = mg;
-      M.part[M.bpad + b] = gg;
+      M.part[b] = mgs;
+      M.part[M.bpad + b] = ggs;
     }
   }
 
@@ -573,36 +865,31 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
     // >= 5.9e-8 in magnitude), inside div_by's exact range.
     const float nspan = clamp_min(__fsub_rn(vmax, vmin), 1e-10f);
     const float rspan = __frcp_rn(nspan);
-    const float top = c.nbf - 1.0f;
     const float* suni = reinterpret_cast<const float*>(st + L::OFF_UNI + L::A4::off(bi));
-    uint8_t* obq = ob + q * OB_STRIDE;
+    uint8_t* gidx = M.v_idx + e0;
+    if (FULL && !fix) {
+      const float2 vmin2 = dup2(vmin), nspan2n = dup2(-nspan), rspan2 = dup2(rspan);
+      const float2 nbf2 = dup2(c.nbf);
+      const float top = c.nbf - 1.0f;
 #pragma unroll 1
-    for (int kq = 0; kq < 4; ++kq) {
-      uint32_t rnd[4] = {0, 0, 0, 0};
-      if (!UNI) {
-        uint32_t c0, c1, c2, c3;
-        ta_sr_counter((uint64_t)b, (uint32_t)j, (uint32_t)kq, c.tid, c.step, &c0, &c1, &c2,
-                      &c3);
-        philox_rk(c0, c1, c2, c3, kp.rk0, kp.rk1, rnd);
+      for (int k = 0; k < 4; ++k) {
+        const int t0 = 4 * j + 32 * k;
+        float4 u4;
+        if (UNI) {
+          u4 = *reinterpret_cast<const float4*>(suni + t0);
+        } else {
+          uint32_t rnd[4], c0, c1, c2, c3;
+          ta_sr_counter((uint64_t)b, (uint32_t)(j + 8 * k), c.tid, c.step, &c0, &c1, &c2, &c3);
+          philox_rk(c0, c1, c2, c3, kp.rk0, kp.rk1, rnd);
+          u4 = make_float4(ta_u01(rnd[0]), ta_u01(rnd[1]), ta_u01(rnd[2]), ta_u01(rnd[3]));
+        }
+        *reinterpret_cast<uint32_t*>(gidx + t0) =
+            requant_quad(scr4[k * 32 + lane], u4, vmin2, nspan2n, rspan2, nbf2, top, P);
       }
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int k = 4 * kq + i;
-        const int t = j + 8 * k;
-        const float u = UNI ? suni[t] : ta_u01(rnd[i]);
-        const float cc = __fmul_rn(div_by(__fsub_rn(scr[k * 32 + lane], vmin), nspan, rspan),
-                                   c.nbf);
-        const float fl = floorf(cc);
-        const float fr = __fsub_rn(cc, fl);
-        float r = __fadd_rn(fl, (u < fr) ? 1.0f : 0.0f);
-        if (!FULL) r = (r < 0.0f) ? 0.0f : r;  // valid elements have L >= min: r >= 0
-        r = (r > top) ? top : r;
-        obq[t] = (uint8_t)r;
-      }
+    } else if (active) {
+      p1_requant_exact<UNI>(scr4, suni, gidx, (uint64_t)b, j, lane, vmin, nspan, rspan, c.nbf,
+                            c.tid, c.step, kp.rk0, kp.rk1);
     }
-    __syncwarp();
-    if (active)
-      reinterpret_cast<uint4*>(M.v_idx + e0)[j] = reinterpret_cast<const uint4*>(obq)[j];
   }
 }
 
@@ -610,8 +897,8 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
 template <int MK, int VK, int PT, bool UNI, bool TABLE>
 __device__ __noinline__ void p1_block_general(const DevTensor* T, const StageMeta& M,
                                               const uint8_t* st, float* table, float* scr,
-                                              uint8_t* ob, const KParams& kp) {
-  p1_block<MK, VK, PT, UNI, TABLE, false>(T, M, st, table, scr, ob, kp);
+                                              const KParams& kp) {
+  p1_block<MK, VK, PT, UNI, TABLE, false>(T, M, st, table, scr, kp);
 }
 
 __device__ __forceinline__ void fill_meta_common(StageMeta& m, const DevTensor& D, const Sc& c,
@@ -634,7 +921,6 @@ __global__ void __launch_bounds__(NTHR, 4) k_pass1(const __grid_constant__ KPara
   uint64_t* done = full + NSTAGE;
   StageMeta* meta = reinterpret_cast<StageMeta*>(done + NSTAGE);
   float* tables = reinterpret_cast<float*>(meta + NSTAGE);
-  uint8_t* obufs = reinterpret_cast<uint8_t*>(tables + NCW * 4 * TABLE_STRIDE + NCW * SCR_FLOATS);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -690,7 +976,6 @@ __global__ void __launch_bounds__(NTHR, 4) k_pass1(const __grid_constant__ KPara
 
   float* table = tables + warp * 4 * TABLE_STRIDE;
   float* scr = tables + NCW * 4 * TABLE_STRIDE + warp * SCR_FLOATS;
-  uint8_t* ob = obufs + warp * OB_BYTES;
   int it = 0;
   for (int64_t tile = blockIdx.x; tile < kp.total; tile += gridDim.x, ++it) {
     const int s = it % NSTAGE;
@@ -705,9 +990,9 @@ __global__ void __launch_bounds__(NTHR, 4) k_pass1(const __grid_constant__ KPara
     const bool fast =
         __all_sync(0xffffffffu, mine_full) && !(pm.c.flags & (DF_M_OUT | DF_V_OUT));
     if (fast)
-      p1_block<MK, VK, PT, UNI, TABLE, true>(kp.T, pm, st, table, scr, ob, kp);
+      p1_block<MK, VK, PT, UNI, TABLE, true>(kp.T, pm, st, table, scr, kp);
     else
-      p1_block_general<MK, VK, PT, UNI, TABLE>(kp.T, pm, st, table, scr, ob, kp);
+      p1_block_general<MK, VK, PT, UNI, TABLE>(kp.T, pm, st, table, scr, kp);
     __syncwarp();
     if (lane == 0) mbar_arrive(&done[s]);
   }
@@ -716,8 +1001,7 @@ __global__ void __launch_bounds__(NTHR, 4) k_pass1(const __grid_constant__ KPara
 template <int MK, int VK, int PT, bool UNI>
 constexpr size_t p1_smem_bytes() {
   return (size_t)NSTAGE * P1L<MK, VK, PT, UNI>::STAGE + 2 * NSTAGE * 8 +
-         NSTAGE * sizeof(StageMeta) + NCW * 4 * TABLE_STRIDE * 4 + NCW * SCR_FLOATS * 4 +
-         NCW * OB_BYTES;
+         NSTAGE * sizeof(StageMeta) + NCW * 4 * TABLE_STRIDE * 4 + NCW * SCR_FLOATS * 4;
 }
 
 // ---------------------------------------------------------------------------

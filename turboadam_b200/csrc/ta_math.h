@@ -120,18 +120,10 @@ TA_HD float ta_sqrt(float a) {
  * only large rounding is the final one.
  * Special inputs: NaN -> the same NaN, +inf -> +inf, 0 -> -inf, negative -> NaN.
  */
-TA_HD float ta_logf(float x) {
-  if (x != x) return x; /* NaN propagates unchanged */
-  if (!(x > 0.0f)) {
-    if (x == 0.0f) return -INFINITY;
-    return ta_u2f(0x7fc00000u); /* negative */
-  }
-  if (x == INFINITY) return x;
-  int32_t ex = 0;
-  if (x < 0x1p-126f) { /* subnormal: scale into the normal range (exact) */
-    x = ta_mul(x, 0x1p23f);
-    ex = -23;
-  }
+/* The polynomial core of ta_logf for a normal positive finite x, with the
+ * exponent offset ex of a prior exact scaling. Called with ex = 0 on any
+ * finite x it is the fast-path log of the kernels (no special cases). */
+TA_HD float ta_logf_core(float x, int32_t ex) {
   uint32_t ix = ta_f2u(x);
   int32_t e = ((int32_t)(ix - 0x3f2aaaabu)) >> 23;
   float m = ta_u2f(ix - ((uint32_t)e << 23));
@@ -153,6 +145,21 @@ TA_HD float ta_logf(float x) {
   float err = ta_add(ta_sub(hi, s), f);      /* Fast2Sum: exact, |hi| >= |f| or hi == 0 */
   float lo = ta_fma(f2, q, ta_fma(ef, TA_LN2_LO, err));
   return ta_add(s, lo);
+}
+
+TA_HD float ta_logf(float x) {
+  if (x != x) return x; /* NaN propagates unchanged */
+  if (!(x > 0.0f)) {
+    if (x == 0.0f) return -INFINITY;
+    return ta_u2f(0x7fc00000u); /* negative */
+  }
+  if (x == INFINITY) return x;
+  int32_t ex = 0;
+  if (x < 0x1p-126f) { /* subnormal: scale into the normal range (exact) */
+    x = ta_mul(x, 0x1p23f);
+    ex = -23;
+  }
+  return ta_logf_core(x, ex);
 }
 
 /*
@@ -264,16 +271,15 @@ TA_HD float ta_u01(uint32_t x) { return ta_mul((float)(x >> 8), 0x1p-24f); }
 
 /*
  * Stochastic-rounding counter layout (shared by kernel and checker).
- * Element e = b*128 + j + 8*k of a tensor (block b, lane j in 0..7, step k in
- * 0..15) takes word (k & 3) of the Philox block with counter
- *   (c0, c1, c2, c3) = (b*32 + 4*j + (k >> 2), tensor_id, step, b >> 27)
+ * Element e = b*128 + 4*Q + i of a tensor (block b, quad Q in 0..31, i in
+ * 0..3) takes word i of the Philox block with counter
+ *   (c0, c1, c2, c3) = (b*32 + Q, tensor_id, step, b >> 27)
  * and key (seed_lo, seed_hi). The draw depends only on (seed, tensor, step,
  * element), so it is the same however the tensor is split across GPUs.
  */
-TA_HD void ta_sr_counter(uint64_t block, uint32_t j, uint32_t kq, uint32_t tensor_id,
-                         uint32_t step, uint32_t* c0, uint32_t* c1, uint32_t* c2,
-                         uint32_t* c3) {
-  *c0 = (uint32_t)(block * 32u + 4u * j + kq);
+TA_HD void ta_sr_counter(uint64_t block, uint32_t quad, uint32_t tensor_id, uint32_t step,
+                         uint32_t* c0, uint32_t* c1, uint32_t* c2, uint32_t* c3) {
+  *c0 = (uint32_t)(block * 32u + quad);
   *c1 = tensor_id;
   *c2 = step;
   *c3 = (uint32_t)(block >> 27);
