@@ -227,10 +227,28 @@ __device__ __forceinline__ float costate_m(float g, float alpha_old, float scale
   return __fadd_rn(__fmul_rn(b1, mh), __fmul_rn(omb1, g));
 }
 
+// IEEE conversions between binary32 and binary16 in one instruction each;
+// identical to ta_f32_to_f16 / ta_f16_to_f32 for every non-NaN input (all
+// 2^32 and 2^16 inputs compared on sm_100a), NaNs take the portable
+// routines' encodings.
+__device__ __forceinline__ uint16_t f32_to_f16_dev(float f) {
+  unsigned short h;
+  asm("cvt.rn.f16.f32 %0, %1;" : "=h"(h) : "f"(f));
+  const uint32_t x = __float_as_uint(f);
+  return (f != f) ? (uint16_t)(((x >> 16) & 0x8000u) | 0x7e00u) : (uint16_t)h;
+}
+__device__ __forceinline__ float f16_to_f32_dev(uint16_t h) {
+  float f;
+  asm("cvt.f32.f16 %0, %1;" : "=f"(f) : "h"((unsigned short)h));
+  const uint32_t u = h;
+  const bool nan = (u & 0x7c00u) == 0x7c00u && (u & 0x3ffu) != 0u;
+  return nan ? __uint_as_float(((u & 0x8000u) << 16) | 0x7f800000u | ((u & 0x3ffu) << 13)) : f;
+}
+
 __device__ __forceinline__ float costate_scale(uint8_t label, float norm, uint16_t amp,
                                                float sqbs) {
   const float ph = __fdiv_rn(norm, sqbs);
-  const float am = ta_f16_to_f32(amp);
+  const float am = f16_to_f32_dev(amp);
   return label == 1 ? ph : (label == 2 ? am : 0.0f);
 }
 
@@ -628,8 +646,8 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
   if (VK == VK_ONEQ) {
     const uint16_t* hdr = reinterpret_cast<const uint16_t*>(st + L::OFF_HDR);
     if (active) {
-      lmin = ta_f16_to_f32(hdr[bi * 2]);
-      span = __fsub_rn(ta_f16_to_f32(hdr[bi * 2 + 1]), lmin);
+      lmin = f16_to_f32_dev(hdr[bi * 2]);
+      span = __fsub_rn(f16_to_f32_dev(hdr[bi * 2 + 1]), lmin);
     }
     if (TABLE) {
       for (int t = j; t < nb; t += 8) {
@@ -860,7 +878,7 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
     }
     if (active && j == 0)
       reinterpret_cast<uint32_t*>(M.v_hdr)[b] =
-          (uint32_t)ta_f32_to_f16(vmin) | ((uint32_t)ta_f32_to_f16(vmax) << 16);
+          (uint32_t)f32_to_f16_dev(vmin) | ((uint32_t)f32_to_f16_dev(vmax) << 16);
     // (L - min) / span: |L - min| is 0 or >= 2^-47 (ln of floats != 1 is
     // >= 5.9e-8 in magnitude), inside div_by's exact range.
     const float nspan = clamp_min(__fsub_rn(vmax, vmin), 1e-10f);
@@ -1114,26 +1132,58 @@ __device__ __forceinline__ void p2_block(const DevTensor* T, const StageMeta& M,
   }
   float accd = 0.0f, accm = 0.0f;
   uint32_t myw = 0;
+  if (FULL) {
+    // elements k, k + 1 of the lane as packed pairs; the two norm
+    // accumulations stay sequential in k (torch's lane order)
+    const PK P(M.c.one, M.c.nzero);
+    const float2 ao2 = dup2(alpha_old), a2 = dup2(alpha), b12 = dup2(b1), omb12 = dup2(omb1);
+    const uint32_t sc = __float_as_uint(cs_scale);
 #pragma unroll 1
-  for (int kq = 0; kq < 4; ++kq) {
-    const uint32_t sw = (has_state && active) ? sgnw[kq] : 0u;
+    for (int kq = 0; kq < 4; ++kq) {
+      const uint32_t sw = has_state ? sgnw[kq] : 0u;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int k = 4 * kq + i;
-      const int t = j + 8 * k;
-      const bool ve = FULL || t < nv;
-      float g;
-      if (fullblk) g = ld_smem_elem<PT>(sg, t);
-      else g = ve ? to_f32<PT>(D->g, e0 + t) : 0.0f;
-      const uint32_t bit = (sw >> (8 * i + 7 - j)) & 1u;
-      const float m = costate_m(g, alpha_old, cs_scale, bit, has_state, b1, omb1);
-      const float dl = ve ? __fsub_rn(m, __fmul_rn(alpha, g)) : 0.0f;  // costate.py:42
-      const float mm = ve ? m : 0.0f;
-      accd = __fadd_rn(accd, __fmul_rn(dl, dl));
-      accm = __fadd_rn(accm, __fmul_rn(mm, mm));
-      const uint32_t w = __ballot_sync(0xffffffffu, dl < 0.0f);
-      myw = (lane == k) ? w : myw;
-      if (!FULL && ve && (flags & DF_M_OUT)) D->m_out[e0 + t] = m;
+      for (int i = 0; i < 4; i += 2) {
+        const int k = 4 * kq + i;
+        const float2 g = make_float2(ld_smem_elem<PT>(sg, j + 8 * k),
+                                     ld_smem_elem<PT>(sg, j + 8 * k + 8));
+        const uint32_t s0 = (sw >> (8 * i + 7 - j)) & 1u, s1 = (sw >> (8 * i + 15 - j)) & 1u;
+        const float2 sd = make_float2(__uint_as_float(sc ^ (s0 << 31)),
+                                      __uint_as_float(sc ^ (s1 << 31)));
+        float2 mh = P.add(P.mul(ao2, g), sd);  // costate.py:261-323
+        if (!has_state) mh = dup2(0.0f);
+        const float2 m = P.add(P.mul(b12, mh), P.mul(omb12, g));  // costate.py:416
+        const float2 dl = P.sub(m, P.mul(a2, g));                 // costate.py:42
+        const float2 dd = P.mul(dl, dl), mm = P.mul(m, m);
+        accd = __fadd_rn(__fadd_rn(accd, dd.x), dd.y);
+        accm = __fadd_rn(__fadd_rn(accm, mm.x), mm.y);
+        const uint32_t w0 = __ballot_sync(0xffffffffu, dl.x < 0.0f);
+        const uint32_t w1 = __ballot_sync(0xffffffffu, dl.y < 0.0f);
+        myw = (lane == k) ? w0 : myw;
+        myw = (lane == k + 1) ? w1 : myw;
+      }
+    }
+  } else {
+#pragma unroll 1
+    for (int kq = 0; kq < 4; ++kq) {
+      const uint32_t sw = (has_state && active) ? sgnw[kq] : 0u;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int k = 4 * kq + i;
+        const int t = j + 8 * k;
+        const bool ve = t < nv;
+        float g;
+        if (fullblk) g = ld_smem_elem<PT>(sg, t);
+        else g = ve ? to_f32<PT>(D->g, e0 + t) : 0.0f;
+        const uint32_t bit = (sw >> (8 * i + 7 - j)) & 1u;
+        const float m = costate_m(g, alpha_old, cs_scale, bit, has_state, b1, omb1);
+        const float dl = ve ? __fsub_rn(m, __fmul_rn(alpha, g)) : 0.0f;  // costate.py:42
+        const float mm = ve ? m : 0.0f;
+        accd = __fadd_rn(accd, __fmul_rn(dl, dl));
+        accm = __fadd_rn(accm, __fmul_rn(mm, mm));
+        const uint32_t w = __ballot_sync(0xffffffffu, dl < 0.0f);
+        myw = (lane == k) ? w : myw;
+        if (ve && (flags & DF_M_OUT)) D->m_out[e0 + t] = m;
+      }
     }
   }
   // torch row-norm order: lane accumulators summed 0..7 in sequence
@@ -1155,7 +1205,7 @@ __device__ __forceinline__ void p2_block(const DevTensor* T, const StageMeta& M,
     reinterpret_cast<uint16_t*>(M.sgn + b * 16)[j] = (uint16_t)(by0 | (by1 << 8));
     if (j == 0) {
       M.nrm[b] = dn;
-      M.amp[b] = ta_f32_to_f16(__fdiv_rn(dn, sqbs));
+      M.amp[b] = f32_to_f16_dev(__fdiv_rn(dn, sqbs));
       M.ratios[b] = (mnorm == 0.0f) ? 0.0f : __fdiv_rn(dn, mnorm);
     }
   }
