@@ -1101,7 +1101,7 @@ __global__ void __launch_bounds__(FIN_THREADS) k_alpha(const __grid_constant__ S
 // ---------------------------------------------------------------------------
 template <int PT, bool FULL>
 __device__ __forceinline__ void p2_block(const DevTensor* T, const StageMeta& M,
-                                         const uint8_t* st) {
+                                         const uint8_t* st, uint2* wb) {
   using L = P2L<PT>;
   const float b1 = M.c.b1, omb1 = M.c.omb1, sqbs = M.c.sqbs;
   const uint32_t flags = M.c.flags;
@@ -1158,8 +1158,7 @@ __device__ __forceinline__ void p2_block(const DevTensor* T, const StageMeta& M,
         accm = __fadd_rn(__fadd_rn(accm, mm.x), mm.y);
         const uint32_t w0 = __ballot_sync(0xffffffffu, dl.x < 0.0f);
         const uint32_t w1 = __ballot_sync(0xffffffffu, dl.y < 0.0f);
-        myw = (lane == k) ? w0 : myw;
-        myw = (lane == k + 1) ? w1 : myw;
+        if (lane == 0) wb[k >> 1] = make_uint2(w0, w1);  // sign words k, k + 1
       }
     }
   } else {
@@ -1197,8 +1196,16 @@ __device__ __forceinline__ void p2_block(const DevTensor* T, const StageMeta& M,
   const float dn = __fsqrt_rn(sd);
   const float mnorm = __fsqrt_rn(sm);
   // sign bytes k = 2j, 2j+1 of this block (MSB = lane 0)
-  const uint32_t w0 = __shfl_sync(0xffffffffu, myw, 2 * j);
-  const uint32_t w1 = __shfl_sync(0xffffffffu, myw, 2 * j + 1);
+  uint32_t w0, w1;
+  if (FULL) {
+    __syncwarp();
+    const uint2 ww = wb[j];
+    w0 = ww.x;
+    w1 = ww.y;
+  } else {
+    w0 = __shfl_sync(0xffffffffu, myw, 2 * j);
+    w1 = __shfl_sync(0xffffffffu, myw, 2 * j + 1);
+  }
   if (active) {
     const uint32_t by0 = __brev((w0 >> (8 * q)) & 0xffu) >> 24;
     const uint32_t by1 = __brev((w1 >> (8 * q)) & 0xffu) >> 24;
@@ -1214,7 +1221,7 @@ __device__ __forceinline__ void p2_block(const DevTensor* T, const StageMeta& M,
 template <int PT>
 __device__ __noinline__ void p2_block_general(const DevTensor* T, const StageMeta& M,
                                               const uint8_t* st) {
-  p2_block<PT, false>(T, M, st);
+  p2_block<PT, false>(T, M, st, nullptr);
 }
 
 template <int PT>
@@ -1226,6 +1233,7 @@ __global__ void __launch_bounds__(NTHR) k_pass2(const __grid_constant__ KParams 
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + NSTAGE2 * L::STAGE);
   uint64_t* done = full + NSTAGE2;
   StageMeta* meta = reinterpret_cast<StageMeta*>(done + NSTAGE2);
+  uint2* wbufs = reinterpret_cast<uint2*>(meta + NSTAGE2);  // [NCW][8] sign words
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -1301,7 +1309,7 @@ __global__ void __launch_bounds__(NTHR) k_pass2(const __grid_constant__ KParams 
     const int bi = 4 * (lane >> 3) + warp;
     const bool mine_full = bi < pm.nblk && pm.n - (pm.b0 + bi) * BS >= BS;
     const bool fast = __all_sync(0xffffffffu, mine_full) && !(pm.c.flags & DF_M_OUT);
-    if (fast) p2_block<PT, true>(kp.T, pm, st);
+    if (fast) p2_block<PT, true>(kp.T, pm, st, wbufs + warp * 8);
     else p2_block_general<PT>(kp.T, pm, st);
     __syncwarp();
     if (lane == 0) mbar_arrive(&done[s]);
@@ -1310,7 +1318,8 @@ __global__ void __launch_bounds__(NTHR) k_pass2(const __grid_constant__ KParams 
 
 template <int PT>
 constexpr size_t p2_smem_bytes() {
-  return (size_t)NSTAGE2 * P2L<PT>::STAGE + 2 * NSTAGE2 * 8 + NSTAGE2 * sizeof(StageMeta);
+  return (size_t)NSTAGE2 * P2L<PT>::STAGE + 2 * NSTAGE2 * 8 + NSTAGE2 * sizeof(StageMeta) +
+         NCW * 8 * sizeof(uint2);
 }
 
 // ---------------------------------------------------------------------------
