@@ -71,9 +71,23 @@ def gpt2_124m_shapes():
     return s
 
 
+def llama3_70b_shapes():
+    d, kv, ffn, vocab, L = 8192, 1024, 28672, 128256, 80
+    shapes = [("embed", (vocab, d))]
+    for i in range(L):
+        shapes += [(f"l{i}.q", (d, d)), (f"l{i}.k", (kv, d)), (f"l{i}.v", (kv, d)),
+                   (f"l{i}.o", (d, d)), (f"l{i}.gate", (ffn, d)), (f"l{i}.up", (ffn, d)),
+                   (f"l{i}.down", (d, ffn)), (f"l{i}.ln1", (d,)), (f"l{i}.ln2", (d,))]
+    shapes += [("norm", (d,)), ("lm_head", (vocab, d))]
+    return shapes
+
+
 CONFIGS = {
     "llama3-8b": dict(shapes=llama3_8b_shapes, kw=dict(lr=6e-4, weight_decay=0.01, v_bits=4),
                       grad_std=1e-4, dtype="fp32"),
+    # bf16 params and grads, 3-bit v + CoState, ZeRO-1 at 4 and 8 GPUs
+    "llama3-70b": dict(shapes=llama3_70b_shapes, kw=dict(lr=6e-4, weight_decay=0.01, v_bits=3),
+                       grad_std=1e-4, dtype="bf16", partition="zero1"),
     "gpt2-block": dict(shapes=gpt2_block_shapes, kw=dict(lr=6e-4, weight_decay=0.01, v_bits=4),
                        grad_std=1e-3, dtype="fp32"),
     "gpt2-124m": dict(shapes=gpt2_124m_shapes, kw=dict(lr=6e-4, weight_decay=0.01, v_bits=4),
@@ -97,16 +111,17 @@ def lpt_assign(shapes, world):
     return lpt_owners([numel(s) for _, s in shapes], world)
 
 
-def kind_of(n, kw):
-    costate = kw.get("compress_m", True) and n >= kw.get("min_m_compress_elements", 4096)
+def kind_of(n, kw, n_policy=None):
+    n_policy = n if n_policy is None else n_policy  # shards decide by the whole tensor
+    costate = kw.get("compress_m", True) and n_policy >= kw.get("min_m_compress_elements", 4096)
     oneq = kw.get("compress_v", True)
     return costate, oneq
 
 
-def pass1_bytes(n, kw, psize=4):
+def pass1_bytes(n, kw, psize=4, n_policy=None):
     """Algorithmic HBM bytes of pass 1 for one tensor: read+write p, read g,
     read the old m state, read+write the v state (u8 layout)."""
-    costate, oneq = kind_of(n, kw)
+    costate, oneq = kind_of(n, kw, n_policy)
     B = (n + 127) // 128
     b = 2 * psize * n + psize * n
     b += (n + 7) // 8 + 7 * B if costate else 8 * n
@@ -114,10 +129,11 @@ def pass1_bytes(n, kw, psize=4):
     return b
 
 
-def step_bytes(n, kw, psize=4):
+def step_bytes(n, kw, psize=4, n_policy=None):
     """Single-touch algorithmic bytes of the whole step (figures:
-    14.42 B/param for 4-bit + CoState fp32, 22.06 v-only fp32)."""
-    costate, oneq = kind_of(n, kw)
+    14.42 B/param for 4-bit + CoState fp32, 22.06 v-only fp32, 8.42 3-bit +
+    CoState bf16)."""
+    costate, oneq = kind_of(n, kw, n_policy)
     B = (n + 127) // 128
     b = 3 * psize * n
     b += 2 * ((n + 7) // 8) + 14 * B if costate else 8 * n
@@ -316,21 +332,35 @@ def run_ours(args, rank, world, local_rank):
     kw = dict(cfg["kw"])
     if args.v_bits:
         kw["v_bits"] = args.v_bits
-    owner = lpt_assign(shapes, world)
-    my_ids = [i for i in range(len(shapes)) if owner[i] == rank]
-    mine = [shapes[i] for i in my_ids]
+    part = args.partition if args.partition != "auto" else cfg.get("partition", "tensor")
+    pdtype = torch.bfloat16 if cfg["dtype"] == "bf16" else torch.float32
+    psize = 2 if cfg["dtype"] == "bf16" else 4
+    # local tensors: (shape, global tensor index, shard (block_offset, global_numel) or None)
+    if part == "zero1":
+        from turboadam_b200.sharding import zero1_partition, zero1_spanning
+
+        parts = zero1_partition([numel(s) for _, s in shapes], world)
+        local = [((e1 - e0,), t, (boff, gn)) for t, e0, e1, boff, gn in parts[rank]]
+        spanning = zero1_spanning(parts)
+    else:
+        owner = lpt_assign(shapes, world)
+        local = [(shapes[i][1], i, None) for i in range(len(shapes)) if owner[i] == rank]
+        spanning = None
+    mine = [(numel(shp), sh[1] if sh else numel(shp)) for shp, _, sh in local]  # (n, n_policy)
     total_params = sum(numel(s) for _, s in shapes)
-    my_params = sum(numel(s) for _, s in mine)
+    my_params = sum(n for n, _ in mine)
     gen = torch.Generator(device=dev)
     params = []
-    for i in my_ids:  # data keyed by the global tensor index: same at every world size
-        gen.manual_seed(1234 + i)
-        p = torch.empty(shapes[i][1], dtype=torch.float32, device=dev)
+    for shp, t, sh in local:  # data keyed by the global tensor (and shard) index
+        gen.manual_seed(1234 + 7919 * t + (sh[0] // 4096 if sh else 0))
+        p = torch.empty(shp, dtype=pdtype, device=dev)
         p.normal_(0.0, 0.02, generator=gen)
         p = torch.nn.Parameter(p)
         p.grad = torch.empty_like(p).normal_(0.0, cfg["grad_std"], generator=gen)
         params.append(p)
-    opt = TurboAdam(params, betas=(0.9, 0.999), seed=2024, tensor_ids=my_ids, **kw)
+    opt = TurboAdam(params, betas=(0.9, 0.999), seed=2024, tensor_ids=[t for _, t, _ in local],
+                    shards=[sh for _, _, sh in local] if part == "zero1" else None,
+                    spanning=spanning, **kw)
     stream = torch.cuda.current_stream(dev)
 
     def barrier():
@@ -386,12 +416,12 @@ def run_ours(args, rank, world, local_rank):
     e2e = None
     if args.e2e_steps > 0:
         largest = max(p.numel() for p in params)
-        h_in = torch.empty(largest, dtype=torch.float32, pin_memory=True)
+        h_in = torch.empty(largest, dtype=pdtype, pin_memory=True)
         h_in.normal_(0.0, cfg["grad_std"])
-        h_out = torch.empty(largest, dtype=torch.float32, pin_memory=True)
+        h_out = torch.empty(largest, dtype=pdtype, pin_memory=True)
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
-        h2d = sum(p.numel() * 4 for p in params)
+        h2d = sum(p.numel() * psize for p in params)
         barrier()
         torch.cuda.synchronize(dev)
         e0.record(stream)
@@ -418,12 +448,12 @@ def run_ours(args, rank, world, local_rank):
     if rank != 0:
         return
     peak, peak_kind = measured_peak()
-    p1_bytes = sum(pass1_bytes(numel(s), kw) for _, s in mine)
-    st_bytes = sum(step_bytes(numel(s), kw) for _, s in mine)
+    p1_bytes = sum(pass1_bytes(n, kw, psize, npol) for n, npol in mine)
+    st_bytes = sum(step_bytes(n, kw, psize, npol) for n, npol in mine)
     achieved = p1_bytes / (phase[0] * 1e-3) / 1e9
     tpp = profiled_traffic(args.config)
-    n_costate = sum(1 for _, s in mine if kind_of(numel(s), kw)[0])
-    kinds = {kind_of(numel(s), kw) for _, s in mine}
+    n_costate = sum(1 for n, npol in mine if kind_of(n, kw, npol)[0])
+    kinds = {kind_of(n, kw, npol) for n, npol in mine}
     launches_per_step = len(kinds) + (1 + 1 + 4 if n_costate else 0)
     out = {
         "metric": METRIC,
@@ -436,12 +466,15 @@ def run_ours(args, rank, world, local_rank):
         "higher_is_better": True,
         "scaling": "strong" if world > 1 else "strong",
         "vs_baseline": None,
-        "dtype": "f32",
+        "dtype": "bf16" if psize == 2 else "f32",
         "data": "synthetic: random-init params N(0,0.02), seeded N(0,%g) grads generated on "
                 "device once and reused each step" % cfg["grad_std"],
         "config": {"workload": args.config, "params": total_params, "tensors": len(shapes),
                    "v_bits": kw["v_bits"], "costate": kw.get("compress_m", True),
-                   "parallelism": f"by-tensor LPT over {world} GPU(s), no collective",
+                   "parallelism": (f"ZeRO-1 flat partition over {world} GPU(s); tensors split "
+                                   "at 4096-block boundaries, 4 all-reduces per step (alpha "
+                                   "chunk sums, 3 histogram rounds)" if part == "zero1" else
+                                   f"by-tensor LPT over {world} GPU(s), no collective"),
                    "l2": "inputs >= 64 GB exceed the 126 MB L2; no flush"},
         "roofline": {
             "bound": "hbm",
@@ -482,6 +515,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="llama3-8b", choices=sorted(CONFIGS))
     ap.add_argument("--v-bits", type=int, default=0)
+    ap.add_argument("--partition", default="auto", choices=["auto", "tensor", "zero1"])
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

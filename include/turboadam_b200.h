@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define TA_ABI_VERSION 1
+#define TA_ABI_VERSION 2
 
 typedef enum ta_status {
   TA_OK = 0,
@@ -47,7 +47,19 @@ enum {
   TA_M_COSTATE = 1u << 0,   /* first moment is CoState (else fp32 exp_avg)        */
   TA_V_ONEQ = 1u << 1,      /* second moment is 1Q (else fp32 exp_avg_sq)         */
   TA_M_HAS_STATE = 1u << 2, /* CoState holds a previous encoding (not first step) */
-  TA_NO_PARAM = 1u << 3     /* skip weight decay and the parameter update         */
+  TA_NO_PARAM = 1u << 3,    /* skip weight decay and the parameter update         */
+  TA_M_SPANNING = 1u << 4   /* CoState shard of a tensor split over ranks:
+                               alpha and thresholds reduced via ta_step_phase     */
+};
+
+/* ta_step_phase phases (in call order; the caller all-reduces (sum) the
+ * exchange regions between them, see ta_exchange_size) */
+enum {
+  TA_PHASE_PASS1 = 0,  /* pass 1; spanning alpha chunk sums -> exchange chunks */
+  TA_PHASE_PASS2 = 1,  /* alpha from summed chunks, pass 2, histogram round 0 */
+  TA_PHASE_SEL1 = 2,   /* pick round 0, histogram round 1                      */
+  TA_PHASE_SEL2 = 3,   /* pick round 1, histogram round 2                      */
+  TA_PHASE_LABELS = 4  /* pick round 2, labels, commit alpha                    */
 };
 
 /* device status bits (ta_read_status) */
@@ -92,7 +104,18 @@ typedef struct ta_tensor {
   const float* alpha_inject_dev;/* optional [1]: replaces the computed alpha       */
   float* m_out_dev;           /* optional [n]: receives m_new (CoState.update seam)*/
   float* v_out_dev;           /* optional [n]: receives fp32 v_new                 */
+  /* shards of a tensor split over ranks (ZeRO-1); 0 for a whole tensor */
+  int64_t block_offset;       /* global block index of this shard's block 0; a
+                                 multiple of TA_SHARD_ALIGN_BLOCKS when spanning    */
+  int64_t global_blocks;      /* blocks of the whole tensor (0: this tensor's)     */
+  int64_t exch_chunk_off;     /* TA_M_SPANNING: this tensor's slot in the exchange */
+  int64_t exch_hist_off;      /*   regions (ta_exchange_layout), in elements       */
 } ta_tensor;
+
+/* shard boundaries of a spanning tensor fall on multiples of this many blocks
+ * (one alpha reduction chunk), which keeps alpha's summation order -- and so
+ * every packed bit -- independent of the number of ranks */
+#define TA_SHARD_ALIGN_BLOCKS 4096
 
 /*
  * Hyper-parameters of one param group (optimizer.py:67-80 defaults).
@@ -145,6 +168,36 @@ TA_API ta_status ta_step_profiled(const ta_tensor* tensors, int32_t n_tensors,
                                   const ta_group* groups, int32_t n_groups, uint64_t seed,
                                   void* workspace_dev, size_t workspace_bytes, void* stream,
                                   void* const* phase_events);
+
+/*
+ * Layout of the exchange buffer of a sharded step, the same on every rank:
+ * for the n tensors split over ranks (the whole job's list, in one agreed
+ * order; global_blocks[i] blocks each) it returns each tensor's slot --
+ * chunk_off[i] in fp64 elements of the chunk region ([2][alpha chunks] per
+ * tensor), hist_off[i] in uint32 elements of the histogram region ([2][2048]
+ * per tensor) -- and the two region sizes (the histogram region follows the
+ * chunk region in the buffer). Copy the slots into exch_chunk_off /
+ * exch_hist_off of the rank's shards. No counterpart in the reference
+ * (single-process); the reductions it carries are costate.py:22-43, :94-118.
+ */
+TA_API ta_status ta_exchange_layout(const int64_t* global_blocks, int32_t n, int64_t* chunk_off,
+                                    int64_t* hist_off, size_t* chunk_bytes,
+                                    size_t* hist_bytes);
+
+/*
+ * One phase of a sharded optimizer step (ZeRO-1). Every rank calls the five
+ * phases in order on the same layout; between them the caller all-reduces
+ * (sums over ranks) the chunk region after TA_PHASE_PASS1 and the histogram
+ * region after PASS2, SEL1 and SEL2 -- on every rank, also on ranks that hold
+ * no split tensor. Each rank then holds exactly the packed state the
+ * unsharded ta_step gives its shards. Tensors without TA_M_SPANNING complete
+ * as in ta_step. No counterpart in the reference.
+ */
+TA_API ta_status ta_step_phase(const ta_tensor* tensors, int32_t n_tensors,
+                               const ta_group* groups, int32_t n_groups, uint64_t seed,
+                               void* workspace_dev, size_t workspace_bytes, void* exchange_dev,
+                               size_t chunk_bytes, size_t hist_bytes, int32_t phase,
+                               void* stream);
 
 /* Reads (and optionally clears) the device status word of a workspace
  * (synchronises the stream). */

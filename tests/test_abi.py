@@ -30,11 +30,11 @@ def test_header_symbols_exported(lib):
     from turboadam_b200 import _lib
 
     names = declared_symbols()
-    assert len(names) == 15
+    assert len(names) == 17
     assert sorted(_lib.EXPORTED) == names
     for n in names:
         assert hasattr(lib, n), n
-    assert lib.ta_abi_version() == 1
+    assert lib.ta_abi_version() == 2
 
 
 def test_struct_layout_matches_header(lib):
@@ -49,9 +49,9 @@ def test_struct_layout_matches_header(lib):
 #include <stddef.h>
 #include "turboadam_b200.h"
 int main(void) {
-  printf("%zu %zu %zu %zu %zu %zu\n", sizeof(ta_tensor), offsetof(ta_tensor, v_idx_dev),
+  printf("%zu %zu %zu %zu %zu %zu %zu\n", sizeof(ta_tensor), offsetof(ta_tensor, v_idx_dev),
          offsetof(ta_tensor, v_out_dev), sizeof(ta_group), offsetof(ta_group, bc1),
-         offsetof(ta_group, v_bits));
+         offsetof(ta_group, v_bits), offsetof(ta_tensor, global_blocks));
   return 0;
 }
 """
@@ -63,7 +63,7 @@ int main(void) {
         got = [int(x) for x in subprocess.check_output([exe]).split()]
     want = [ctypes.sizeof(_lib.TaTensor), _lib.TaTensor.v_idx_dev.offset,
             _lib.TaTensor.v_out_dev.offset, ctypes.sizeof(_lib.TaGroup), _lib.TaGroup.bc1.offset,
-            _lib.TaGroup.v_bits.offset]
+            _lib.TaGroup.v_bits.offset, _lib.TaTensor.global_blocks.offset]
     assert got == want
     assert _lib.TENSOR_DTYPE.itemsize == want[0]
 

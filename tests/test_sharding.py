@@ -185,3 +185,101 @@ def test_turboadam_shard_with_global_ids_matches_unsharded():
                     assert torch.equal(ea[k], eb[k]), (i, k)
     with pytest.raises(ValueError):
         TurboAdam(full, tensor_ids=[0])
+
+
+def test_zero1_partition_cuts_on_chunk_boundaries():
+    from turboadam_b200.sharding import ALIGN_BLOCKS, zero1_partition
+
+    n = llama3_8b_numels()
+    for world in (1, 2, 4, 8):
+        parts = zero1_partition(n, world)
+        covered = {}
+        for shards in parts:
+            for t, e0, e1, boff, gn in shards:
+                assert gn == n[t] and boff * 128 == e0
+                assert e0 % (ALIGN_BLOCKS * 128) == 0 or e0 == 0
+                assert e1 == n[t] or e1 % (ALIGN_BLOCKS * 128) == 0
+                covered.setdefault(t, []).append((e0, e1))
+        for t, spans in covered.items():  # every tensor exactly covered
+            spans.sort()
+            assert spans[0][0] == 0 and spans[-1][1] == n[t]
+            assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+        loads = [sum(e1 - e0 for _, e0, e1, _, _ in s) for s in parts]
+        assert max(loads) - min(loads) <= 2 * ALIGN_BLOCKS * 128
+
+
+ZSHAPES = [(5000, 300), (777,), (4100, 256), (96, 70), (3000, 700)]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("world", [2, 3, 5])
+def test_zero1_phased_step_matches_unsharded(world):
+    """ZeRO-1 shards stepped through the phased C ABI, ranks emulated in one
+    process (their exchange regions summed between phases, what the NCCL
+    all-reduce does across GPUs): every parameter and packed-state bit equals
+    the unsharded step's."""
+    from turboadam_b200 import TurboAdam
+    from turboadam_b200.sharding import zero1_partition, zero1_spanning
+
+    numels = [int(np.prod(s)) for s in ZSHAPES]
+    init = [(torch.randn(n, generator=torch.Generator().manual_seed(40 + i)) * 0.02)
+            for i, n in enumerate(numels)]
+    grads = [[torch.randn(n, generator=torch.Generator().manual_seed(1000 * s + i)) * 1e-3
+              for i, n in enumerate(numels)] for s in range(3)]
+    kw = dict(lr=6e-4, weight_decay=0.01, v_bits=4, seed=9)
+
+    full = [torch.nn.Parameter(x.clone().cuda()) for x in init]
+    ofull = TurboAdam(full, **kw)
+    for s in range(3):
+        for p, g in zip(full, grads[s]):
+            p.grad = g.cuda()
+        ofull.step()
+
+    parts = zero1_partition(numels, world)
+    spanning = zero1_spanning(parts)
+    assert spanning  # the case splits at least one CoState tensor
+    ranks = []
+    for shards in parts:
+        ps = [torch.nn.Parameter(init[t][e0:e1].clone().cuda()) for t, e0, e1, _, _ in shards]
+        opt = TurboAdam(ps, tensor_ids=[t for t, *_ in shards],
+                        shards=[(boff, gn) for _, _, _, boff, gn in shards], spanning=spanning,
+                        **kw)
+        ranks.append((shards, ps, opt))
+    for s in range(3):
+        for shards, ps, _ in ranks:
+            for (t, e0, e1, _, _), p in zip(shards, ps):
+                p.grad = grads[s][t][e0:e1].cuda()
+        gens = [opt._step_gen() for _, _, opt in ranks]
+        regions = [next(g) for g in gens]
+        while regions:
+            total = torch.stack(regions).sum(0)
+            for r in regions:
+                r.copy_(total)
+            nxt = []
+            for g in gens:  # resume every rank, also past its last exchange
+                try:
+                    nxt.append(g.send(None))
+                except StopIteration:
+                    pass
+            assert len(nxt) in (0, len(gens))
+            regions = nxt
+    torch.cuda.synchronize()
+    for shards, ps, opt in ranks:
+        for (t, e0, e1, boff, _), p in zip(shards, ps):
+            q = full[t]
+            tag = f"world {world} tensor {t} [{e0}, {e1})"
+            assert torch.equal(p.data.view(-1).view(torch.int32),
+                               q.data.view(-1)[e0:e1].view(torch.int32)), tag
+            a, b = opt.state[p], ofull.state[q]
+            B0, B1 = boff, boff + (e1 - e0 + 127) // 128
+            assert torch.equal(a["compressed_v"]["indices"][:(e1 - e0)],
+                               b["compressed_v"]["indices"][e0:e1]), tag
+            assert torch.equal(a["compressed_v"]["scales"].view(torch.int16)[:B1 - B0],
+                               b["compressed_v"]["scales"].view(torch.int16)[B0:B1]), tag
+            if "m_mgr" in a:
+                ea, eb = a["m_mgr"]._encoded, b["m_mgr"]._encoded
+                assert float(a["m_mgr"]._alpha) == float(b["m_mgr"]._alpha), tag
+                assert torch.equal(ea["labels"], eb["labels"][B0:B1]), tag
+                assert torch.equal(ea["sign_packed"], eb["sign_packed"][e0 // 8:(e1 + 7) // 8]), tag
+                assert torch.equal(ea["block_norms"].view(torch.int32),
+                                   eb["block_norms"][B0:B1].view(torch.int32)), tag

@@ -22,6 +22,9 @@ TA_M_COSTATE = 1 << 0
 TA_V_ONEQ = 1 << 1
 TA_M_HAS_STATE = 1 << 2
 TA_NO_PARAM = 1 << 3
+TA_M_SPANNING = 1 << 4
+TA_PHASE_PASS1, TA_PHASE_PASS2, TA_PHASE_SEL1, TA_PHASE_SEL2, TA_PHASE_LABELS = range(5)
+TA_SHARD_ALIGN_BLOCKS = 4096
 TA_STATUS_NONFINITE_GRAD = 1 << 0
 TA_STATUS_WAIT_TIMEOUT = 1 << 1
 
@@ -50,6 +53,8 @@ EXPORTED = (
     "ta_costate_encode",
     "ta_thresholds",
     "ta_aux_workspace_size",
+    "ta_exchange_layout",
+    "ta_step_phase",
 )
 
 
@@ -81,6 +86,10 @@ class TaTensor(ctypes.Structure):
         ("alpha_inject_dev", ctypes.c_void_p),
         ("m_out_dev", ctypes.c_void_p),
         ("v_out_dev", ctypes.c_void_p),
+        ("block_offset", ctypes.c_int64),
+        ("global_blocks", ctypes.c_int64),
+        ("exch_chunk_off", ctypes.c_int64),
+        ("exch_hist_off", ctypes.c_int64),
     ]
 
 
@@ -153,6 +162,12 @@ _SIG = {
     "ta_thresholds": (ctypes.c_int, [_P, ctypes.c_int64, ctypes.c_double, ctypes.c_double, _P,
                                      _P, _P, ctypes.c_size_t, _P]),
     "ta_aux_workspace_size": (ctypes.c_size_t, [ctypes.c_int64]),
+    "ta_exchange_layout": (ctypes.c_int, [_P, ctypes.c_int32, _P, _P,
+                                          ctypes.POINTER(ctypes.c_size_t),
+                                          ctypes.POINTER(ctypes.c_size_t)]),
+    "ta_step_phase": (ctypes.c_int, [_P, ctypes.c_int32, _P, ctypes.c_int32, ctypes.c_uint64, _P,
+                                     ctypes.c_size_t, _P, ctypes.c_size_t, ctypes.c_size_t,
+                                     ctypes.c_int32, _P]),
 }
 
 _lib = None

@@ -109,6 +109,16 @@ std::vector<int64_t> cs_bpads(const ta_tensor* ts, int n) {
   return v;
 }
 
+bool is_spanning(const ta_tensor& t) {
+  return t.numel > 0 && is_costate(t) && (t.flags & TA_M_SPANNING) != 0;
+}
+
+// Exchange slot sizes of one split tensor (elements).
+inline int64_t xchunk_elems(int64_t global_blocks) {
+  return 2 * cdiv(cdiv(global_blocks, TB), FIN_THREADS);
+}
+constexpr int64_t kXHistElems = 2 * HBINS;
+
 // ---- kernel registry (one-time attribute setup, occupancy) --------------
 template <typename K>
 int setup_kernel(K kern, size_t smem, int threads) {
@@ -211,6 +221,17 @@ ta_status validate(const ta_tensor& t, int i, int n_groups, const ta_group* grou
                            !t.m_amp_dev || !t.m_alpha_dev))
     return bad("CoState state pointer missing");
   if (vk == VK_ONEQ && (!t.v_idx_dev || !t.v_hdr_dev)) return bad("1Q state pointer missing");
+  if (t.block_offset < 0 || t.global_blocks < 0) return bad("negative shard offset / size");
+  const int64_t nb_local = cdiv(t.numel, BS);
+  if (t.global_blocks && t.block_offset + nb_local > t.global_blocks)
+    return bad("shard extends past global_blocks");
+  if (t.flags & TA_M_SPANNING) {
+    if (mk != MK_COSTATE) return bad("TA_M_SPANNING needs a CoState first moment");
+    if (t.block_offset % TA_SHARD_ALIGN_BLOCKS)
+      return bad("a spanning shard must start at a multiple of TA_SHARD_ALIGN_BLOCKS blocks");
+    if (t.block_offset + nb_local < t.global_blocks && t.numel % BS)
+      return bad("only the last shard of a tensor may end in a partial block");
+  }
   const void* al[] = {t.param_dev, t.grad_dev, t.v_idx_dev, t.v_hdr_dev, t.exp_avg_sq_dev,
                       t.m_labels_dev, t.m_signs_dev, t.m_norms_dev, t.m_amp_dev, t.exp_avg_dev,
                       t.sr_uniforms_dev};
@@ -241,7 +262,11 @@ DevTensor make_dev(const ta_tensor& t, const ta_group& g, uint64_t seed) {
   D.n = t.numel;
   D.nblk = cdiv(t.numel, BS);
   D.bpad = cdiv(D.nblk, TB) * TB;
-  threshold_ranks(D.nblk, g.null_pct, g.amp_pct, &D.k_lo, &D.k_hi);
+  const int64_t gblocks = t.global_blocks ? t.global_blocks : D.nblk;
+  threshold_ranks(gblocks, g.null_pct, g.amp_pct, &D.k_lo, &D.k_hi);
+  D.boff = t.block_offset;
+  D.cglob = cdiv(cdiv(gblocks, TB), FIN_THREADS);
+  D.coff = t.block_offset / (TB * FIN_THREADS);
   // fp32 values of the Python scalars exactly as torch rounds them
   D.b1 = (float)g.beta1;
   D.omb1 = (float)(1.0 - g.beta1);
@@ -267,6 +292,7 @@ DevTensor make_dev(const ta_tensor& t, const ta_group& g, uint64_t seed) {
   if (t.m_out_dev) f |= DF_M_OUT;
   if (t.v_out_dev) f |= DF_V_OUT;
   if (t.dtype == TA_BF16) f |= DF_BF16;
+  if (t.flags & TA_M_SPANNING) f |= DF_SPAN;
   D.flags = f;
   D.tid = t.tensor_id;
   D.step = t.step;
@@ -281,8 +307,76 @@ DevTensor make_dev(const ta_tensor& t, const ta_group& g, uint64_t seed) {
 // Runs the fixed kernel sequence for an already validated tensor list.
 // ev (optional, 5 entries, may be null individually): cudaEvent_t recorded on
 // `st` before pass 1, after pass 1, after alpha, after pass 2, after labels.
+struct P1Key { int mk, vk, pt; bool uni, table; };
+
+// One phase of a sharded step (TA_PHASE_*), after the descriptors are uploaded.
+ta_status run_phase(int phase, const std::vector<std::pair<P1Key, LaunchList>>& p1,
+                    const std::vector<KParams>& p1k, const KParams* p2k, const SelParams& ap,
+                    int64_t achunks, const SelParams& sp, int64_t nchunks, const SelParams& xap,
+                    unsigned xa_chunks, const SelParams& xsp, unsigned xsel_chunks,
+                    const SelParams& xp, unsigned nx, uint8_t* exch, size_t chunk_bytes,
+                    size_t hist_bytes, cudaStream_t st) {
+  uint8_t* xh = exch + chunk_bytes;
+  switch (phase) {
+    case TA_PHASE_PASS1:
+      for (size_t i = 0; i < p1.size(); ++i) {
+        const P1Key& k = p1[i].first;
+        ta_status r = dispatch_p1(k.mk, k.vk, k.pt, k.uni, k.table, p1k[i], st);
+        if (r != TA_OK) return r;
+      }
+      if (achunks) k_alpha<<<(unsigned)achunks, FIN_THREADS, 0, st>>>(ap);
+      // every rank clears its regions (also one without split tensors: its
+      // zeros take part in the sum)
+      if (exch && chunk_bytes) TA_CU(cudaMemsetAsync(exch, 0, chunk_bytes, st));
+      if (nx) k_alpha_part<<<xa_chunks, FIN_THREADS, 0, st>>>(xap);
+      break;
+    case TA_PHASE_PASS2:
+      if (nx) k_alpha_fin<<<nx, FIN_THREADS, 0, st>>>(xp);
+      for (int pt = 0; pt < 2; ++pt) {
+        if (!p2k[pt].total) continue;
+        ta_status r = pt ? launch_p2<1>(p2k[pt], st) : launch_p2<0>(p2k[pt], st);
+        if (r != TA_OK) return r;
+      }
+      if (nchunks) {
+        k_select<0><<<(unsigned)nchunks, SEL_THREADS, 0, st>>>(sp);
+        k_select<1><<<(unsigned)nchunks, SEL_THREADS, 0, st>>>(sp);
+        k_select<2><<<(unsigned)nchunks, SEL_THREADS, 0, st>>>(sp);
+        k_labels<<<(unsigned)nchunks, SEL_THREADS, 0, st>>>(sp);
+      }
+      if (exch && hist_bytes) TA_CU(cudaMemsetAsync(xh, 0, hist_bytes, st));
+      if (nx) k_hist<0><<<xsel_chunks, SEL_THREADS, 0, st>>>(xsp);
+      break;
+    case TA_PHASE_SEL1:
+    case TA_PHASE_SEL2:
+      if (nx) {
+        if (phase == TA_PHASE_SEL1) k_pick<0><<<nx, SEL_THREADS, 0, st>>>(xp);
+        else k_pick<1><<<nx, SEL_THREADS, 0, st>>>(xp);
+      }
+      if (exch && hist_bytes) TA_CU(cudaMemsetAsync(xh, 0, hist_bytes, st));
+      if (nx) {
+        if (phase == TA_PHASE_SEL1) k_hist<1><<<xsel_chunks, SEL_THREADS, 0, st>>>(xsp);
+        else k_hist<2><<<xsel_chunks, SEL_THREADS, 0, st>>>(xsp);
+      }
+      break;
+    case TA_PHASE_LABELS:
+      if (nx) {
+        k_pick<2><<<nx, SEL_THREADS, 0, st>>>(xp);
+        k_labels<<<xsel_chunks, SEL_THREADS, 0, st>>>(xsp);
+      }
+      break;
+    default:
+      return fail(TA_ERR_INVALID, "unknown phase " + std::to_string(phase));
+  }
+  TA_CU(cudaGetLastError());
+  return TA_OK;
+}
+
+// phase < 0: the whole step (no spanning tensors allowed); phase 0..4: one
+// phase of a sharded step (TA_PHASE_*), exch the caller's exchange buffer.
 ta_status run_step(const ta_tensor* ts, int nT, const ta_group* groups, uint64_t seed,
-                   uint8_t* ws, size_t ws_bytes, cudaStream_t st, void* const* ev = nullptr) {
+                   uint8_t* ws, size_t ws_bytes, cudaStream_t st, void* const* ev = nullptr,
+                   int phase = -1, uint8_t* exch = nullptr, size_t chunk_bytes = 0,
+                   size_t hist_bytes = 0) {
   auto mark = [&](int i) -> cudaError_t {
     if (ev && ev[i]) return cudaEventRecord((cudaEvent_t)ev[i], st);
     return cudaSuccess;
@@ -292,6 +386,21 @@ ta_status run_step(const ta_tensor* ts, int nT, const ta_group* groups, uint64_t
   if (ws_bytes < L.total)
     return fail(TA_ERR_WORKSPACE, "workspace too small: need " + std::to_string(L.total) +
                                       " bytes, got " + std::to_string(ws_bytes));
+  bool any_span = false;
+  for (int i = 0; i < nT; ++i) {
+    if (!is_spanning(ts[i])) continue;
+    any_span = true;
+    const int64_t gb = ts[i].global_blocks ? ts[i].global_blocks : cdiv(ts[i].numel, BS);
+    if (phase < 0)
+      return fail(TA_ERR_INVALID, "TA_M_SPANNING tensors need the phased step (ta_step_phase)");
+    if (ts[i].exch_chunk_off < 0 || ts[i].exch_hist_off < 0 ||
+        (size_t)(ts[i].exch_chunk_off + xchunk_elems(gb)) * sizeof(double) > chunk_bytes ||
+        (size_t)(ts[i].exch_hist_off + kXHistElems) * sizeof(uint32_t) > hist_bytes)
+      return fail(TA_ERR_WORKSPACE, "tensor " + std::to_string(i) +
+                                        ": exchange slot outside the exchange regions");
+  }
+  if (any_span && (!exch || chunk_bytes % 16))
+    return fail(TA_ERR_INVALID, "exchange buffer missing or chunk region not 16-byte sized");
   std::vector<uint8_t> host(L.lists + L.list_stride * kMaxLists, 0);
   DevTensor* H = reinterpret_cast<DevTensor*>(host.data() + L.table);
   std::vector<int32_t> cs_list;
@@ -311,10 +420,13 @@ ta_status run_step(const ta_tensor* ts, int nT, const ta_group* groups, uint64_t
       H[i].alpha_new = reinterpret_cast<float*>(ws + s.alpha);
       H[i].chunk = reinterpret_cast<double*>(ws + s.chunk);
       cs_list.push_back(i);
+      if (is_spanning(ts[i])) {
+        H[i].xchunk = reinterpret_cast<double*>(exch) + ts[i].exch_chunk_off;
+        H[i].xhist = reinterpret_cast<uint32_t*>(exch + chunk_bytes) + ts[i].exch_hist_off;
+      }
     }
   }
   // launch lists: pass 1 by (mk, vk, pt, uni), pass 2 by pt, select chunks
-  struct P1Key { int mk, vk, pt; bool uni, table; };
   std::vector<std::pair<P1Key, LaunchList>> p1;
   auto p1_list = [&](P1Key k) -> LaunchList& {
     for (auto& e : p1)
@@ -328,9 +440,12 @@ ta_status run_step(const ta_tensor* ts, int nT, const ta_group* groups, uint64_t
   LaunchList p2[2];
   p2[0].beg.push_back(0);
   p2[1].beg.push_back(0);
-  LaunchList sel, alist;
+  LaunchList sel, alist, xsel, xalist, xlist;  // x*: spanning tensors
   sel.beg.push_back(0);
   alist.beg.push_back(0);
+  xsel.beg.push_back(0);
+  xalist.beg.push_back(0);
+  xlist.beg.push_back(0);
   for (int i = 0; i < nT; ++i) {
     if (ts[i].numel == 0) continue;
     const DevTensor& D = H[i];
@@ -344,10 +459,16 @@ ta_status run_step(const ta_tensor* ts, int nT, const ta_group* groups, uint64_t
     if (is_costate(ts[i])) {
       p2[pt].idx.push_back(i);
       p2[pt].beg.push_back(p2[pt].beg.back() + tiles);
-      sel.idx.push_back(i);
-      sel.beg.push_back(sel.beg.back() + D.sel_chunks);
-      alist.idx.push_back(i);
-      alist.beg.push_back(alist.beg.back() + D.alpha_chunks);
+      LaunchList& sl = is_spanning(ts[i]) ? xsel : sel;
+      LaunchList& al = is_spanning(ts[i]) ? xalist : alist;
+      sl.idx.push_back(i);
+      sl.beg.push_back(sl.beg.back() + D.sel_chunks);
+      al.idx.push_back(i);
+      al.beg.push_back(al.beg.back() + D.alpha_chunks);
+      if (is_spanning(ts[i])) {
+        xlist.idx.push_back(i);
+        xlist.beg.push_back(xlist.beg.back() + 1);
+      }
     }
   }
   // serialise the lists into the host image of the workspace
@@ -402,9 +523,22 @@ ta_status run_step(const ta_tensor* ts, int nT, const ta_group* groups, uint64_t
   put(alist, &ap.cbeg, &ap.cidx);
   ap.ncs = (int32_t)alist.idx.size();
   const int64_t achunks = alist.beg.back();
+  SelParams xsp, xap, xp;
+  xsp.T = xap.T = xp.T = dT;
+  put(xsel, &xsp.cbeg, &xsp.cidx);
+  xsp.ncs = (int32_t)xsel.idx.size();
+  put(xalist, &xap.cbeg, &xap.cidx);
+  xap.ncs = (int32_t)xalist.idx.size();
+  put(xlist, &xp.cbeg, &xp.cidx);
+  xp.ncs = (int32_t)xlist.idx.size();
+  const unsigned nx = (unsigned)xlist.idx.size();
+  const unsigned xsel_chunks = (unsigned)xsel.beg.back();
+  const unsigned xa_chunks = (unsigned)xalist.beg.back();
 
   TA_CU(cudaMemcpyAsync(ws + L.table, host.data() + L.table, host.size() - L.table,
                         cudaMemcpyHostToDevice, st));
+  if (phase >= 0) return run_phase(phase, p1, p1k, p2k, ap, achunks, sp, nchunks, xap, xa_chunks,
+                                   xsp, xsel_chunks, xp, nx, exch, chunk_bytes, hist_bytes, st);
   TA_CU(mark(0));
   for (size_t i = 0; i < p1.size(); ++i) {
     const P1Key& k = p1[i].first;
@@ -486,6 +620,47 @@ ta_status ta_step_profiled(const ta_tensor* tensors, int32_t n_tensors, const ta
   }
   return run_step(tensors, n_tensors, groups, seed, (uint8_t*)workspace_dev, workspace_bytes,
                   (cudaStream_t)stream, phase_events);
+}
+
+ta_status ta_exchange_layout(const int64_t* global_blocks, int32_t n, int64_t* chunk_off,
+                             int64_t* hist_off, size_t* chunk_bytes, size_t* hist_bytes) {
+  g_err.clear();
+  if (n < 0 || (n > 0 && (!global_blocks || !chunk_off || !hist_off)) || !chunk_bytes ||
+      !hist_bytes)
+    return fail(TA_ERR_INVALID, "bad arguments");
+  int64_t c = 0, h = 0;
+  for (int i = 0; i < n; ++i) {
+    if (global_blocks[i] <= 0) return fail(TA_ERR_INVALID, "global_blocks must be > 0");
+    chunk_off[i] = c;
+    c += xchunk_elems(global_blocks[i]);
+    hist_off[i] = h;
+    h += kXHistElems;
+  }
+  *chunk_bytes = al256((size_t)c * sizeof(double));
+  *hist_bytes = al256((size_t)h * sizeof(uint32_t));
+  return TA_OK;
+}
+
+ta_status ta_step_phase(const ta_tensor* tensors, int32_t n_tensors, const ta_group* groups,
+                        int32_t n_groups, uint64_t seed, void* workspace_dev,
+                        size_t workspace_bytes, void* exchange_dev, size_t chunk_bytes,
+                        size_t hist_bytes, int32_t phase, void* stream) {
+  g_err.clear();
+  if (n_tensors < 0 || (n_tensors > 0 && (!tensors || !groups)) || n_groups < 0)
+    return fail(TA_ERR_INVALID, "bad tensor / group arrays");
+  if (!workspace_dev || !aligned16(workspace_dev))
+    return fail(TA_ERR_INVALID, "workspace must be a 16-byte aligned device pointer");
+  if (phase < TA_PHASE_PASS1 || phase > TA_PHASE_LABELS)
+    return fail(TA_ERR_INVALID, "phase must be one of TA_PHASE_*");
+  if (exchange_dev && !aligned16(exchange_dev))
+    return fail(TA_ERR_INVALID, "exchange buffer must be 16-byte aligned");
+  for (int i = 0; i < n_tensors; ++i) {
+    ta_status r = validate(tensors[i], i, n_groups, groups);
+    if (r != TA_OK) return r;
+  }
+  return run_step(tensors, n_tensors, groups, seed, (uint8_t*)workspace_dev, workspace_bytes,
+                  (cudaStream_t)stream, nullptr, phase, (uint8_t*)exchange_dev, chunk_bytes,
+                  hist_bytes);
 }
 
 ta_status ta_read_status(void* workspace_dev, int32_t clear, uint32_t* status_out,

@@ -39,6 +39,7 @@ enum : uint32_t {
   DF_M_OUT = 1u << 11,
   DF_V_OUT = 1u << 12,
   DF_BF16 = 1u << 13,
+  DF_SPAN = 1u << 4,  // == TA_M_SPANNING
 };
 
 // Per-tensor descriptor, built on the host, uploaded into the workspace.
@@ -80,6 +81,12 @@ struct __align__(16) DevTensor {
   int32_t sel_chunks;  // ceil(bpad / SEL_CHUNK)
   int32_t alpha_chunks;  // ceil(tiles / FIN_THREADS)
   float one;           // 1.0f, stored by the host (a runtime identity operand)
+  // shards of a tensor split over ranks
+  int64_t boff;        // global block index of block 0 (stochastic-rounding counters)
+  int64_t cglob;       // alpha chunks of the whole tensor
+  int64_t coff;        // global chunk index of local chunk 0
+  double* xchunk;      // exchange: [2][cglob] fp64 chunk sums
+  uint32_t* xhist;     // exchange: [2][HBINS] histogram counts
 };
 
 // sel[] layout

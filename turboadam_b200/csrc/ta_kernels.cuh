@@ -156,6 +156,7 @@ struct __align__(16) StageMeta {
   int64_t n;
   int64_t bpad;
   int64_t b0;       // first block (within tensor)
+  int64_t boff;     // global block index of the tensor's block 0 (shards)
   int32_t t;        // tensor index
   int32_t nblk;     // blocks of this tile
   float alpha_old;  // CoState alpha of the previous step (state)
@@ -897,7 +898,8 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
           u4 = *reinterpret_cast<const float4*>(suni + t0);
         } else {
           uint32_t rnd[4], c0, c1, c2, c3;
-          ta_sr_counter((uint64_t)b, (uint32_t)(j + 8 * k), c.tid, c.step, &c0, &c1, &c2, &c3);
+          ta_sr_counter((uint64_t)(b + M.boff), (uint32_t)(j + 8 * k), c.tid, c.step, &c0, &c1,
+                        &c2, &c3);
           philox_rk(c0, c1, c2, c3, kp.rk0, kp.rk1, rnd);
           u4 = make_float4(ta_u01(rnd[0]), ta_u01(rnd[1]), ta_u01(rnd[2]), ta_u01(rnd[3]));
         }
@@ -905,7 +907,7 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
             requant_quad(scr4[k * 32 + lane], u4, vmin2, nspan2n, rspan2, nbf2, top, P);
       }
     } else if (active) {
-      p1_requant_exact<UNI>(scr4, suni, gidx, (uint64_t)b, j, lane, vmin, nspan, rspan, c.nbf,
+      p1_requant_exact<UNI>(scr4, suni, gidx, (uint64_t)(b + M.boff), j, lane, vmin, nspan, rspan, c.nbf,
                             c.tid, c.step, kp.rk0, kp.rk1);
     }
   }
@@ -925,6 +927,7 @@ __device__ __forceinline__ void fill_meta_common(StageMeta& m, const DevTensor& 
   m.n = D.n;
   m.bpad = D.bpad;
   m.b0 = b0;
+  m.boff = D.boff;
   m.t = t;
   m.nblk = nblk;
   m.alpha_old = aold;
@@ -1035,12 +1038,12 @@ struct SelParams {
   int32_t ncs;
 };
 
-__global__ void __launch_bounds__(FIN_THREADS) k_alpha(const __grid_constant__ SelParams sp) {
+// fp64 sums (m.g, g.g) of chunk c of a tensor: thread t sums the 16 block
+// partials of tile 256c + t in block order, then 32-wide xor butterflies and
+// the 8 warp sums in order. Block-wide; the result is valid in thread 0.
+__device__ __forceinline__ void alpha_chunk_sum(const DevTensor& D, int64_t c, double* cm,
+                                                double* cg) {
   const int tid = threadIdx.x;
-  const int64_t chunk = blockIdx.x;
-  const int en = find_entry(sp.cbeg, sp.ncs, chunk);
-  const DevTensor& D = sp.T[sp.cidx[en]];
-  const int64_t c = chunk - sp.cbeg[en];
   const int64_t ntile = (D.nblk + TB - 1) / TB;
   const int64_t t = c * FIN_THREADS + tid;
   double tm = 0.0, tg = 0.0;
@@ -1057,34 +1060,35 @@ __global__ void __launch_bounds__(FIN_THREADS) k_alpha(const __grid_constant__ S
     tg = tg + __shfl_xor_sync(0xffffffffu, tg, off);
   }
   __shared__ double wm[FIN_THREADS / 32], wg[FIN_THREADS / 32];
-  __shared__ int last;
   if ((tid & 31) == 0) {
     wm[tid >> 5] = tm;
     wg[tid >> 5] = tg;
   }
   __syncthreads();
   if (tid == 0) {
-    double cm = wm[0], cg = wg[0];
+    double sm = wm[0], sg = wg[0];
     for (int w = 1; w < FIN_THREADS / 32; ++w) {
-      cm += wm[w];
-      cg += wg[w];
+      sm += wm[w];
+      sg += wg[w];
     }
-    D.chunk[c] = cm;
-    D.chunk[D.alpha_chunks + c] = cg;
-    __threadfence();
-    last = (atomicAdd(&D.sel[SEL_CNTA], 1u) == (uint32_t)D.alpha_chunks - 1u);
+    *cm = sm;
+    *cg = sg;
   }
-  __syncthreads();
-  if (!last) return;
-  __threadfence();
-  // zero the select histograms / round counters of this tensor for this step
-  for (int i = tid; i < 3 * 2 * HBINS; i += FIN_THREADS) D.hist[i] = 0u;
+}
+
+// alpha = fl(sum m.g) / fl(sum g.g) from nchunks chunk sums (chunks[0..n) and
+// chunks[stride..stride+n)) summed in chunk order, then the per-step reset of
+// the select state of the tensor. Block-wide.
+__device__ __forceinline__ void alpha_finish(const DevTensor& D, const double* chunks,
+                                             int64_t nchunks, int64_t stride) {
+  const int tid = threadIdx.x;
+  for (int i = tid; i < 3 * 2 * HBINS; i += blockDim.x) D.hist[i] = 0u;
   if (tid < 3) D.sel[SEL_CNT0 + tid] = 0u;
   if (tid == 0) {
     double am = 0.0, ag = 0.0;
-    for (int64_t k = 0; k < D.alpha_chunks; ++k) {
-      am += __ldcg(&D.chunk[k]);
-      ag += __ldcg(&D.chunk[D.alpha_chunks + k]);
+    for (int64_t k = 0; k < nchunks; ++k) {
+      am += __ldcg(&chunks[k]);
+      ag += __ldcg(&chunks[stride + k]);
     }
     const float mg = (float)am, gg = (float)ag;
     float a = (gg > 0.0f) ? __fdiv_rn(mg, gg) : 0.0f;
@@ -1094,6 +1098,48 @@ __global__ void __launch_bounds__(FIN_THREADS) k_alpha(const __grid_constant__ S
     D.sel[SEL_RHI] = (uint32_t)D.k_hi;
     D.sel[SEL_CNTA] = 0u;
   }
+}
+
+__global__ void __launch_bounds__(FIN_THREADS) k_alpha(const __grid_constant__ SelParams sp) {
+  const int tid = threadIdx.x;
+  const int64_t chunk = blockIdx.x;
+  const int en = find_entry(sp.cbeg, sp.ncs, chunk);
+  const DevTensor& D = sp.T[sp.cidx[en]];
+  const int64_t c = chunk - sp.cbeg[en];
+  __shared__ int last;
+  double cm = 0.0, cg = 0.0;
+  alpha_chunk_sum(D, c, &cm, &cg);
+  if (tid == 0) {
+    D.chunk[c] = cm;
+    D.chunk[D.alpha_chunks + c] = cg;
+    __threadfence();
+    last = (atomicAdd(&D.sel[SEL_CNTA], 1u) == (uint32_t)D.alpha_chunks - 1u);
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  alpha_finish(D, D.chunk, D.alpha_chunks, D.alpha_chunks);
+}
+
+// Tensors split over ranks: each rank writes its chunk sums at their global
+// chunk positions of the exchange buffer (zero elsewhere); after the caller's
+// all-reduce, every rank sums all chunks in global order.
+__global__ void __launch_bounds__(FIN_THREADS) k_alpha_part(const __grid_constant__ SelParams sp) {
+  const int64_t chunk = blockIdx.x;
+  const int en = find_entry(sp.cbeg, sp.ncs, chunk);
+  const DevTensor& D = sp.T[sp.cidx[en]];
+  const int64_t c = chunk - sp.cbeg[en];
+  double cm = 0.0, cg = 0.0;
+  alpha_chunk_sum(D, c, &cm, &cg);
+  if (threadIdx.x == 0) {
+    D.xchunk[D.coff + c] = cm;
+    D.xchunk[D.cglob + D.coff + c] = cg;
+  }
+}
+
+__global__ void __launch_bounds__(FIN_THREADS) k_alpha_fin(const __grid_constant__ SelParams sp) {
+  const DevTensor& D = sp.T[sp.cidx[blockIdx.x]];
+  alpha_finish(D, D.xchunk, D.cglob, D.cglob);
 }
 
 // ---------------------------------------------------------------------------
@@ -1363,16 +1409,13 @@ __device__ __forceinline__ void scan_pick(const uint32_t* h, int nbins, uint32_t
   __syncthreads();
 }
 
+// Round-R histogram of the ratios in select chunk c of a tensor, added into
+// gh (round 0: one histogram of bits[31:21]; rounds 1, 2: the histograms of
+// the P10 and P90 candidates at gh and gh + HBINS). Block-wide.
 template <int R>
-__global__ void __launch_bounds__(SEL_THREADS) k_select(const __grid_constant__ SelParams sp) {
+__device__ __forceinline__ void sel_hist_chunk(const DevTensor& D, int64_t c, uint32_t* gh) {
   __shared__ uint32_t h[2][HBINS];
-  __shared__ uint32_t sh[SEL_THREADS];
-  __shared__ int last;
   const int tid = threadIdx.x;
-  const int64_t chunk = blockIdx.x;
-  const int en = find_entry(sp.cbeg, sp.ncs, chunk);
-  const DevTensor& D = sp.T[sp.cidx[en]];
-  const int64_t c = chunk - sp.cbeg[en];
   const int64_t i0 = c * SEL_CHUNK;
   const int64_t i1 = min(D.nblk, i0 + SEL_CHUNK);
   constexpr int NB = (R == 2) ? 1024 : 2048;
@@ -1398,22 +1441,29 @@ __global__ void __launch_bounds__(SEL_THREADS) k_select(const __grid_constant__ 
     }
   }
   __syncthreads();
-  uint32_t* gh = D.hist + R * 2 * HBINS;
   const int nh = (R == 0) ? 1 : 2;
   for (int k = 0; k < nh; ++k)
     for (int i = tid; i < NB; i += SEL_THREADS)
       if (h[k][i]) atomicAdd(&gh[k * HBINS + i], h[k][i]);
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) last = (atomicAdd(&D.sel[SEL_CNT0 + R], 1u) == (uint32_t)D.sel_chunks - 1u);
-  __syncthreads();
-  if (!last) return;
-  __threadfence();
+}
+
+// The round-R pick from a complete histogram gh: bins and remaining ranks of
+// the P10 / P90 order statistics (round 2: the thresholds). Block-wide.
+template <int R>
+__device__ __forceinline__ void sel_pick(const DevTensor& D, const uint32_t* gh) {
+  __shared__ uint32_t sh[SEL_THREADS];
   __shared__ uint32_t pick[4];
+  const int tid = threadIdx.x;
+  constexpr int NB = (R == 2) ? 1024 : 2048;
   if (tid < 4) pick[tid] = 0u;
   __syncthreads();
   // L2 (__ldcg) reads: the histogram was built by other CTAs' atomics
   const uint32_t rlo = __ldcg(&D.sel[SEL_RLO]), rhi = __ldcg(&D.sel[SEL_RHI]);
+  uint32_t plo = 0, phi = 0;
+  if (R > 0) {
+    plo = __ldcg(&D.sel[SEL_PLO]);
+    phi = __ldcg(&D.sel[SEL_PHI]);
+  }
   for (int k = 0; k < 2; ++k) {
     const uint32_t* src = gh + ((R == 0) ? 0 : k * HBINS);
     scan_pick(src, NB, k == 0 ? rlo : rhi, &pick[2 * k], &pick[2 * k + 1], sh);
@@ -1433,6 +1483,40 @@ __global__ void __launch_bounds__(SEL_THREADS) k_select(const __grid_constant__ 
     D.sel[SEL_RLO] = pick[1];
     D.sel[SEL_RHI] = pick[3];
   }
+}
+
+template <int R>
+__global__ void __launch_bounds__(SEL_THREADS) k_select(const __grid_constant__ SelParams sp) {
+  __shared__ int last;
+  const int tid = threadIdx.x;
+  const int64_t chunk = blockIdx.x;
+  const int en = find_entry(sp.cbeg, sp.ncs, chunk);
+  const DevTensor& D = sp.T[sp.cidx[en]];
+  const int64_t c = chunk - sp.cbeg[en];
+  uint32_t* gh = D.hist + R * 2 * HBINS;
+  sel_hist_chunk<R>(D, c, gh);
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) last = (atomicAdd(&D.sel[SEL_CNT0 + R], 1u) == (uint32_t)D.sel_chunks - 1u);
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  sel_pick<R>(D, gh);
+}
+
+// Split select for tensors over ranks: local histogram into the exchange
+// buffer (zeroed by the host first), pick from the all-reduced histogram.
+template <int R>
+__global__ void __launch_bounds__(SEL_THREADS) k_hist(const __grid_constant__ SelParams sp) {
+  const int64_t chunk = blockIdx.x;
+  const int en = find_entry(sp.cbeg, sp.ncs, chunk);
+  const DevTensor& D = sp.T[sp.cidx[en]];
+  sel_hist_chunk<R>(D, chunk - sp.cbeg[en], D.xhist);
+}
+
+template <int R>
+__global__ void __launch_bounds__(SEL_THREADS) k_pick(const __grid_constant__ SelParams sp) {
+  sel_pick<R>(sp.T[sp.cidx[blockIdx.x]], sp.T[sp.cidx[blockIdx.x]].xhist);
 }
 
 // labels (costate.py:126-149) and commit alpha (costate.py:443-456)

@@ -37,7 +37,16 @@ class TurboAdam(Optimizer):
     stream -- by default its position in that order. A rank that steps a
     shard of a larger parameter set passes the shard's global indices
     (``turboadam_b200.sharding.shard_by_tensor``) so its packed state matches
-    the unsharded run bit for bit.
+    the unsharded run bit for bit. ``shards`` (same order; None or
+    ``(block_offset, global_numel)`` per parameter) marks parameters that are
+    slices of a larger tensor split over ranks (ZeRO-1,
+    ``turboadam_b200.sharding.zero1_partition``). ``spanning`` lists, in the
+    same order on every rank, ``(tensor_id, global_numel)`` of every tensor of
+    the job that is split over ranks (``sharding.zero1_spanning``): when it is
+    not empty each step runs in phases with the CoState alpha sums and
+    threshold histograms all-reduced over ``process_group`` (default group)
+    between them -- on every rank, also one that holds no split tensor -- which
+    leaves every packed bit equal to the unsharded step's.
     """
 
     def __init__(
@@ -59,6 +68,9 @@ class TurboAdam(Optimizer):
         *,
         seed: int | None = None,
         tensor_ids=None,
+        shards=None,
+        spanning=None,
+        process_group=None,
     ):
         if v_bits not in (2, 3, 4, 6, 8):
             raise ValueError(f"v_bits must be one of {{2, 3, 4, 6, 8}}, got {v_bits}")
@@ -92,6 +104,36 @@ class TurboAdam(Optimizer):
             if any(t < 0 or t > 0xFFFFFFFF for t in tensor_ids):
                 raise ValueError("tensor_ids must be 32-bit unsigned integers")
             self._tid_override = {id(p): t for p, t in zip(flat, tensor_ids)}
+        self._shard = {}
+        if shards is not None:
+            flat = [p for g in self.param_groups for p in g["params"]]
+            shards = list(shards)
+            if len(shards) != len(flat):
+                raise ValueError(f"shards has {len(shards)} entries for {len(flat)} parameters")
+            for p, sh in zip(flat, shards):
+                if sh is None:
+                    continue
+                boff, gnumel = int(sh[0]), int(sh[1])
+                if boff < 0 or boff * block_size + p.numel() > gnumel:
+                    raise ValueError("shard (block_offset, global_numel) does not hold the "
+                                     "parameter")
+                self._shard[id(p)] = (boff, gnumel)
+        self._pg = process_group
+        self._xbuf = {}
+        self._xslot = {}
+        self._xbytes = (0, 0)
+        if spanning:
+            spanning = [(int(t), int(n)) for t, n in spanning]
+            gblocks = np.array([-(-n // block_size) for _, n in spanning], dtype=np.int64)
+            coff = np.zeros(len(spanning), dtype=np.int64)
+            hoff = np.zeros(len(spanning), dtype=np.int64)
+            cb, hb = ctypes.c_size_t(0), ctypes.c_size_t(0)
+            lib = _lib.load()
+            _lib.check(lib.ta_exchange_layout(gblocks.ctypes.data, len(spanning), coff.ctypes.data,
+                                              hoff.ctypes.data, ctypes.byref(cb), ctypes.byref(hb)),
+                       "ta_exchange_layout")
+            self._xslot = {t: (int(c), int(h)) for (t, _), c, h in zip(spanning, coff, hoff)}
+            self._xbytes = (cb.value, hb.value)
         self._plans = None
         self._ws = {}
         # test hook: {"uniforms": {param: fp32 [B*128] cuda}, "alpha": {param: fp32 [1] cuda}}
@@ -137,7 +179,10 @@ class TurboAdam(Optimizer):
         block_size = group["block_size"]
         if len(state) == 0:  # optimizer.py:243-269
             state["step"] = 0
-            compress_this_m = group["compress_m"] and p.numel() >= group["min_m_compress_elements"]
+            # the policy looks at the whole tensor, so every rank of a split
+            # tensor makes the same choice
+            gnumel = self._shard.get(id(p), (0, p.numel()))[1]
+            compress_this_m = group["compress_m"] and gnumel >= group["min_m_compress_elements"]
             state["_compress_m"] = compress_this_m
             if compress_this_m:
                 mgr = CoStateManager(block_size=block_size, null_pct=group["null_pct"],
@@ -181,6 +226,26 @@ class TurboAdam(Optimizer):
     @torch.no_grad()
     def step(self, closure=None):
         """Perform a single optimization step."""
+        gen = self._step_gen(closure)
+        try:
+            region = next(gen)
+            while True:
+                self._exchange(region)
+                region = gen.send(None)
+        except StopIteration as done:
+            return done.value
+
+    def _exchange(self, region):
+        """Sum an exchange region over the ranks (NCCL all-reduce ordered on
+        the current stream)."""
+        import torch.distributed as dist
+
+        dist.all_reduce(region, op=dist.ReduceOp.SUM, group=self._pg)
+
+    def _step_gen(self, closure=None):
+        """The step as a generator: yields each exchange region (fp64 alpha
+        chunk sums, then int32 histograms) that must be summed over the ranks
+        in place before it is resumed; returns the closure's loss."""
         loss = None
         if closure is not None:
             with torch.enable_grad():
@@ -215,7 +280,7 @@ class TurboAdam(Optimizer):
         for gi, p in work:
             by_dev.setdefault(p.device, []).append((gi, p))
         for dev, items in by_dev.items():
-            self._run_device(dev, items, bcs)
+            yield from self._run_device(dev, items, bcs)
         return loss
 
     # ------------------------------------------------------------------
@@ -244,6 +309,19 @@ class TurboAdam(Optimizer):
             r["group"] = gi
             r["tensor_id"] = tids[id(p)] & 0xFFFFFFFF
             flags = 0
+            sh = self._shard.get(id(p))
+            if sh is not None:
+                boff, gnumel = sh
+                gblocks = -(-gnumel // group["block_size"])
+                r["block_offset"] = boff
+                r["global_blocks"] = gblocks
+                if st["_compress_m"] and (boff != 0 or -(-p.numel() // group["block_size"]) != gblocks):
+                    flags |= _lib.TA_M_SPANNING
+                    slot = self._xslot.get(tids[id(p)])
+                    if slot is None:
+                        raise ValueError(f"tensor {tids[id(p)]} is split over ranks but missing "
+                                         "from `spanning`")
+                    r["exch_chunk_off"], r["exch_hist_off"] = slot
             if st["_compress_m"]:
                 mgr = st["m_mgr"]
                 flags |= _lib.TA_M_COSTATE
@@ -268,7 +346,17 @@ class TurboAdam(Optimizer):
             ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)
             self._ws[dev] = ws
         groups = np.zeros(len(self.param_groups), dtype=_lib.GROUP_DTYPE)
-        return {"key": tuple(id(p) for _, p in items), "arr": arr, "groups": groups}
+        cb, hb = self._xbytes
+        if cb + hb:
+            if len({pp.device for _, pp in items}) != 1 or (self._xbuf and dev not in self._xbuf):
+                raise NotImplementedError("a sharded step keeps all of a rank's parameters on one "
+                                          "device")
+            xb = self._xbuf.get(dev)
+            if xb is None:
+                xb = torch.zeros(cb + hb, dtype=torch.uint8, device=dev)
+                self._xbuf[dev] = xb
+        return {"key": tuple(id(p) for _, p in items), "arr": arr, "groups": groups,
+                "xbytes": cb + hb, "chunk_bytes": cb, "hist_bytes": hb}
 
     def _run_device(self, dev, items, bcs):
         lib = _lib.load()
@@ -329,6 +417,37 @@ class TurboAdam(Optimizer):
             g["block_size"] = group["block_size"]
             g["v_bits"] = group["v_bits"]
         ws = self._ws[dev]
+        if plan["xbytes"]:  # tensors split over ranks: the phased step
+            xb = self._xbuf[dev]
+            cb, hb = plan["chunk_bytes"], plan["hist_bytes"]
+            evs = self._phase_events
+            cur = torch.cuda.current_stream(dev)
+            for phase in range(_lib.TA_PHASE_LABELS + 1):
+                if evs is not None and phase == _lib.TA_PHASE_PASS1:
+                    evs[0].record(cur)
+                with torch.cuda.device(dev):
+                    rc = lib.ta_step_phase(arr.ctypes.data, len(items), groups.ctypes.data,
+                                           len(groups), self._seed, ws.data_ptr(), ws.numel(),
+                                           xb.data_ptr(), cb, hb, phase, _lib.stream_ptr(dev))
+                _lib.check(rc, "ta_step_phase")
+                if evs is not None:  # pass 1 | (alpha) | alpha, pass 2 | select, labels
+                    if phase == _lib.TA_PHASE_PASS1:
+                        evs[1].record(cur)
+                        evs[2].record(cur)
+                    elif phase == _lib.TA_PHASE_PASS2:
+                        evs[3].record(cur)
+                    elif phase == _lib.TA_PHASE_LABELS:
+                        evs[4].record(cur)
+                if phase == _lib.TA_PHASE_PASS1:
+                    yield xb[:cb].view(torch.float64)
+                elif phase < _lib.TA_PHASE_LABELS:
+                    yield xb[cb:cb + hb].view(torch.int32)
+            for _, p in items:
+                mgr = self.state[p].get("m_mgr")
+                if mgr is not None:
+                    mgr.mark_updated()
+            del keep
+            return
         with torch.cuda.device(dev):
             if self._phase_events is None:
                 rc = lib.ta_step(arr.ctypes.data, len(items), groups.ctypes.data, len(groups),

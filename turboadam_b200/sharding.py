@@ -50,3 +50,54 @@ def rank_loads(numels: Sequence[int], world: int) -> list[int]:
     for n, r in zip(numels, lpt_owners(numels, world)):
         load[r] += int(n)
     return load
+
+
+ALIGN_BLOCKS = 4096  # TA_SHARD_ALIGN_BLOCKS: one alpha reduction chunk
+
+
+def zero1_partition(numels: Sequence[int], world: int, block_size: int = 128):
+    """ZeRO-1 flat partition of a parameter set (all tensors concatenated in
+    order) into ``world`` contiguous ranges of about equal size. A cut inside a
+    tensor is moved to the nearest multiple of ALIGN_BLOCKS blocks of that
+    tensor (or to its start / end), so no alpha reduction chunk straddles two
+    ranks. Returns, per rank, a list of shards
+    ``(tensor_index, elem_lo, elem_hi, block_offset, global_numel)``."""
+    if world < 1:
+        raise ValueError(f"world size must be >= 1, got {world}")
+    numels = [int(n) for n in numels]
+    starts = [0]
+    for n in numels:
+        starts.append(starts[-1] + n)
+    total = starts[-1]
+    align = ALIGN_BLOCKS * block_size
+    cuts = [0]
+    for r in range(1, world):
+        x = (total * r) // world
+        t = max(i for i in range(len(numels)) if starts[i] <= x) if numels else 0
+        off = x - starts[t]
+        snapped = min(numels[t], int(round(off / align)) * align) if numels else 0
+        cuts.append(max(cuts[-1], starts[t] + snapped))
+    cuts.append(total)
+    out = []
+    for r in range(world):
+        lo, hi = cuts[r], cuts[r + 1]
+        mine = []
+        for t, n in enumerate(numels):
+            a, b = max(lo, starts[t]), min(hi, starts[t] + n)
+            if a < b:
+                e0, e1 = a - starts[t], b - starts[t]
+                mine.append((t, e0, e1, e0 // block_size, n))
+        out.append(mine)
+    return out
+
+
+def zero1_spanning(partition):
+    """The job's tensors that a zero1_partition splits over ranks, as
+    ``(tensor_index, global_numel)`` in tensor order (the same on every
+    rank): the ``spanning`` argument of TurboAdam."""
+    count, numel = {}, {}
+    for shards in partition:
+        for t, _, _, _, gn in shards:
+            count[t] = count.get(t, 0) + 1
+            numel[t] = gn
+    return [(t, numel[t]) for t in sorted(count) if count[t] > 1]
