@@ -65,7 +65,8 @@ enum {
 /* device status bits (ta_read_status) */
 enum {
   TA_STATUS_NONFINITE_GRAD = 1u << 0,
-  TA_STATUS_WAIT_TIMEOUT = 1u << 1
+  TA_STATUS_WAIT_TIMEOUT = 1u << 1,
+  TA_STATUS_BIAS_TABLE_SHORT = 1u << 2  /* ta_step_prepared ran past its bias table */
 };
 
 /*
@@ -168,6 +169,47 @@ TA_API ta_status ta_step_profiled(const ta_tensor* tensors, int32_t n_tensors,
                                   const ta_group* groups, int32_t n_groups, uint64_t seed,
                                   void* workspace_dev, size_t workspace_bytes, void* stream,
                                   void* const* phase_events);
+
+/*
+ * Device-resident per-step values of a CUDA-graph-capturable step
+ * (ta_step_prepared), so that a graph replay needs nothing from the host.
+ */
+typedef struct ta_dynamic {
+  int32_t* steps_dev;           /* [n_tensors] step counts; each step adds 1     */
+  const float* bias_table_dev;  /* [n_groups][table_steps][2] fp32 (1 - beta1^t,
+                                   1 - beta2^t) for t = 1..table_steps, computed
+                                   on the host exactly as optimizer.py:172-188  */
+  int64_t table_steps;
+  const double* lr_dev;         /* optional [n_groups] learning rates (else ta_group.lr) */
+  const float* grad_scale_dev;  /* optional [1]: AMP loss scale; gradients enter
+                                   the step multiplied by RN(1 / scale), as
+                                   GradScaler.unscale_ leaves them           */
+  const float* found_inf_dev;   /* optional [1]: nonzero skips the whole step
+                                   (step counts included)                    */
+} ta_dynamic;
+
+/*
+ * Uploads the descriptor table of a tensor list into the workspace (one
+ * stream-ordered host-to-device copy). Call it outside any stream capture,
+ * again whenever a pointer, size or group setting changes.
+ * No counterpart in the reference (capturable=True raises there).
+ */
+TA_API ta_status ta_plan_prepare(const ta_tensor* tensors, int32_t n_tensors,
+                                 const ta_group* groups, int32_t n_groups, uint64_t seed,
+                                 void* workspace_dev, size_t workspace_bytes, void* stream);
+
+/*
+ * ta_step on a prepared workspace with its per-step values taken from device
+ * memory: one small kernel advances the step counts, bias corrections, flags
+ * and (optional) learning rates and loss scale, then the step's kernels run.
+ * Only kernel launches: it can be captured into a CUDA graph and replayed.
+ * The step / TA_M_HAS_STATE fields of `tensors` are ignored (device counts).
+ * No counterpart in the reference.
+ */
+TA_API ta_status ta_step_prepared(const ta_tensor* tensors, int32_t n_tensors,
+                                  const ta_group* groups, int32_t n_groups, uint64_t seed,
+                                  void* workspace_dev, size_t workspace_bytes,
+                                  const ta_dynamic* dyn, void* stream);
 
 /*
  * Layout of the exchange buffer of a sharded step, the same on every rank:

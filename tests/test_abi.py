@@ -30,7 +30,7 @@ def test_header_symbols_exported(lib):
     from turboadam_b200 import _lib
 
     names = declared_symbols()
-    assert len(names) == 17
+    assert len(names) == 19
     assert sorted(_lib.EXPORTED) == names
     for n in names:
         assert hasattr(lib, n), n
@@ -139,8 +139,9 @@ def test_optimizer_constructor_api():
     assert TurboAdam(p, block_size=64, v_bits=6).defaults["v_bits"] == 6
     with pytest.raises(ValueError, match="v_bits must be one of"):
         TurboAdam(p, v_bits=10)
-    with pytest.raises(NotImplementedError, match="CUDA graph capture"):
-        TurboAdam(p, capturable=True)
+    # capturable=True, which the reference refuses, is built here
+    assert TurboAdam(p, capturable=True)._capturable
+    assert TurboAdam._step_supports_amp_scaling
 
 
 def test_cpu_params_fail_loudly():

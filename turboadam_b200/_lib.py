@@ -27,6 +27,7 @@ TA_PHASE_PASS1, TA_PHASE_PASS2, TA_PHASE_SEL1, TA_PHASE_SEL2, TA_PHASE_LABELS = 
 TA_SHARD_ALIGN_BLOCKS = 4096
 TA_STATUS_NONFINITE_GRAD = 1 << 0
 TA_STATUS_WAIT_TIMEOUT = 1 << 1
+TA_STATUS_BIAS_TABLE_SHORT = 1 << 2
 
 STATUS_NAMES = {
     1: "TA_ERR_INVALID",
@@ -55,6 +56,8 @@ EXPORTED = (
     "ta_aux_workspace_size",
     "ta_exchange_layout",
     "ta_step_phase",
+    "ta_plan_prepare",
+    "ta_step_prepared",
 )
 
 
@@ -106,6 +109,17 @@ class TaGroup(ctypes.Structure):
         ("bc2", ctypes.c_float),
         ("block_size", ctypes.c_int32),
         ("v_bits", ctypes.c_int32),
+    ]
+
+
+class TaDynamic(ctypes.Structure):
+    _fields_ = [
+        ("steps_dev", ctypes.c_void_p),
+        ("bias_table_dev", ctypes.c_void_p),
+        ("table_steps", ctypes.c_int64),
+        ("lr_dev", ctypes.c_void_p),
+        ("grad_scale_dev", ctypes.c_void_p),
+        ("found_inf_dev", ctypes.c_void_p),
     ]
 
 
@@ -168,6 +182,10 @@ _SIG = {
     "ta_step_phase": (ctypes.c_int, [_P, ctypes.c_int32, _P, ctypes.c_int32, ctypes.c_uint64, _P,
                                      ctypes.c_size_t, _P, ctypes.c_size_t, ctypes.c_size_t,
                                      ctypes.c_int32, _P]),
+    "ta_plan_prepare": (ctypes.c_int, [_P, ctypes.c_int32, _P, ctypes.c_int32, ctypes.c_uint64, _P,
+                                       ctypes.c_size_t, _P]),
+    "ta_step_prepared": (ctypes.c_int, [_P, ctypes.c_int32, _P, ctypes.c_int32, ctypes.c_uint64,
+                                        _P, ctypes.c_size_t, ctypes.POINTER(TaDynamic), _P]),
 }
 
 _lib = None

@@ -22,6 +22,7 @@ import numpy as np
 import torch
 
 from .costate import CoStateManager
+from .oneq import adopt_compressed_v
 
 FORMAT = "turboadam_b200/portable-1"
 
@@ -117,4 +118,18 @@ def load_portable_state_dict(opt, sd: dict) -> None:
                 o[name] = v
         state[k] = o
     opt.load_state_dict({"state": state, "param_groups": sd["param_groups"]})
+    # torch casts floating state to the parameter's dtype on load (lossy for
+    # bf16 parameters: fp16 headers, fp32 moments); put the exact values back
+    ids = [i for g in sd["param_groups"] for i in g["params"]]
+    params = [p for g in opt.param_groups for p in g["params"]]
+    for k, p in zip(ids, params):
+        if k not in state or p not in opt.state:
+            continue
+        src, dst = state[k], opt.state[p]
+        if "compressed_v" in src:
+            dst["compressed_v"] = adopt_compressed_v(src["compressed_v"], p.device)
+        for name in ("exp_avg", "exp_avg_sq"):
+            if name in src:
+                dst[name] = src[name].to(device=p.device, dtype=torch.float32).contiguous()
+    opt._plans = None
     opt._seed = int(sd["seed"]) & 0xFFFFFFFFFFFFFFFF

@@ -301,6 +301,9 @@ DevTensor make_dev(const ta_tensor& t, const ta_group& g, uint64_t seed) {
   D.sel_chunks = (int32_t)cdiv(D.bpad, SEL_CHUNK);
   D.alpha_chunks = (int32_t)cdiv(D.bpad / TB, FIN_THREADS);
   D.one = 1.0f;
+  D.group = t.group;
+  D.ginv = 1.0f;
+  D.wdd = g.weight_decay;
   return D;
 }
 
@@ -376,7 +379,9 @@ ta_status run_phase(int phase, const std::vector<std::pair<P1Key, LaunchList>>& 
 ta_status run_step(const ta_tensor* ts, int nT, const ta_group* groups, uint64_t seed,
                    uint8_t* ws, size_t ws_bytes, cudaStream_t st, void* const* ev = nullptr,
                    int phase = -1, uint8_t* exch = nullptr, size_t chunk_bytes = 0,
-                   size_t hist_bytes = 0) {
+                   size_t hist_bytes = 0, int mode = 0, const ta_dynamic* dyn = nullptr) {
+  // mode 0: upload the descriptor table and run; 1: upload only (prepare);
+  // 2: run on a prepared table with device-advanced step values (no copies)
   auto mark = [&](int i) -> cudaError_t {
     if (ev && ev[i]) return cudaEventRecord((cudaEvent_t)ev[i], st);
     return cudaSuccess;
@@ -494,6 +499,7 @@ ta_status run_step(const ta_tensor* ts, int nT, const ta_group* groups, uint64_t
   };
   std::vector<KParams> p1k(p1.size());
   uint32_t* status = reinterpret_cast<uint32_t*>(ws + L.status);
+  uint32_t* skip = mode == 2 ? status + 1 : nullptr;
   const DevTensor* dT = reinterpret_cast<const DevTensor*>(ws + L.table);
   for (size_t i = 0; i < p1.size(); ++i) {
     KParams& kp = p1k[i];
@@ -502,6 +508,7 @@ ta_status run_step(const ta_tensor* ts, int nT, const ta_group* groups, uint64_t
     kp.nl = (int32_t)p1[i].second.idx.size();
     kp.total = p1[i].second.beg.back();
     kp.status = status;
+    kp.skip = skip;
     set_rk(kp);
   }
   KParams p2k[2];
@@ -511,20 +518,24 @@ ta_status run_step(const ta_tensor* ts, int nT, const ta_group* groups, uint64_t
     p2k[pt].nl = (int32_t)p2[pt].idx.size();
     p2k[pt].total = p2[pt].beg.back();
     p2k[pt].status = status;
+    p2k[pt].skip = skip;
     set_rk(p2k[pt]);
   }
   SelParams sp;
   sp.T = dT;
+  sp.skip = skip;
   put(sel, &sp.cbeg, &sp.cidx);
   sp.ncs = (int32_t)sel.idx.size();
   const int64_t nchunks = sel.beg.back();
   SelParams ap;
   ap.T = dT;
+  ap.skip = skip;
   put(alist, &ap.cbeg, &ap.cidx);
   ap.ncs = (int32_t)alist.idx.size();
   const int64_t achunks = alist.beg.back();
   SelParams xsp, xap, xp;
   xsp.T = xap.T = xp.T = dT;
+  xsp.skip = xap.skip = xp.skip = skip;
   put(xsel, &xsp.cbeg, &xsp.cidx);
   xsp.ncs = (int32_t)xsel.idx.size();
   put(xalist, &xap.cbeg, &xap.cidx);
@@ -535,8 +546,25 @@ ta_status run_step(const ta_tensor* ts, int nT, const ta_group* groups, uint64_t
   const unsigned xsel_chunks = (unsigned)xsel.beg.back();
   const unsigned xa_chunks = (unsigned)xalist.beg.back();
 
-  TA_CU(cudaMemcpyAsync(ws + L.table, host.data() + L.table, host.size() - L.table,
-                        cudaMemcpyHostToDevice, st));
+  if (mode != 2)
+    TA_CU(cudaMemcpyAsync(ws + L.table, host.data() + L.table, host.size() - L.table,
+                          cudaMemcpyHostToDevice, st));
+  if (mode == 1) return TA_OK;
+  if (mode == 2) {
+    AdvParams a;
+    a.T = reinterpret_cast<DevTensor*>(ws + L.table);
+    a.n = nT;
+    a.steps = dyn->steps_dev;
+    a.table = dyn->bias_table_dev;
+    a.tsteps = dyn->table_steps;
+    a.lr = dyn->lr_dev;
+    a.gscale = dyn->grad_scale_dev;
+    a.finf = dyn->found_inf_dev;
+    a.skip = skip;
+    a.status = status;
+    k_advance<<<(unsigned)std::max<int64_t>(1, cdiv(nT, 256)), 256, 0, st>>>(a);
+    TA_CU(cudaGetLastError());
+  }
   if (phase >= 0) return run_phase(phase, p1, p1k, p2k, ap, achunks, sp, nchunks, xap, xa_chunks,
                                    xsp, xsel_chunks, xp, nx, exch, chunk_bytes, hist_bytes, st);
   TA_CU(mark(0));
@@ -661,6 +689,46 @@ ta_status ta_step_phase(const ta_tensor* tensors, int32_t n_tensors, const ta_gr
   return run_step(tensors, n_tensors, groups, seed, (uint8_t*)workspace_dev, workspace_bytes,
                   (cudaStream_t)stream, nullptr, phase, (uint8_t*)exchange_dev, chunk_bytes,
                   hist_bytes);
+}
+
+ta_status ta_plan_prepare(const ta_tensor* tensors, int32_t n_tensors, const ta_group* groups,
+                          int32_t n_groups, uint64_t seed, void* workspace_dev,
+                          size_t workspace_bytes, void* stream) {
+  g_err.clear();
+  if (n_tensors < 0 || (n_tensors > 0 && (!tensors || !groups)) || n_groups < 0)
+    return fail(TA_ERR_INVALID, "bad tensor / group arrays");
+  if (!workspace_dev || !aligned16(workspace_dev))
+    return fail(TA_ERR_INVALID, "workspace must be a 16-byte aligned device pointer");
+  for (int i = 0; i < n_tensors; ++i) {
+    ta_tensor t = tensors[i];
+    if (t.step == 0) t.step = 1;  // the device advances the counts
+    ta_status r = validate(t, i, n_groups, groups);
+    if (r != TA_OK) return r;
+  }
+  return run_step(tensors, n_tensors, groups, seed, (uint8_t*)workspace_dev, workspace_bytes,
+                  (cudaStream_t)stream, nullptr, -1, nullptr, 0, 0, 1, nullptr);
+}
+
+ta_status ta_step_prepared(const ta_tensor* tensors, int32_t n_tensors, const ta_group* groups,
+                           int32_t n_groups, uint64_t seed, void* workspace_dev,
+                           size_t workspace_bytes, const ta_dynamic* dyn, void* stream) {
+  g_err.clear();
+  if (n_tensors < 0 || (n_tensors > 0 && (!tensors || !groups)) || n_groups < 0)
+    return fail(TA_ERR_INVALID, "bad tensor / group arrays");
+  if (!workspace_dev || !aligned16(workspace_dev))
+    return fail(TA_ERR_INVALID, "workspace must be a 16-byte aligned device pointer");
+  if (!dyn || !dyn->steps_dev || !dyn->bias_table_dev || dyn->table_steps <= 0)
+    return fail(TA_ERR_INVALID, "ta_dynamic needs steps_dev and a bias table");
+  for (int i = 0; i < n_tensors; ++i) {
+    ta_tensor t = tensors[i];
+    if (t.step == 0) t.step = 1;
+    if (t.flags & TA_M_SPANNING)
+      return fail(TA_ERR_UNSUPPORTED, "the prepared step does not take split tensors");
+    ta_status r = validate(t, i, n_groups, groups);
+    if (r != TA_OK) return r;
+  }
+  return run_step(tensors, n_tensors, groups, seed, (uint8_t*)workspace_dev, workspace_bytes,
+                  (cudaStream_t)stream, nullptr, -1, nullptr, 0, 0, 2, dyn);
 }
 
 ta_status ta_read_status(void* workspace_dev, int32_t clear, uint32_t* status_out,

@@ -40,6 +40,7 @@ enum : uint32_t {
   DF_V_OUT = 1u << 12,
   DF_BF16 = 1u << 13,
   DF_SPAN = 1u << 4,  // == TA_M_SPANNING
+  DF_AMP = 1u << 14,  // gradients are multiplied by ginv on load
 };
 
 // Per-tensor descriptor, built on the host, uploaded into the workspace.
@@ -87,6 +88,10 @@ struct __align__(16) DevTensor {
   int64_t coff;        // global chunk index of local chunk 0
   double* xchunk;      // exchange: [2][cglob] fp64 chunk sums
   uint32_t* xhist;     // exchange: [2][HBINS] histogram counts
+  // device-advanced steps (ta_step_prepared)
+  int32_t group;
+  float ginv;          // RN(1 / loss scale) when DF_AMP
+  double wdd;          // weight decay (wdf = fl(1 - lr * wd) from a device lr)
 };
 
 // sel[] layout

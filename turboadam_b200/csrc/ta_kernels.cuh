@@ -123,6 +123,7 @@ struct __align__(16) Sc {
   float rnbf;   // 2^-nbits (exact)
   float one;    // 1 and -0 as runtime values: the identity operands of PK
   float nzero;
+  float ginv;   // DF_AMP: RN(1 / loss scale)
 };
 
 __device__ __forceinline__ Sc load_sc(const DevTensor& D) {
@@ -135,6 +136,7 @@ __device__ __forceinline__ Sc load_sc(const DevTensor& D) {
   s.rnbf = __uint_as_float((uint32_t)(127 - D.nbits) << 23);
   s.one = D.one;
   s.nzero = -0.0f * D.one;
+  s.ginv = D.ginv;
   return s;
 }
 
@@ -170,8 +172,13 @@ struct KParams {
   int32_t nl;
   int64_t total;        // tiles in this launch
   uint32_t* status;
+  const uint32_t* skip;       // optional: nonzero -> the step is skipped (AMP found_inf)
   uint32_t rk0[10], rk1[10];  // Philox round keys (seed words + r * Weyl constants)
 };
+// A skipped step (AMP found_inf) leaves every kernel of it without effect.
+__device__ __forceinline__ bool step_skipped(const uint32_t* skip) {
+  return skip != nullptr && *reinterpret_cast<const volatile uint32_t*>(skip) != 0u;
+}
 
 __device__ __forceinline__ int find_entry(const int64_t* lbeg, int nl, int64_t tile) {
   int lo = 0, hi = nl - 1;
@@ -425,6 +432,14 @@ __device__ __forceinline__ void st_quad(void* p, int64_t e, float4 v) {
 
 // bf16 parameters: p * (1 - lr*wd) is rounded to bf16 before the update
 // (torch computes the in-place op in fp32 and stores bf16).
+// GradScaler.unscale_ of one gradient: fl(g * inv_scale) in fp32, stored back
+// in the gradient's dtype (bf16 gradients round again).
+template <int PT>
+__device__ __forceinline__ float amp_unscale(float g, float ginv) {
+  const float u = __fmul_rn(g, ginv);
+  return PT ? ta_bf16_to_f32(ta_f32_to_bf16(u)) : u;
+}
+
 template <int PT>
 __device__ __forceinline__ float2 round_param2(float2 v) {
   if (PT) return make_float2(ta_bf16_to_f32(ta_f32_to_bf16(v.x)), ta_bf16_to_f32(ta_f32_to_bf16(v.y)));
@@ -500,7 +515,8 @@ __device__ __noinline__ float p1_fix_elem(const StageMeta& M, const uint8_t* st,
                                           float span, uint32_t* status) {
   using L = P1L<MK, VK, PT, UNI>;
   const Sc c = M.c;
-  const float g = ld_smem_elem<PT>(st + L::OFF_G + L::AP::off(bi), t);
+  float g = ld_smem_elem<PT>(st + L::OFF_G + L::AP::off(bi), t);
+  if (c.flags & DF_AMP) g = amp_unscale<PT>(g, c.ginv);
   if (!(fabsf(g) <= 3.4028234663852886e38f)) atomicOr(status, 1u);
   float m = 0.0f;
   if (MK == MK_COSTATE) {
@@ -673,7 +689,11 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
       const int t0 = 4 * j + 32 * k;
       const int64_t e = e0 + t0;
       const float4 g4 = ld_quad<PT>(sg, t0);
-      const float2 g01 = lo2(g4), g23 = hi2(g4);
+      float2 g01 = lo2(g4), g23 = hi2(g4);
+      if (c.flags & DF_AMP) {  // GradScaler.unscale_: g * RN(1 / scale), stored in g's dtype
+        g01 = round_param2<PT>(P.mul(g01, dup2(c.ginv)));
+        g23 = round_param2<PT>(P.mul(g23, dup2(c.ginv)));
+      }
       float2 m01 = zero2, m23 = zero2;
       if (MK == MK_COSTATE) {
         const uint32_t sb = sw0 << sshift;
@@ -781,6 +801,7 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
         float g;
         if (fullblk) g = ld_smem_elem<PT>(sg, t);
         else g = ve ? to_f32<PT>(D->g, e) : 0.0f;
+        if (c.flags & DF_AMP) g = amp_unscale<PT>(g, c.ginv);
         gbad = __fmaf_rn(g, 0.0f, gbad);
         float m = 0.0f;
         if (MK == MK_COSTATE) {
@@ -935,6 +956,7 @@ __device__ __forceinline__ void fill_meta_common(StageMeta& m, const DevTensor& 
 
 template <int MK, int VK, int PT, bool UNI, bool TABLE>
 __global__ void __launch_bounds__(NTHR, 4) k_pass1(const __grid_constant__ KParams kp) {
+  if (step_skipped(kp.skip)) return;
   using L = P1L<MK, VK, PT, UNI>;
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* stages = smem;
@@ -1036,7 +1058,9 @@ struct SelParams {
   const int64_t* cbeg;  // [ncs + 1] chunk prefix
   const int32_t* cidx;  // [ncs] tensor indices
   int32_t ncs;
+  const uint32_t* skip;  // optional: nonzero -> the step is skipped
 };
+
 
 // fp64 sums (m.g, g.g) of chunk c of a tensor: thread t sums the 16 block
 // partials of tile 256c + t in block order, then 32-wide xor butterflies and
@@ -1101,6 +1125,7 @@ __device__ __forceinline__ void alpha_finish(const DevTensor& D, const double* c
 }
 
 __global__ void __launch_bounds__(FIN_THREADS) k_alpha(const __grid_constant__ SelParams sp) {
+  if (step_skipped(sp.skip)) return;
   const int tid = threadIdx.x;
   const int64_t chunk = blockIdx.x;
   const int en = find_entry(sp.cbeg, sp.ncs, chunk);
@@ -1125,6 +1150,7 @@ __global__ void __launch_bounds__(FIN_THREADS) k_alpha(const __grid_constant__ S
 // chunk positions of the exchange buffer (zero elsewhere); after the caller's
 // all-reduce, every rank sums all chunks in global order.
 __global__ void __launch_bounds__(FIN_THREADS) k_alpha_part(const __grid_constant__ SelParams sp) {
+  if (step_skipped(sp.skip)) return;
   const int64_t chunk = blockIdx.x;
   const int en = find_entry(sp.cbeg, sp.ncs, chunk);
   const DevTensor& D = sp.T[sp.cidx[en]];
@@ -1138,6 +1164,7 @@ __global__ void __launch_bounds__(FIN_THREADS) k_alpha_part(const __grid_constan
 }
 
 __global__ void __launch_bounds__(FIN_THREADS) k_alpha_fin(const __grid_constant__ SelParams sp) {
+  if (step_skipped(sp.skip)) return;
   const DevTensor& D = sp.T[sp.cidx[blockIdx.x]];
   alpha_finish(D, D.xchunk, D.cglob, D.cglob);
 }
@@ -1149,7 +1176,7 @@ template <int PT, bool FULL>
 __device__ __forceinline__ void p2_block(const DevTensor* T, const StageMeta& M,
                                          const uint8_t* st, uint2* wb) {
   using L = P2L<PT>;
-  const float b1 = M.c.b1, omb1 = M.c.omb1, sqbs = M.c.sqbs;
+  const float b1 = M.c.b1, omb1 = M.c.omb1, sqbs = M.c.sqbs, ginv = M.c.ginv;
   const uint32_t flags = M.c.flags;
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -1190,8 +1217,9 @@ __device__ __forceinline__ void p2_block(const DevTensor* T, const StageMeta& M,
 #pragma unroll
       for (int i = 0; i < 4; i += 2) {
         const int k = 4 * kq + i;
-        const float2 g = make_float2(ld_smem_elem<PT>(sg, j + 8 * k),
-                                     ld_smem_elem<PT>(sg, j + 8 * k + 8));
+        float2 g = make_float2(ld_smem_elem<PT>(sg, j + 8 * k),
+                               ld_smem_elem<PT>(sg, j + 8 * k + 8));
+        if (flags & DF_AMP) g = round_param2<PT>(P.mul(g, dup2(ginv)));
         const uint32_t s0 = (sw >> (8 * i + 7 - j)) & 1u, s1 = (sw >> (8 * i + 15 - j)) & 1u;
         const float2 sd = make_float2(__uint_as_float(sc ^ (s0 << 31)),
                                       __uint_as_float(sc ^ (s1 << 31)));
@@ -1219,6 +1247,7 @@ __device__ __forceinline__ void p2_block(const DevTensor* T, const StageMeta& M,
         float g;
         if (fullblk) g = ld_smem_elem<PT>(sg, t);
         else g = ve ? to_f32<PT>(D->g, e0 + t) : 0.0f;
+        if (flags & DF_AMP) g = amp_unscale<PT>(g, ginv);
         const uint32_t bit = (sw >> (8 * i + 7 - j)) & 1u;
         const float m = costate_m(g, alpha_old, cs_scale, bit, has_state, b1, omb1);
         const float dl = ve ? __fsub_rn(m, __fmul_rn(alpha, g)) : 0.0f;  // costate.py:42
@@ -1272,6 +1301,7 @@ __device__ __noinline__ void p2_block_general(const DevTensor* T, const StageMet
 
 template <int PT>
 __global__ void __launch_bounds__(NTHR) k_pass2(const __grid_constant__ KParams kp) {
+  if (step_skipped(kp.skip)) return;
   using L = P2L<PT>;
   using AG = typename L::AG;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -1487,6 +1517,7 @@ __device__ __forceinline__ void sel_pick(const DevTensor& D, const uint32_t* gh)
 
 template <int R>
 __global__ void __launch_bounds__(SEL_THREADS) k_select(const __grid_constant__ SelParams sp) {
+  if (step_skipped(sp.skip)) return;
   __shared__ int last;
   const int tid = threadIdx.x;
   const int64_t chunk = blockIdx.x;
@@ -1508,6 +1539,7 @@ __global__ void __launch_bounds__(SEL_THREADS) k_select(const __grid_constant__ 
 // buffer (zeroed by the host first), pick from the all-reduced histogram.
 template <int R>
 __global__ void __launch_bounds__(SEL_THREADS) k_hist(const __grid_constant__ SelParams sp) {
+  if (step_skipped(sp.skip)) return;
   const int64_t chunk = blockIdx.x;
   const int en = find_entry(sp.cbeg, sp.ncs, chunk);
   const DevTensor& D = sp.T[sp.cidx[en]];
@@ -1516,11 +1548,13 @@ __global__ void __launch_bounds__(SEL_THREADS) k_hist(const __grid_constant__ Se
 
 template <int R>
 __global__ void __launch_bounds__(SEL_THREADS) k_pick(const __grid_constant__ SelParams sp) {
+  if (step_skipped(sp.skip)) return;
   sel_pick<R>(sp.T[sp.cidx[blockIdx.x]], sp.T[sp.cidx[blockIdx.x]].xhist);
 }
 
 // labels (costate.py:126-149) and commit alpha (costate.py:443-456)
 __global__ void __launch_bounds__(SEL_THREADS) k_labels(const __grid_constant__ SelParams sp) {
+  if (step_skipped(sp.skip)) return;
   const int64_t chunk = blockIdx.x;
   const int en = find_entry(sp.cbeg, sp.ncs, chunk);
   const DevTensor& D = sp.T[sp.cidx[en]];
@@ -1536,6 +1570,62 @@ __global__ void __launch_bounds__(SEL_THREADS) k_labels(const __grid_constant__ 
     D.lab[i] = l;
   }
   if (c == 0 && threadIdx.x == 0 && D.alpha_state) *D.alpha_state = D.alpha_new[0];
+}
+
+// ---------------------------------------------------------------------------
+// Device-advanced step values (ta_step_prepared): step counts, bias
+// corrections from the host-computed table, CoState has-state flags, and the
+// optional device learning rates and AMP loss scale, written into the
+// descriptor table before the step's kernels read it.
+// ---------------------------------------------------------------------------
+struct AdvParams {
+  DevTensor* T;
+  int32_t n;
+  int32_t* steps;
+  const float* table;    // [groups][tsteps][2]
+  int64_t tsteps;
+  const double* lr;      // optional [groups]
+  const float* gscale;   // optional [1]
+  const float* finf;     // optional [1]
+  uint32_t* skip;
+  uint32_t* status;
+};
+
+__global__ void __launch_bounds__(256) k_advance(const __grid_constant__ AdvParams a) {
+  const bool skip = a.finf != nullptr && *a.finf != 0.0f;
+  if (blockIdx.x == 0 && threadIdx.x == 0) *a.skip = skip ? 1u : 0u;
+  if (skip) return;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < a.n; i += gridDim.x * blockDim.x) {
+    DevTensor& D = a.T[i];
+    if (D.n == 0) continue;
+    const int32_t s = a.steps[i] + 1;  // optimizer.py:103
+    a.steps[i] = s;
+    D.step = (uint32_t)s;
+    int64_t te = (int64_t)s - 1;
+    if (te >= a.tsteps) {
+      atomicOr(a.status, 4u);  // TA_STATUS_BIAS_TABLE_SHORT
+      te = a.tsteps - 1;
+    }
+    const float* bc = a.table + ((int64_t)D.group * a.tsteps + te) * 2;
+    D.bc1 = bc[0];
+    D.bc2 = bc[1];
+    D.rbc2 = __fdiv_rn(1.0f, bc[1]);
+    if (D.flags & DF_M_COSTATE) {  // a previous encoding exists from step 2 on
+      if (s > 1) D.flags |= DF_M_HAS_STATE;
+      else D.flags &= ~DF_M_HAS_STATE;
+    }
+    if (a.lr != nullptr) {  // optimizer.py:106, 170 with the scalars rounded as torch does
+      const double lr = a.lr[D.group];
+      D.nlr = __double2float_rn(-lr);
+      D.wdf = __double2float_rn(__dsub_rn(1.0, __dmul_rn(lr, D.wdd)));
+    }
+    if (a.gscale != nullptr) {
+      D.ginv = __double2float_rn(__drcp_rn((double)*a.gscale));
+      D.flags |= DF_AMP;
+    } else {
+      D.flags &= ~DF_AMP;
+    }
+  }
 }
 
 }  // namespace ta

@@ -27,10 +27,32 @@ from .oneq import adopt_compressed_v, init_compressed_v, is_padded, storage_capa
 _DTYPES = {torch.float32: _lib.TA_F32, torch.bfloat16: _lib.TA_BF16}
 
 
+# steps covered by the device bias-correction table of a capturable optimizer
+CAPTURE_TABLE_STEPS = 1 << 20
+
+
+def _bias_table(betas, steps):
+    """fp32 (1 - beta1^t, 1 - beta2^t) for t = 1..steps, each computed in
+    Python float arithmetic exactly as the step does (optimizer.py:172-188)."""
+    b1, b2 = float(betas[0]), float(betas[1])
+    t = np.empty((steps, 2), np.float32)
+    t[:, 0] = [1.0 - b1 ** k for k in range(1, steps + 1)]
+    t[:, 1] = [1.0 - b2 ** k for k in range(1, steps + 1)]
+    return t
+
+
 class TurboAdam(Optimizer):
     """Adam with CoState-compressed m and 1Q log-scale v (reference API).
 
-    Args mirror the reference (optimizer.py:44-81). Keyword-only extras:
+    Args mirror the reference (optimizer.py:44-81); ``capturable=True`` (which
+    the reference refuses) keeps step counts, bias corrections and the AMP
+    loss scale on the device so ``step()`` can be captured into a CUDA graph
+    (the first step runs outside capture; gradients must stay at fixed
+    addresses). With torch.amp.GradScaler the optimizer takes the
+    ``grad_scale`` / ``found_inf`` hand-off (``_step_supports_amp_scaling``):
+    gradients are used as ``g * RN(1/scale)``, what ``GradScaler.unscale_``
+    would leave, and a step with ``found_inf`` set changes nothing.
+    Keyword-only extras:
     ``seed`` keys the stochastic-rounding generator (default
     torch.initial_seed()); ``tensor_ids`` gives each parameter (in the order
     the constructor's param groups list them) the id that keys its rounding
@@ -48,6 +70,10 @@ class TurboAdam(Optimizer):
     between them -- on every rank, also one that holds no split tensor -- which
     leaves every packed bit equal to the unsharded step's.
     """
+
+    # torch.amp.GradScaler hands over `grad_scale` / `found_inf` instead of
+    # unscaling the gradients itself
+    _step_supports_amp_scaling = True
 
     def __init__(
         self,
@@ -74,9 +100,7 @@ class TurboAdam(Optimizer):
     ):
         if v_bits not in (2, 3, 4, 6, 8):
             raise ValueError(f"v_bits must be one of {{2, 3, 4, 6, 8}}, got {v_bits}")
-        if capturable:
-            raise NotImplementedError(
-                "CUDA graph capture is not yet supported. Set capturable=False.")
+
         defaults = dict(
             lr=lr,
             betas=betas,
@@ -118,6 +142,8 @@ class TurboAdam(Optimizer):
                     raise ValueError("shard (block_offset, global_numel) does not hold the "
                                      "parameter")
                 self._shard[id(p)] = (boff, gnumel)
+        self._capturable = bool(capturable)
+        self._btab = {}
         self._pg = process_group
         self._xbuf = {}
         self._xslot = {}
@@ -269,6 +295,29 @@ class TurboAdam(Optimizer):
                 work.append((gi, p))
         if not work:
             return loss
+        gs = getattr(self, "grad_scale", None)
+        fi = getattr(self, "found_inf", None)
+        if self._capturable:
+            by_dev = {}
+            for gi, p in work:
+                by_dev.setdefault(p.device, []).append((gi, p))
+            for dev, items in by_dev.items():
+                self._run_device_capturable(dev, items, gs, fi)
+            return loss
+        if fi is not None and float(fi) != 0.0:
+            return loss  # GradScaler skips a step whose gradients overflowed
+        if gs is not None:  # GradScaler.unscale_: g *= RN(1 / scale), in place
+            inv = gs.double().reciprocal().float()
+            dummy = torch.zeros(1, dtype=torch.float32, device=inv.device)
+            for dev in {p.device for _, p in work}:
+                grads = [p.grad for _, p in work if p.device == dev]
+                f32 = [g for g in grads if g.dtype == torch.float32]
+                if f32:
+                    torch._amp_foreach_non_finite_check_and_unscale_(f32, dummy.to(dev),
+                                                                     inv.to(dev))
+                for g in grads:  # bf16: the fp32 product rounded back (as on the device)
+                    if g.dtype != torch.float32:
+                        g.mul_(inv.to(dev))
         bcs = self._bias_corrections()
         for gi, (bc1, bc2) in bcs.items():
             for key, gt in self._group_step_tensors.items():
@@ -404,18 +453,7 @@ class TurboAdam(Optimizer):
                 uni[i] = 0
                 ainj[i] = 0
         groups = plan["groups"]
-        for gi, group in enumerate(self.param_groups):
-            g = groups[gi]
-            g["lr"] = group["lr"]
-            g["beta1"], g["beta2"] = group["betas"]
-            g["eps"] = group["eps"]
-            g["weight_decay"] = group["weight_decay"]
-            g["null_pct"] = group["null_pct"]
-            g["amp_pct"] = group["amp_pct"]
-            bc = bcs.get(gi, (np.float32(1.0), np.float32(1.0)))
-            g["bc1"], g["bc2"] = bc
-            g["block_size"] = group["block_size"]
-            g["v_bits"] = group["v_bits"]
+        self._fill_groups(groups, bcs)
         ws = self._ws[dev]
         if plan["xbytes"]:  # tensors split over ranks: the phased step
             xb = self._xbuf[dev]
@@ -465,6 +503,103 @@ class TurboAdam(Optimizer):
         # Temporaries in `keep` were allocated on the current stream, so the
         # caching allocator only reuses them for work ordered after ta_step.
         del keep
+
+    def _fill_groups(self, groups, bcs):
+        for gi, group in enumerate(self.param_groups):
+            g = groups[gi]
+            lr = group["lr"]
+            g["lr"] = float(lr) if not isinstance(lr, torch.Tensor) else float(lr.item())
+            g["beta1"], g["beta2"] = group["betas"]
+            g["eps"] = group["eps"]
+            g["weight_decay"] = group["weight_decay"]
+            g["null_pct"] = group["null_pct"]
+            g["amp_pct"] = group["amp_pct"]
+            bc = bcs.get(gi, (np.float32(1.0), np.float32(1.0)))
+            g["bc1"], g["bc2"] = bc
+            g["block_size"] = group["block_size"]
+            g["v_bits"] = group["v_bits"]
+
+    # ------------------------------------------------------------------
+    def _run_device_capturable(self, dev, items, gs, fi):
+        """capturable=True: the plan (descriptor table, step counts, bias
+        table) is uploaded once; each step is ta_step_prepared, kernel
+        launches only."""
+        lib = _lib.load()
+        if self._plans is None:
+            self._plans = {}
+        plan = self._plans.get(dev)
+        key = tuple(id(p) for _, p in items)
+        gptrs = tuple(p.grad.data_ptr() for _, p in items)
+        if plan is None or plan["key"] != key or plan.get("gptrs") != gptrs:
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("the first capturable step, and any change of parameters or "
+                                   "gradient storage, must run outside CUDA graph capture")
+            for _, p in items:
+                g = p.grad
+                if g.dtype != p.dtype or not g.is_contiguous() or g.data_ptr() % 16:
+                    raise NotImplementedError("capturable steps need contiguous, 16-byte aligned "
+                                              "gradients of the parameter's dtype")
+            plan = self._build_plan(dev, items)
+            arr = plan["arr"]
+            steps = []
+            for i, (gi, p) in enumerate(items):
+                st = self.state[p]
+                s0 = st["step"]
+                s0 = int(s0.item()) if isinstance(s0, torch.Tensor) else int(s0)
+                steps.append(s0)
+                arr[i]["grad_dev"] = p.grad.data_ptr()
+                arr[i]["step"] = s0 + 1
+                mgr = st.get("m_mgr")
+                if mgr is not None and mgr._has_state:
+                    arr[i]["flags"] = int(arr[i]["flags"]) | _lib.TA_M_HAS_STATE
+            groups = plan["groups"]
+            self._fill_groups(groups, {})
+            tables = []
+            for g in self.param_groups:
+                k = (float(g["betas"][0]), float(g["betas"][1]))
+                if k not in self._btab:
+                    self._btab[k] = _bias_table(k, CAPTURE_TABLE_STEPS)
+                tables.append(self._btab[k])
+            plan["table"] = torch.from_numpy(np.stack(tables)).to(dev)
+            plan["steps"] = torch.tensor(steps, dtype=torch.int32, device=dev)
+            plan["gptrs"] = gptrs
+            with torch.cuda.device(dev):
+                rc = lib.ta_plan_prepare(arr.ctypes.data, len(items), groups.ctypes.data,
+                                         len(groups), self._seed, self._ws[dev].data_ptr(),
+                                         self._ws[dev].numel(), _lib.stream_ptr(dev))
+            _lib.check(rc, "ta_plan_prepare")
+            for i, (gi, p) in enumerate(items):
+                self.state[p]["step"] = plan["steps"][i]
+            self._plans[dev] = plan
+        lr_ptr = None
+        if any(isinstance(g["lr"], torch.Tensor) for g in self.param_groups):
+            if "lr" not in plan:
+                plan["lr"] = torch.zeros(len(self.param_groups), dtype=torch.float64, device=dev)
+            for gi, g in enumerate(self.param_groups):
+                if isinstance(g["lr"], torch.Tensor):
+                    plan["lr"][gi].copy_(g["lr"])
+                else:
+                    plan["lr"][gi].fill_(float(g["lr"]))
+            lr_ptr = plan["lr"].data_ptr()
+        for t in (gs, fi):
+            if t is not None and (t.device != dev or t.dtype != torch.float32):
+                raise NotImplementedError("grad_scale / found_inf must be float32 tensors on "
+                                          "the parameters' device")
+        dyn = _lib.TaDynamic(plan["steps"].data_ptr(), plan["table"].data_ptr(),
+                             CAPTURE_TABLE_STEPS, lr_ptr,
+                             gs.data_ptr() if gs is not None else None,
+                             fi.data_ptr() if fi is not None else None)
+        ws = self._ws[dev]
+        with torch.cuda.device(dev):
+            rc = lib.ta_step_prepared(plan["arr"].ctypes.data, len(items),
+                                      plan["groups"].ctypes.data, len(plan["groups"]),
+                                      self._seed, ws.data_ptr(), ws.numel(), ctypes.byref(dyn),
+                                      _lib.stream_ptr(dev))
+        _lib.check(rc, "ta_step_prepared")
+        for _, p in items:
+            mgr = self.state[p].get("m_mgr")
+            if mgr is not None:
+                mgr.mark_updated()
 
     # ------------------------------------------------------------------
     def read_status(self, clear: bool = True) -> int:
