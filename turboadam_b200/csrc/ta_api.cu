@@ -66,6 +66,8 @@ struct Layout {
   size_t table = 0;
   size_t lists = 0;
   size_t list_stride = 0;
+  size_t sel_block = 0;    // the select state of every CoState tensor, contiguous
+  size_t sel_bytes = 0;    //   (cleared at the start of each step)
   std::vector<CsSlot> cs;  // per CoState tensor
   size_t total = 0;
 };
@@ -80,16 +82,19 @@ Layout layout_for(int nT, const std::vector<int64_t>& cs_bpad) {
   L.lists = off;
   L.list_stride = al256((size_t)(nT + 1) * sizeof(int64_t) + (size_t)nT * sizeof(int32_t));
   off += L.list_stride * kMaxLists;
+  L.sel_block = off;
+  L.sel_bytes = al256(cs_bpad.size() * 16 * 4);
+  off += L.sel_bytes;
+  size_t ci = 0;
   for (int64_t bp : cs_bpad) {
     CsSlot s;
+    s.sel = L.sel_block + 16 * 4 * ci++;
     s.part = off;
     off = al256(off + (size_t)bp * 2 * 4);
     s.ratios = off;
     off = al256(off + (size_t)bp * 4);
     s.hist = off;
     off = al256(off + (size_t)3 * 2 * HBINS * 4);
-    s.sel = off;
-    off = al256(off + 16 * 4);
     s.alpha = off;
     off = al256(off + 4 * 4);
     s.chunk = off;
@@ -550,6 +555,10 @@ ta_status run_step(const ta_tensor* ts, int nT, const ta_group* groups, uint64_t
     TA_CU(cudaMemcpyAsync(ws + L.table, host.data() + L.table, host.size() - L.table,
                           cudaMemcpyHostToDevice, st));
   if (mode == 1) return TA_OK;
+  // the select state (alpha's last-CTA counter first of all) starts each step
+  // at zero, wherever a new tensor list put it
+  if (L.sel_bytes && (phase < 0 || phase == TA_PHASE_PASS1))
+    TA_CU(cudaMemsetAsync(ws + L.sel_block, 0, L.sel_bytes, st));
   if (mode == 2) {
     AdvParams a;
     a.T = reinterpret_cast<DevTensor*>(ws + L.table);

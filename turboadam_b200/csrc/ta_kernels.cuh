@@ -172,7 +172,7 @@ struct KParams {
   int32_t nl;
   int64_t total;        // tiles in this launch
   uint32_t* status;
-  const uint32_t* skip;       // optional: nonzero -> the step is skipped (AMP found_inf)
+  const uint32_t* skip = nullptr;  // optional: nonzero -> the step is skipped (found_inf)
   uint32_t rk0[10], rk1[10];  // Philox round keys (seed words + r * Weyl constants)
 };
 // A skipped step (AMP found_inf) leaves every kernel of it without effect.
@@ -1058,7 +1058,7 @@ struct SelParams {
   const int64_t* cbeg;  // [ncs + 1] chunk prefix
   const int32_t* cidx;  // [ncs] tensor indices
   int32_t ncs;
-  const uint32_t* skip;  // optional: nonzero -> the step is skipped
+  const uint32_t* skip = nullptr;  // optional: nonzero -> the step is skipped
 };
 
 
