@@ -1172,7 +1172,7 @@ __global__ void __launch_bounds__(FIN_THREADS) k_alpha_fin(const __grid_constant
 // ---------------------------------------------------------------------------
 // Pass 2: CoState encode (costate.py:419-425, :51-86, :213-258)
 // ---------------------------------------------------------------------------
-template <int PT, bool FULL>
+template <int PT, bool FULL, bool AMP = false>
 __device__ __forceinline__ void p2_block(const DevTensor* T, const StageMeta& M,
                                          const uint8_t* st, uint2* wb) {
   using L = P2L<PT>;
@@ -1219,7 +1219,7 @@ __device__ __forceinline__ void p2_block(const DevTensor* T, const StageMeta& M,
         const int k = 4 * kq + i;
         float2 g = make_float2(ld_smem_elem<PT>(sg, j + 8 * k),
                                ld_smem_elem<PT>(sg, j + 8 * k + 8));
-        if (flags & DF_AMP) g = round_param2<PT>(P.mul(g, dup2(ginv)));
+        if (AMP) g = round_param2<PT>(P.mul(g, dup2(ginv)));
         const uint32_t s0 = (sw >> (8 * i + 7 - j)) & 1u, s1 = (sw >> (8 * i + 15 - j)) & 1u;
         const float2 sd = make_float2(__uint_as_float(sc ^ (s0 << 31)),
                                       __uint_as_float(sc ^ (s1 << 31)));
@@ -1385,7 +1385,8 @@ __global__ void __launch_bounds__(NTHR) k_pass2(const __grid_constant__ KParams 
     const int bi = 4 * (lane >> 3) + warp;
     const bool mine_full = bi < pm.nblk && pm.n - (pm.b0 + bi) * BS >= BS;
     const bool fast = __all_sync(0xffffffffu, mine_full) && !(pm.c.flags & DF_M_OUT);
-    if (fast) p2_block<PT, true>(kp.T, pm, st, wbufs + warp * 8);
+    if (fast && (pm.c.flags & DF_AMP)) p2_block<PT, true, true>(kp.T, pm, st, wbufs + warp * 8);
+    else if (fast) p2_block<PT, true, false>(kp.T, pm, st, wbufs + warp * 8);
     else p2_block_general<PT>(kp.T, pm, st);
     __syncwarp();
     if (lane == 0) mbar_arrive(&done[s]);
