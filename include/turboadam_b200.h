@@ -322,6 +322,18 @@ TA_API ta_status ta_thresholds(const float* ratios_dev, int64_t n_blocks, double
 /* Workspace bytes for ta_v_update / ta_thresholds on n elements / blocks. */
 TA_API size_t ta_aux_workspace_size(int64_t n);
 
+/*
+ * Device self-test of the two properties the certified fast re-quantisation
+ * of the step relies on. No counterpart in the reference (its log is torch's).
+ * Over every normal binary32 x with ta_logf(x) >= -69.3 it writes
+ *   out_dev[0] = bits of the double max |RN(ln2 * lg2.approx(x)) - ta_logf(x)|
+ *                (the step assumes <= 2^-16),
+ *   out_dev[1] = number of adjacent normal pairs x < x' with
+ *                ta_logf(x') < ta_logf(x) (the step assumes 0).
+ * out_dev: 2 uint64 in device memory, zeroed by the caller.
+ */
+TA_API ta_status ta_selftest_lg2_bound(uint64_t* out_dev, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

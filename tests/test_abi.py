@@ -30,7 +30,7 @@ def test_header_symbols_exported(lib):
     from turboadam_b200 import _lib
 
     names = declared_symbols()
-    assert len(names) == 19
+    assert len(names) == 20
     assert sorted(_lib.EXPORTED) == names
     for n in names:
         assert hasattr(lib, n), n

@@ -1,0 +1,76 @@
+"""Device checks of the properties behind the certified fast re-quantisation
+of pass 1 (exact indices from an approximate log plus a per-quad error test):
+the hardware lg2 approximation stays within the error bound the kernel
+assumes, and the checker's log is monotone, over every normal binary32 input.
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def test_lg2_bound_and_log_monotone_exhaustive():
+    from turboadam_b200 import _lib
+
+    lib = _lib.load()
+    out = torch.zeros(2, dtype=torch.int64, device="cuda")
+    _lib.check(lib.ta_selftest_lg2_bound(out.data_ptr(), torch.cuda.current_stream().cuda_stream),
+               "ta_selftest_lg2_bound")
+    torch.cuda.synchronize()
+    words = out.cpu().numpy().astype(np.uint64)
+    max_err = float(words[:1].view(np.float64)[0])
+    assert int(words[1]) == 0, "ta_logf is not monotone on the normal floats"
+    assert 0.0 < max_err <= 2.0 ** -16, f"lg2.approx error {max_err} (2^{math.log2(max_err):.2f})"
+
+
+@pytest.mark.parametrize("v_bits", [2, 4, 8])
+def test_boundary_heavy_blocks_bitexact(oracle, v_bits):
+    """Gradients built so that many elements sit on or near re-quantisation
+    decision points (constant blocks, repeated values, two magnitudes, tiny
+    and graded spans, zero rows): the step must still match the checker bit
+    for bit in every index, header and parameter, in both random modes."""
+    from turboadam_b200 import TurboAdam
+
+    rng = np.random.default_rng(11 + v_bits)
+    n = 128 * 64
+    kw = dict(lr=6e-4, betas=(0.9, 0.999), weight_decay=0.01, v_bits=v_bits)
+    init = (rng.standard_normal(n) * 0.02).astype(np.float32)
+    tp = torch.nn.Parameter(torch.from_numpy(init.copy()).cuda())
+    op = oracle.OracleParam(init.copy())
+    opt = TurboAdam([tp], seed=3, **kw)
+    oopt = oracle.OracleTurboAdam([oracle.OracleTurboAdam.make_group([op], **kw)])
+    for step in range(8):
+        g = (rng.standard_normal(n) * 1e-3).astype(np.float32)
+        gb = g.reshape(64, 128)
+        gb[0:8] = 1e-3                                    # constant blocks
+        gb[8:16] = gb[8:16, :1]                           # constant per block
+        gb[16:24] = np.where(rng.random((8, 128)) < 0.5, 1e-3, -1e-3)
+        gb[24:32] *= np.float32(1e-4)                     # tiny gradients
+        gb[32:40] = (np.arange(128) * 1e-5).astype(np.float32)  # graded
+        gb[40:44] = 0.0                                   # zero rows
+        tp.grad = torch.from_numpy(g.copy()).cuda()
+        op.grad = g.copy()
+        parity = step % 2 == 1
+        if parity:
+            u = rng.random(n, np.float32)
+            u.reshape(64, 128)[:, ::3] = rng.integers(0, 2, (64, 43)).astype(np.float32) * 0.5
+            opt._parity = {"uniforms": {tp: torch.from_numpy(u).cuda()}}
+            ufn = lambda i, st, npad, u=u: u  # noqa: E731
+        else:
+            opt._parity = None
+            ufn = lambda i, st, npad: oracle.sr_uniforms(op.n, i, st, 3)  # noqa: E731
+        opt.step()
+        oopt.step(uniforms=ufn)
+        torch.cuda.synchronize()
+        st = opt.state[tp]
+        ost = oopt.state[id(op)]
+        tag = f"step {step} parity {parity}"
+        np.testing.assert_array_equal(st["compressed_v"]["indices"].cpu().numpy(), ost.v_idx,
+                                      err_msg=tag)
+        hdr = st["compressed_v"]["scales"].contiguous().view(torch.int16).cpu().numpy()
+        np.testing.assert_array_equal(hdr.view(np.uint16).reshape(-1), ost.v_hdr, err_msg=tag)
+        got = tp.detach().cpu().numpy()
+        assert np.array_equal(got.view(np.uint32), op.data.view(np.uint32)), tag

@@ -58,6 +58,7 @@ EXPORTED = (
     "ta_step_phase",
     "ta_plan_prepare",
     "ta_step_prepared",
+    "ta_selftest_lg2_bound",
 )
 
 
@@ -186,6 +187,7 @@ _SIG = {
                                        ctypes.c_size_t, _P]),
     "ta_step_prepared": (ctypes.c_int, [_P, ctypes.c_int32, _P, ctypes.c_int32, ctypes.c_uint64,
                                         _P, ctypes.c_size_t, ctypes.POINTER(TaDynamic), _P]),
+    "ta_selftest_lg2_bound": (ctypes.c_int, [_P, _P]),
 }
 
 _lib = None

@@ -966,9 +966,37 @@ ta_status noalloc_scratch(cudaStream_t st, void** out) {
   *out = g_noalloc_ptr[dev];
   return TA_OK;
 }
+__global__ void __launch_bounds__(256) k_selftest_lg2(unsigned long long* out) {
+  unsigned long long me = 0, nm = 0;
+  const uint64_t lo = 0x00800000u, hi = 0x7f800000u;  // the normal binary32 numbers
+  for (uint64_t u = lo + blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; u < hi;
+       u += (uint64_t)gridDim.x * blockDim.x) {
+    const float x = __uint_as_float((uint32_t)u);
+    const float le = ta_logf_core(x, 0);
+    if (u + 1 < hi && ta_logf_core(__uint_as_float((uint32_t)u + 1u), 0) < le) ++nm;
+    if (le >= -69.3f) {
+      const float la = __fmul_rn(lg2_approx(x), LN2_F);
+      const unsigned long long d =
+          (unsigned long long)__double_as_longlong(fabs((double)la - (double)le));
+      me = d > me ? d : me;
+    }
+  }
+  atomicMax(&out[0], me);
+  atomicAdd(&out[1], nm);
+}
+
 }  // namespace
 
 extern "C" {
+
+ta_status ta_selftest_lg2_bound(uint64_t* out_dev, void* stream) {
+  g_err.clear();
+  if (!out_dev) return fail(TA_ERR_INVALID, "null argument");
+  k_selftest_lg2<<<sm_count() * 8, 256, 0, (cudaStream_t)stream>>>(
+      reinterpret_cast<unsigned long long*>(out_dev));
+  TA_CU(cudaGetLastError());
+  return TA_OK;
+}
 
 ta_status ta_v_update_noalloc(const uint8_t* idx_dev, const uint16_t* hdr_dev,
                               const void* grad_dev, int32_t grad_dtype, int64_t n,

@@ -373,9 +373,9 @@ __device__ __forceinline__ float2 hi2(float4 v) { return make_float2(v.z, v.w); 
 __device__ __forceinline__ float4 cat4(float2 a, float2 b) { return make_float4(a.x, a.y, b.x, b.y); }
 
 // ta_logf for x in [2^-126, FLT_MAX], two at a time: the same operations as
-// log_clamped without the clamp and the special-case selects. For x = 0 or a
-// subnormal x the result is below -69.3 (checked exhaustively by the tests),
-// which the caller's range flag catches; other inputs never reach it unflagged.
+// log_clamped without the clamp and the special-case selects. Pass 1 applies
+// it to the block extremes of v_new, which its range flags keep normal and
+// finite.
 __device__ __forceinline__ float2 log_fast2(float2 x, const PK& P) {
   const uint32_t ix0 = __float_as_uint(x.x), ix1 = __float_as_uint(x.y);
   const int32_t e0 = ((int32_t)(ix0 - 0x3f2aaaabu)) >> 23;
@@ -402,11 +402,6 @@ __device__ __forceinline__ float2 log_fast2(float2 x, const PK& P) {
   return P.add(s, lo);
 }
 
-// Range flag thresholds of the fast path: ln v_new below -69.3 (v_new below
-// ~8.9e-31, incl. every v_new < 2^-100, zero and subnormal) takes the exact
-// path, where v / bc2 needs the scaled or IEEE division and the log its
-// subnormal and zero handling.
-constexpr float FAST_LN_MIN = -69.3f;
 
 template <int PT>
 __device__ __forceinline__ float4 ld_quad(const uint8_t* base, int t0) {
@@ -579,27 +574,102 @@ __device__ __noinline__ void p1_requant_exact(const float4* scr4, const float* s
   }
 }
 
-// Stochastic re-quantisation of 4 finite logs of a fast block: the same
-// operations as p1_requant_exact, paired, with the 4 indices packed into one
-// word (index + 2^23 carries the integer in its low byte).
-__device__ __forceinline__ uint32_t requant_quad(float4 l, float4 u, float2 vmin2, float2 nspan2n,
-                                                 float2 rspan2, float2 nbf2, float top,
-                                                 const PK& P) {
-  float2 a0 = P.sub(lo2(l), vmin2), a1 = P.sub(hi2(l), vmin2);
-  float2 q0 = P.mul(a0, rspan2), q1 = P.mul(a1, rspan2);
-  q0 = fma2(fma2(q0, nspan2n, a0), rspan2, q0);  // Markstein: RN((L - min) / span)
-  q1 = fma2(fma2(q1, nspan2n, a1), rspan2, q1);
-  const float2 c0 = P.mul(q0, nbf2), c1 = P.mul(q1, nbf2);
-  const float2 f0 = make_float2(floorf(c0.x), floorf(c0.y));
-  const float2 f1 = make_float2(floorf(c1.x), floorf(c1.y));
-  const float2 r0 = P.sub(c0, f0), r1 = P.sub(c1, f1);
-  float2 k0 = P.add(f0, make_float2(u.x < r0.x ? 1.0f : 0.0f, u.y < r0.y ? 1.0f : 0.0f));
-  float2 k1 = P.add(f1, make_float2(u.z < r1.x ? 1.0f : 0.0f, u.w < r1.y ? 1.0f : 0.0f));
-  k0 = P.add(make_float2(fminf(k0.x, top), fminf(k0.y, top)), dup2(8388608.0f));
-  k1 = P.add(make_float2(fminf(k1.x, top), fminf(k1.y, top)), dup2(8388608.0f));
-  const uint32_t w01 = __byte_perm(__float_as_uint(k0.x), __float_as_uint(k0.y), 0x0040);
-  const uint32_t w23 = __byte_perm(__float_as_uint(k1.x), __float_as_uint(k1.y), 0x0040);
+// ---------------------------------------------------------------------------
+// Certified fast re-quantisation (full blocks without range flags).
+//
+// The exact rule (quantize.py:275-294) is idx = clamp(floor(C) + (u < C -
+// floor(C)), 0, nb - 1) with C = RN(RN(L - Lmin) / span) * nb and L =
+// ta_logf(v). For real C >= 0 and u in [0, 1) that is clamp(ceil(C - u)),
+// which changes only where C - u crosses an integer. The fast path therefore
+// evaluates D = (La - Lmin) * (nb / span) + (0.5 - u) with La = RN(ln2 *
+// lg2.approx(v)) in place of L, takes rint(D) (= ceil(C - u) unless C - u is
+// within E of an integer), and reports |D - rint(D)|: when that stays below
+// 0.5 - E for all four elements of a quad the indices equal the exact rule's;
+// otherwise the quad is recomputed with the exact log (p1_requant_quad_exact).
+// E bounds |D - (C - u + 0.5)|: |La - L| <= 2^-17 for every normal v with
+// L >= -69.3 (checked exhaustively on the device by ta_selftest_lg2_bound;
+// E uses 2^-16) propagated through nb / span, plus the roundings of A, D,
+// RN(1/span), C and 0.5 - u (see requant_threshold).
+// The block extremes of L are the exact logs of the extremes of v: ta_logf
+// is monotone non-decreasing on the normal floats (checked exhaustively).
+// ---------------------------------------------------------------------------
+constexpr float LN2_F = 0x1.62e43p-1f;       // RN(ln 2)
+constexpr float RINT_MAGIC = 0x1.8p23f;      // x + 1.5 * 2^23 rounds x to an integer
+constexpr float FAST_V_MIN = 0x1p-99f;       // smaller v_new -> exact path (L < -68.6)
+
+__device__ __forceinline__ float lg2_approx(float x) {
+  float r;
+  asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+// La = RN(ln2 * lg2.approx(v)) for a pair
+__device__ __forceinline__ float2 ln_approx2(float2 v, const PK& P) {
+  return P.mul(make_float2(lg2_approx(v.x), lg2_approx(v.y)), dup2(LN2_F));
+}
+
+// 0.5 - E for a block: E = k1 * 2^-16 * 1.0625 + nb * 2^-22 + 2^-19 bounds
+// |D - (C - u + 0.5)| with k1 = nb / span (0 for a constant block, where
+// every C is 0 and D = 0.5 - u exactly).
+__device__ __forceinline__ float requant_threshold(float k1, float nbf) {
+  return 0.5f - __fmaf_rn(k1, 0x1.1p-16f, __fmaf_rn(nbf, 0x1p-22f, 0x1p-19f));
+}
+
+// Fast indices of one quad: w = 0.5 - u; returns the 4 packed indices and
+// the largest |D - rint(D)| in *emax.
+__device__ __forceinline__ uint32_t requant_quad_fast(float4 la, float4 w, float2 lmin2, float2 k12,
+                                                      float tops, const PK& P, float* emax) {
+  const float2 a0 = P.sub(lo2(la), lmin2), a1 = P.sub(hi2(la), lmin2);
+  const float2 d0 = fma2(a0, k12, lo2(w)), d1 = fma2(a1, k12, hi2(w));
+  const float2 s0 = P.add(d0, dup2(RINT_MAGIC)), s1 = P.add(d1, dup2(RINT_MAGIC));
+  const float2 e0 = P.sub(d0, P.sub(s0, dup2(RINT_MAGIC)));
+  const float2 e1 = P.sub(d1, P.sub(s1, dup2(RINT_MAGIC)));
+  *emax = fmaxf(fmaxf(fmaxf(fabsf(e0.x), fabsf(e0.y)), fmaxf(fabsf(e1.x), fabsf(e1.y))), *emax);
+  // the integer part of s is rint(d) (its low byte, 0..nb-1 after the clamp)
+  const uint32_t w01 = __byte_perm(__float_as_uint(fminf(s0.x, tops)),
+                                   __float_as_uint(fminf(s0.y, tops)), 0x0040);
+  const uint32_t w23 = __byte_perm(__float_as_uint(fminf(s1.x, tops)),
+                                   __float_as_uint(fminf(s1.y, tops)), 0x0040);
   return __byte_perm(w01, w23, 0x5410);
+}
+
+// Exact indices of one quad of a full, unflagged block (rare: a quad whose
+// fast decision was uncertain). Recomputes v_new of the 4 elements from the
+// staged inputs exactly as phase A does, takes ta_logf and applies the
+// reference rule with the same uniforms.
+template <int MK, int VK, int PT, bool UNI, bool TABLE>
+__device__ __noinline__ uint32_t p1_requant_quad_exact(const StageMeta& M, const uint8_t* st,
+                                                       int bi, int t0, const float* tab,
+                                                       float lmin, float span, float4 u4,
+                                                       float vmin, float nspan, float rspan) {
+  using L = P1L<MK, VK, PT, UNI>;
+  const Sc c = M.c;
+  const float ua[4] = {u4.x, u4.y, u4.z, u4.w};
+  const float top = c.nbf - 1.0f;
+  uint32_t word = 0;
+#pragma unroll 1
+  for (int i = 0; i < 4; ++i) {
+    const int t = t0 + i;
+    float g = ld_smem_elem<PT>(st + L::OFF_G + L::AP::off(bi), t);
+    if (c.flags & DF_AMP) g = amp_unscale<PT>(g, c.ginv);
+    const int id = st[L::OFF_IDX + L::A1::off(bi) + t];
+    float vo;
+    if (TABLE) {
+      vo = tab[id];
+    } else {
+      const float qv = __fmul_rn(__fadd_rn((float)id, 0.5f), c.rnbf);
+      vo = ta_expf(__fadd_rn(lmin, __fmul_rn(qv, span)));
+    }
+    const float vn = __fmaf_rn(__fmul_rn(g, g), c.omb2, __fmul_rn(vo, c.b2));
+    const float lv = ta_logf_core(vn, 0);  // vn is a finite normal number here
+    const float cc = __fmul_rn(div_by(__fsub_rn(lv, vmin), nspan, rspan), c.nbf);
+    const float fl = floorf(cc);
+    const float fr = __fsub_rn(cc, fl);
+    float r = __fadd_rn(fl, (ua[i] < fr) ? 1.0f : 0.0f);
+    r = (r < 0.0f) ? 0.0f : r;
+    r = (r > top) ? top : r;
+    word |= (uint32_t)r << (8 * i);
+  }
+  return word;
 }
 
 // One 128-element block per 8-lane group (quad layout above).
@@ -744,10 +814,11 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
         // quantize.py:270: v = b2 * v_old + (1 - b2) * g^2
         v01 = fma2(P.mul(g01, g01), dup2(c.omb2), P.mul(make_float2(vo[0], vo[1]), dup2(c.b2)));
         v23 = fma2(P.mul(g23, g23), dup2(c.omb2), P.mul(make_float2(vo[2], vo[3]), dup2(c.b2)));
-        const float2 l01 = log_fast2(v01, P), l23 = log_fast2(v23, P);  // quantize.py:275
-        scr4[k * 32 + lane] = cat4(l01, l23);
-        vmin = fminf(fminf(l01.x, l01.y), fminf(fminf(l23.x, l23.y), vmin));
-        vmax = fmaxf(fmaxf(l01.x, l01.y), fmaxf(fmaxf(l23.x, l23.y), vmax));
+        // quantize.py:275: approximate ln v_new (certified re-quantisation);
+        // the block extremes are taken over v_new and converted exactly later
+        scr4[k * 32 + lane] = cat4(ln_approx2(v01, P), ln_approx2(v23, P));
+        vmin = fminf(fminf(v01.x, v01.y), fminf(fminf(v23.x, v23.y), vmin));
+        vmax = fmaxf(fmaxf(v01.x, v01.y), fmaxf(fmaxf(v23.x, v23.y), vmax));
       } else if (VK == VK_FP32) {
         const float4 s4 = *reinterpret_cast<const float4*>(seas + t0);
         v01 = fma2(P.mul(dup2(c.omb2), g01), g01, P.mul(lo2(s4), dup2(c.b2)));  // optimizer.py:166
@@ -781,8 +852,12 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
       ggs = __fadd_rn(ag.x, ag.y);
     }
     const bool bad = (nanacc.x != nanacc.x) || (nanacc.y != nanacc.y);
-    if (VK == VK_ONEQ)
-      fix = bad || vmin < FAST_LN_MIN || (TABLE && (idor & (0x01010101u * (uint32_t)(0xff & ~(nb - 1)))) != 0);
+    if (VK == VK_ONEQ) {
+      fix = bad || vmin < FAST_V_MIN || (TABLE && (idor & (0x01010101u * (uint32_t)(0xff & ~(nb - 1)))) != 0);
+      // the whole block takes one path: its extremes are of v_new (fast) or
+      // of ln v_new (exact path), never a mix
+      fix = (__ballot_sync(0xffffffffu, fix) >> (8 * q)) & 0xffu;
+    }
     else if (VK == VK_FP32)
       fix = bad || !(vmin_fp >= 0x1p-100f);
     else if (bad)
@@ -898,6 +973,11 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
       vmin = fminf(vmin, __shfl_xor_sync(0xffffffffu, vmin, off));
       vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, off));
     }
+    if (FULL && !fix) {  // extremes of v_new -> extremes of ln v_new (exact, monotone)
+      const float2 le = log_fast2(make_float2(vmin, vmax), P);
+      vmin = le.x;
+      vmax = le.y;
+    }
     if (active && j == 0)
       reinterpret_cast<uint32_t*>(M.v_hdr)[b] =
           (uint32_t)f32_to_f16_dev(vmin) | ((uint32_t)f32_to_f16_dev(vmax) << 16);
@@ -908,24 +988,38 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
     const float* suni = reinterpret_cast<const float*>(st + L::OFF_UNI + L::A4::off(bi));
     uint8_t* gidx = M.v_idx + e0;
     if (FULL && !fix) {
-      const float2 vmin2 = dup2(vmin), nspan2n = dup2(-nspan), rspan2 = dup2(rspan);
-      const float2 nbf2 = dup2(c.nbf);
-      const float top = c.nbf - 1.0f;
+      // nb / span exactly (power-of-two scaling); 0 when every ln v_new of the
+      // block is equal (all C are 0 then)
+      const float k1 = (vmax == vmin) ? 0.0f : __fmul_rn(rspan, c.nbf);
+      const float thr = requant_threshold(k1, c.nbf);
+      const float2 lmin2 = dup2(vmin), k12 = dup2(k1);
+      const float tops = __fadd_rn(RINT_MAGIC, c.nbf - 1.0f);
 #pragma unroll 1
       for (int k = 0; k < 4; ++k) {
         const int t0 = 4 * j + 32 * k;
-        float4 u4;
+        float4 u4, w4;
         if (UNI) {
           u4 = *reinterpret_cast<const float4*>(suni + t0);
+          w4 = cat4(P.sub(dup2(0.5f), lo2(u4)), P.sub(dup2(0.5f), hi2(u4)));
         } else {
           uint32_t rnd[4], c0, c1, c2, c3;
           ta_sr_counter((uint64_t)(b + M.boff), (uint32_t)(j + 8 * k), c.tid, c.step, &c0, &c1,
                         &c2, &c3);
           philox_rk(c0, c1, c2, c3, kp.rk0, kp.rk1, rnd);
-          u4 = make_float4(ta_u01(rnd[0]), ta_u01(rnd[1]), ta_u01(rnd[2]), ta_u01(rnd[3]));
+          // u = (x >> 8) 2^-24 (ta_u01); 0.5 - u is exact
+          const float2 x01 = make_float2((float)(rnd[0] >> 8), (float)(rnd[1] >> 8));
+          const float2 x23 = make_float2((float)(rnd[2] >> 8), (float)(rnd[3] >> 8));
+          w4 = cat4(fma2(x01, dup2(-0x1p-24f), dup2(0.5f)), fma2(x23, dup2(-0x1p-24f), dup2(0.5f)));
+          u4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);  // recovered from w4 if needed
         }
-        *reinterpret_cast<uint32_t*>(gidx + t0) =
-            requant_quad(scr4[k * 32 + lane], u4, vmin2, nspan2n, rspan2, nbf2, top, P);
+        float emax = 0.0f;
+        uint32_t word = requant_quad_fast(scr4[k * 32 + lane], w4, lmin2, k12, tops, P, &emax);
+        if (emax >= thr) {  // rare: some element of the quad is within E of a decision boundary
+          if (!UNI) u4 = cat4(P.sub(dup2(0.5f), lo2(w4)), P.sub(dup2(0.5f), hi2(w4)));
+          word = p1_requant_quad_exact<MK, VK, PT, UNI, TABLE>(M, st, bi, t0, tab, lmin, span, u4,
+                                                               vmin, nspan, rspan);
+        }
+        *reinterpret_cast<uint32_t*>(gidx + t0) = word;
       }
     } else if (active) {
       p1_requant_exact<UNI>(scr4, suni, gidx, (uint64_t)(b + M.boff), j, lane, vmin, nspan, rspan, c.nbf,
