@@ -754,7 +754,7 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
     float vmin_fp = INFINITY;  // VK_FP32: smallest v_new
     uint32_t idor = 0;
     const float2 zero2 = dup2(0.0f);
-#pragma unroll 1
+#pragma unroll
     for (int k = 0; k < 4; ++k) {
       const int t0 = 4 * j + 32 * k;
       const int64_t e = e0 + t0;
@@ -1305,18 +1305,19 @@ __device__ __forceinline__ void p2_block(const DevTensor* T, const StageMeta& M,
     const PK P(M.c.one, M.c.nzero);
     const float2 ao2 = dup2(alpha_old), a2 = dup2(alpha), b12 = dup2(b1), omb12 = dup2(omb1);
     const uint32_t sc = __float_as_uint(cs_scale);
-#pragma unroll 1
+#pragma unroll
     for (int kq = 0; kq < 4; ++kq) {
-      const uint32_t sw = has_state ? sgnw[kq] : 0u;
+      // element j + 8k's sign is bit 7 - j of byte k: shifted left by j, the
+      // 4 bits of word kq sit at the byte tops (bits 7, 15, 23, 31)
+      const uint32_t sw = has_state ? (sgnw[kq] << j) : 0u;
 #pragma unroll
       for (int i = 0; i < 4; i += 2) {
         const int k = 4 * kq + i;
         float2 g = make_float2(ld_smem_elem<PT>(sg, j + 8 * k),
                                ld_smem_elem<PT>(sg, j + 8 * k + 8));
         if (AMP) g = round_param2<PT>(P.mul(g, dup2(ginv)));
-        const uint32_t s0 = (sw >> (8 * i + 7 - j)) & 1u, s1 = (sw >> (8 * i + 15 - j)) & 1u;
-        const float2 sd = make_float2(__uint_as_float(sc ^ (s0 << 31)),
-                                      __uint_as_float(sc ^ (s1 << 31)));
+        const float2 sd = make_float2(__uint_as_float(sc ^ ((sw << (24 - 8 * i)) & 0x80000000u)),
+                                      __uint_as_float(sc ^ ((sw << (16 - 8 * i)) & 0x80000000u)));
         float2 mh = P.add(P.mul(ao2, g), sd);  // costate.py:261-323
         if (!has_state) mh = dup2(0.0f);
         const float2 m = P.add(P.mul(b12, mh), P.mul(omb12, g));  // costate.py:416
