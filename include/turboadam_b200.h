@@ -48,8 +48,15 @@ enum {
   TA_V_ONEQ = 1u << 1,      /* second moment is 1Q (else fp32 exp_avg_sq)         */
   TA_M_HAS_STATE = 1u << 2, /* CoState holds a previous encoding (not first step) */
   TA_NO_PARAM = 1u << 3,    /* skip weight decay and the parameter update         */
-  TA_M_SPANNING = 1u << 4   /* CoState shard of a tensor split over ranks:
+  TA_M_SPANNING = 1u << 4,  /* CoState shard of a tensor split over ranks:
                                alpha and thresholds reduced via ta_step_phase     */
+  TA_EXACT_PARAM = 1u << 5  /* parameter update with correctly rounded v / bc2,
+                               sqrt and division: bit-identical to the
+                               reference's op sequence (optimizer.py:163-170).
+                               Without it those three ops use the hardware
+                               estimates plus one correction each (within about
+                               one ulp per op); no state depends on them, so
+                               every packed state bit is the same either way  */
 };
 
 /* ta_step_phase phases (in call order; the caller all-reduces (sum) the
@@ -323,16 +330,20 @@ TA_API ta_status ta_thresholds(const float* ratios_dev, int64_t n_blocks, double
 TA_API size_t ta_aux_workspace_size(int64_t n);
 
 /*
- * Device self-test of the two properties the certified fast re-quantisation
- * of the step relies on. No counterpart in the reference (its log is torch's).
- * Over every normal binary32 x with ta_logf(x) >= -69.3 it writes
+ * Device self-test of the hardware-estimate properties the step relies on.
+ * No counterpart in the reference (its arithmetic is torch's CPU ops).
+ * Over every normal binary32 x it writes
  *   out_dev[0] = bits of the double max |RN(ln2 * lg2.approx(x)) - ta_logf(x)|
- *                (the step assumes <= 2^-16),
+ *                over x with ta_logf(x) >= -69.3 (the certified
+ *                re-quantisation assumes <= 2^-16),
  *   out_dev[1] = number of adjacent normal pairs x < x' with
- *                ta_logf(x') < ta_logf(x) (the step assumes 0).
- * out_dev: 2 uint64 in device memory, zeroed by the caller.
+ *                ta_logf(x') < ta_logf(x) (the step assumes 0),
+ *   out_dev[2] = number of x with a normal 1/x where rcp.approx plus one
+ *                Newton step differs from RN(1/x) (the default parameter
+ *                update assumes 0).
+ * out_dev: 3 uint64 in device memory, zeroed by the caller.
  */
-TA_API ta_status ta_selftest_lg2_bound(uint64_t* out_dev, void* stream);
+TA_API ta_status ta_selftest_fast_math(uint64_t* out_dev, void* stream);
 
 #ifdef __cplusplus
 }

@@ -1,7 +1,9 @@
-"""Device checks of the properties behind the certified fast re-quantisation
-of pass 1 (exact indices from an approximate log plus a per-quad error test):
-the hardware lg2 approximation stays within the error bound the kernel
-assumes, and the checker's log is monotone, over every normal binary32 input.
+"""Device checks of the properties behind the fast paths of pass 1: the
+certified re-quantisation (exact indices from an approximate log plus a
+per-quad error test) needs the hardware lg2 estimate within its assumed bound
+and the checker's log monotone; the default parameter update uses a
+reciprocal that is correctly rounded after one Newton step. All three are
+checked over every normal binary32 input.
 """
 import math
 
@@ -12,18 +14,19 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
-def test_lg2_bound_and_log_monotone_exhaustive():
+def test_fast_math_properties_exhaustive():
     from turboadam_b200 import _lib
 
     lib = _lib.load()
-    out = torch.zeros(2, dtype=torch.int64, device="cuda")
-    _lib.check(lib.ta_selftest_lg2_bound(out.data_ptr(), torch.cuda.current_stream().cuda_stream),
-               "ta_selftest_lg2_bound")
+    out = torch.zeros(3, dtype=torch.int64, device="cuda")
+    _lib.check(lib.ta_selftest_fast_math(out.data_ptr(), torch.cuda.current_stream().cuda_stream),
+               "ta_selftest_fast_math")
     torch.cuda.synchronize()
     words = out.cpu().numpy().astype(np.uint64)
     max_err = float(words[:1].view(np.float64)[0])
     assert int(words[1]) == 0, "ta_logf is not monotone on the normal floats"
     assert 0.0 < max_err <= 2.0 ** -16, f"lg2.approx error {max_err} (2^{math.log2(max_err):.2f})"
+    assert int(words[2]) == 0, "rcp.approx + one Newton step is not RN(1/x) everywhere"
 
 
 @pytest.mark.parametrize("v_bits", [2, 4, 8])
@@ -40,7 +43,7 @@ def test_boundary_heavy_blocks_bitexact(oracle, v_bits):
     init = (rng.standard_normal(n) * 0.02).astype(np.float32)
     tp = torch.nn.Parameter(torch.from_numpy(init.copy()).cuda())
     op = oracle.OracleParam(init.copy())
-    opt = TurboAdam([tp], seed=3, **kw)
+    opt = TurboAdam([tp], seed=3, exact_params=True, **kw)
     oopt = oracle.OracleTurboAdam([oracle.OracleTurboAdam.make_group([op], **kw)])
     for step in range(8):
         g = (rng.standard_normal(n) * 1e-3).astype(np.float32)

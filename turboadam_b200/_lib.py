@@ -23,6 +23,7 @@ TA_V_ONEQ = 1 << 1
 TA_M_HAS_STATE = 1 << 2
 TA_NO_PARAM = 1 << 3
 TA_M_SPANNING = 1 << 4
+TA_EXACT_PARAM = 1 << 5
 TA_PHASE_PASS1, TA_PHASE_PASS2, TA_PHASE_SEL1, TA_PHASE_SEL2, TA_PHASE_LABELS = range(5)
 TA_SHARD_ALIGN_BLOCKS = 4096
 TA_STATUS_NONFINITE_GRAD = 1 << 0
@@ -58,7 +59,7 @@ EXPORTED = (
     "ta_step_phase",
     "ta_plan_prepare",
     "ta_step_prepared",
-    "ta_selftest_lg2_bound",
+    "ta_selftest_fast_math",
 )
 
 
@@ -187,7 +188,7 @@ _SIG = {
                                        ctypes.c_size_t, _P]),
     "ta_step_prepared": (ctypes.c_int, [_P, ctypes.c_int32, _P, ctypes.c_int32, ctypes.c_uint64,
                                         _P, ctypes.c_size_t, ctypes.POINTER(TaDynamic), _P]),
-    "ta_selftest_lg2_bound": (ctypes.c_int, [_P, _P]),
+    "ta_selftest_fast_math": (ctypes.c_int, [_P, _P]),
 }
 
 _lib = None

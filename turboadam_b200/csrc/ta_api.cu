@@ -298,6 +298,7 @@ DevTensor make_dev(const ta_tensor& t, const ta_group& g, uint64_t seed) {
   if (t.v_out_dev) f |= DF_V_OUT;
   if (t.dtype == TA_BF16) f |= DF_BF16;
   if (t.flags & TA_M_SPANNING) f |= DF_SPAN;
+  if (t.flags & TA_EXACT_PARAM) f |= DF_EXACT_P;
   D.flags = f;
   D.tid = t.tensor_id;
   D.step = t.step;
@@ -966,8 +967,8 @@ ta_status noalloc_scratch(cudaStream_t st, void** out) {
   *out = g_noalloc_ptr[dev];
   return TA_OK;
 }
-__global__ void __launch_bounds__(256) k_selftest_lg2(unsigned long long* out) {
-  unsigned long long me = 0, nm = 0;
+__global__ void __launch_bounds__(256) k_selftest_fast_math(unsigned long long* out) {
+  unsigned long long me = 0, nm = 0, nr = 0;
   const uint64_t lo = 0x00800000u, hi = 0x7f800000u;  // the normal binary32 numbers
   for (uint64_t u = lo + blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; u < hi;
        u += (uint64_t)gridDim.x * blockDim.x) {
@@ -980,19 +981,25 @@ __global__ void __launch_bounds__(256) k_selftest_lg2(unsigned long long* out) {
           (unsigned long long)__double_as_longlong(fabs((double)la - (double)le));
       me = d > me ? d : me;
     }
+    if (u < 0x7e800000u) {  // 1/x normal
+      const float y0 = rcp_approx(x);
+      const float y = __fmaf_rn(__fmaf_rn(-x, y0, 1.0f), y0, y0);
+      if (__float_as_uint(y) != __float_as_uint(__frcp_rn(x))) ++nr;
+    }
   }
   atomicMax(&out[0], me);
   atomicAdd(&out[1], nm);
+  atomicAdd(&out[2], nr);
 }
 
 }  // namespace
 
 extern "C" {
 
-ta_status ta_selftest_lg2_bound(uint64_t* out_dev, void* stream) {
+ta_status ta_selftest_fast_math(uint64_t* out_dev, void* stream) {
   g_err.clear();
   if (!out_dev) return fail(TA_ERR_INVALID, "null argument");
-  k_selftest_lg2<<<sm_count() * 8, 256, 0, (cudaStream_t)stream>>>(
+  k_selftest_fast_math<<<sm_count() * 8, 256, 0, (cudaStream_t)stream>>>(
       reinterpret_cast<unsigned long long*>(out_dev));
   TA_CU(cudaGetLastError());
   return TA_OK;

@@ -41,6 +41,7 @@ enum : uint32_t {
   DF_BF16 = 1u << 13,
   DF_SPAN = 1u << 4,  // == TA_M_SPANNING
   DF_AMP = 1u << 14,  // gradients are multiplied by ginv on load
+  DF_EXACT_P = 1u << 15,  // correctly rounded parameter update (TA_EXACT_PARAM)
 };
 
 // Per-tensor descriptor, built on the host, uploaded into the workspace.

@@ -441,6 +441,40 @@ __device__ __forceinline__ float2 round_param2(float2 v) {
   return v;
 }
 
+__device__ __forceinline__ float rsqrt_approx(float x) {
+  float r;
+  asm("rsqrt.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
+// Parameter update of a pair without TA_EXACT_PARAM (optimizer.py:163-170):
+// p = w + fl(-lr m) / fl(d bc1), d = sqrt(x) + eps, x = fl(v * RN(1/bc2)).
+// sqrt(x): s = x y from y = rsqrt.approx(x), corrected once by s - (s^2 - x)
+// y / 2 (Markstein); 1 / den: rcp.approx plus one Newton step, which is
+// RN(1/den) for every normal den (checked exhaustively on the device);
+// the quotient gets Markstein's residual correction. Each op is within about
+// one ulp of the correctly rounded one, so p agrees with the reference's
+// sequence to a few ulp of the update. Inputs come from unflagged blocks:
+// x is a finite normal number, den a positive normal number.
+__device__ __forceinline__ float2 adam_pair_fast(float2 w, float2 x, float2 m, const Sc& c,
+                                                 const PK& P) {
+  const float2 y = make_float2(rsqrt_approx(x.x), rsqrt_approx(x.y));
+  const float2 s = P.mul(x, y);
+  const float2 s2mx = fma2(s, s, P.mul(x, P.mone));                    // s^2 - x
+  const float2 sq = fma2(s2mx, P.mul(y, dup2(-0.5f)), s);
+  const float2 nden = P.mul(P.add(sq, dup2(c.eps)), dup2(-c.bc1));    // -(d bc1)
+  const float2 y0 = make_float2(rcp_approx(-nden.x), rcp_approx(-nden.y));
+  const float2 yr = fma2(fma2(nden, y0, P.one), y0, y0);               // RN(1/den)
+  const float2 n = P.mul(dup2(c.nlr), m);
+  const float2 q = P.mul(n, yr);
+  return P.add(w, fma2(fma2(nden, q, n), yr, q));                      // q + (n - den q)/den
+}
+
 // ---------------------------------------------------------------------------
 // Pass 1
 // ---------------------------------------------------------------------------
@@ -587,7 +621,7 @@ __device__ __noinline__ void p1_requant_exact(const float4* scr4, const float* s
 // 0.5 - E for all four elements of a quad the indices equal the exact rule's;
 // otherwise the quad is recomputed with the exact log (p1_requant_quad_exact).
 // E bounds |D - (C - u + 0.5)|: |La - L| <= 2^-17 for every normal v with
-// L >= -69.3 (checked exhaustively on the device by ta_selftest_lg2_bound;
+// L >= -69.3 (checked exhaustively on the device by ta_selftest_fast_math;
 // E uses 2^-16) propagated through nb / span, plus the roundings of A, D,
 // RN(1/span), C and 0.5 - u (see requant_threshold).
 // The block extremes of L are the exact logs of the extremes of v: ta_logf
@@ -833,17 +867,23 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
         const float4 p4 = ld_quad<PT>(sp, t0);
         const float2 w01 = round_param2<PT>(P.mul(lo2(p4), dup2(c.wdf)));
         const float2 w23 = round_param2<PT>(P.mul(hi2(p4), dup2(c.wdf)));
-        // v / bc2 by Markstein with y = RN(1/bc2): exact for v in the unflagged range
         float2 x01 = P.mul(v01, dup2(c.rbc2)), x23 = P.mul(v23, dup2(c.rbc2));
         nanacc = fma2(x01, zero2, fma2(x23, zero2, nanacc));  // v or v / bc2 not finite
-        x01 = fma2(fma2(x01, dup2(-c.bc2), v01), dup2(c.rbc2), x01);
-        x23 = fma2(fma2(x23, dup2(-c.bc2), v23), dup2(c.rbc2), x23);
-        const float2 d01 = P.add(make_float2(__fsqrt_rn(x01.x), __fsqrt_rn(x01.y)), dup2(c.eps));
-        const float2 d23 = P.add(make_float2(__fsqrt_rn(x23.x), __fsqrt_rn(x23.y)), dup2(c.eps));
-        const float2 n01 = P.mul(dup2(c.nlr), m01), n23 = P.mul(dup2(c.nlr), m23);
-        const float2 den01 = P.mul(d01, dup2(c.bc1)), den23 = P.mul(d23, dup2(c.bc1));
-        const float2 p01 = P.add(w01, make_float2(__fdiv_rn(n01.x, den01.x), __fdiv_rn(n01.y, den01.y)));
-        const float2 p23 = P.add(w23, make_float2(__fdiv_rn(n23.x, den23.x), __fdiv_rn(n23.y, den23.y)));
+        float2 p01, p23;
+        if (c.flags & DF_EXACT_P) {
+          // v / bc2 by Markstein with y = RN(1/bc2): exact for v in the unflagged range
+          x01 = fma2(fma2(x01, dup2(-c.bc2), v01), dup2(c.rbc2), x01);
+          x23 = fma2(fma2(x23, dup2(-c.bc2), v23), dup2(c.rbc2), x23);
+          const float2 d01 = P.add(make_float2(__fsqrt_rn(x01.x), __fsqrt_rn(x01.y)), dup2(c.eps));
+          const float2 d23 = P.add(make_float2(__fsqrt_rn(x23.x), __fsqrt_rn(x23.y)), dup2(c.eps));
+          const float2 n01 = P.mul(dup2(c.nlr), m01), n23 = P.mul(dup2(c.nlr), m23);
+          const float2 den01 = P.mul(d01, dup2(c.bc1)), den23 = P.mul(d23, dup2(c.bc1));
+          p01 = P.add(w01, make_float2(__fdiv_rn(n01.x, den01.x), __fdiv_rn(n01.y, den01.y)));
+          p23 = P.add(w23, make_float2(__fdiv_rn(n23.x, den23.x), __fdiv_rn(n23.y, den23.y)));
+        } else {
+          p01 = adam_pair_fast(w01, x01, m01, c, P);
+          p23 = adam_pair_fast(w23, x23, m23, c, P);
+        }
         st_quad<PT>(gp, e, cat4(p01, p23));
       }
     }
@@ -994,7 +1034,7 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
       const float thr = requant_threshold(k1, c.nbf);
       const float2 lmin2 = dup2(vmin), k12 = dup2(k1);
       const float tops = __fadd_rn(RINT_MAGIC, c.nbf - 1.0f);
-#pragma unroll 1
+#pragma unroll
       for (int k = 0; k < 4; ++k) {
         const int t0 = 4 * j + 32 * k;
         float4 u4, w4;
@@ -1395,7 +1435,7 @@ __device__ __noinline__ void p2_block_general(const DevTensor* T, const StageMet
 }
 
 template <int PT>
-__global__ void __launch_bounds__(NTHR) k_pass2(const __grid_constant__ KParams kp) {
+__global__ void __launch_bounds__(NTHR, 6) k_pass2(const __grid_constant__ KParams kp) {
   if (step_skipped(kp.skip)) return;
   using L = P2L<PT>;
   using AG = typename L::AG;

@@ -69,6 +69,12 @@ class TurboAdam(Optimizer):
     threshold histograms all-reduced over ``process_group`` (default group)
     between them -- on every rank, also one that holds no split tensor -- which
     leaves every packed bit equal to the unsharded step's.
+    ``exact_params=True`` computes the parameter update's v / bc2, square root
+    and division correctly rounded, so parameters equal the reference's op
+    sequence bit for bit; by default those three ops use the hardware
+    estimates with one correction each (about one ulp per op: parameters
+    agree to a few ulp of the update, far inside 1e-6 relative). No state
+    depends on the parameters: every packed state bit is the same either way.
     """
 
     # torch.amp.GradScaler hands over `grad_scale` / `found_inf` instead of
@@ -97,6 +103,7 @@ class TurboAdam(Optimizer):
         shards=None,
         spanning=None,
         process_group=None,
+        exact_params: bool = False,
     ):
         if v_bits not in (2, 3, 4, 6, 8):
             raise ValueError(f"v_bits must be one of {{2, 3, 4, 6, 8}}, got {v_bits}")
@@ -143,6 +150,7 @@ class TurboAdam(Optimizer):
                                      "parameter")
                 self._shard[id(p)] = (boff, gnumel)
         self._capturable = bool(capturable)
+        self._exact_params = bool(exact_params)
         self._btab = {}
         self._pg = process_group
         self._xbuf = {}
@@ -357,7 +365,7 @@ class TurboAdam(Optimizer):
             r["dtype"] = _DTYPES[p.dtype]
             r["group"] = gi
             r["tensor_id"] = tids[id(p)] & 0xFFFFFFFF
-            flags = 0
+            flags = _lib.TA_EXACT_PARAM if self._exact_params else 0
             sh = self._shard.get(id(p))
             if sh is not None:
                 boff, gnumel = sh
