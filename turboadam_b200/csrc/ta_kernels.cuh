@@ -526,8 +526,9 @@ __device__ __forceinline__ uint32_t p1_issue(const DevTensor& D, uint8_t* st, in
 
 // Element layout inside a 128-element block: lane j of the block's 8-lane
 // group owns the quads Q = j + 8k (k = 0..3), i.e. elements 4Q + i, i = 0..3.
-// The stochastic-rounding draws of quad Q of block b are the 4 words of
-// Philox(b*32 + Q, tensor_id, step, b >> 27) (ta_sr_counter); the alpha
+// The lane's stochastic-rounding draws: the 16-bit leads of its 16 elements
+// come from one Philox call per quad pair, the 8-bit trails from one call
+// (ta_sr_lead_counter / ta_sr_trail_counter in ta_math.h); the alpha
 // partial of a lane accumulates its elements with i even and i odd in two
 // chains (k ascending) that are added at the end, then the 8 lanes are
 // combined ((l0+l4)+(l2+l6))+((l1+l5)+(l3+l7)).
@@ -583,20 +584,23 @@ __device__ __noinline__ void p1_requant_exact(const float4* scr4, const float* s
                                               uint32_t tid, uint32_t step, const uint32_t* rk0,
                                               const uint32_t* rk1) {
   const float top = nbf - 1.0f;
+  uint32_t lead[4] = {0, 0, 0, 0}, trail[4] = {0, 0, 0, 0}, c[4];
+  if (!UNI) {
+    ta_sr_trail_counter(b, (uint32_t)j, tid, step, c);
+    philox_rk(c[0], c[1], c[2], c[3], rk0, rk1, trail);
+  }
 #pragma unroll 1
   for (int k = 0; k < 4; ++k) {
     const int t0 = 4 * j + 32 * k;
-    uint32_t rnd[4] = {0, 0, 0, 0};
-    if (!UNI) {
-      uint32_t c0, c1, c2, c3;
-      ta_sr_counter(b, (uint32_t)(j + 8 * k), tid, step, &c0, &c1, &c2, &c3);
-      philox_rk(c0, c1, c2, c3, rk0, rk1, rnd);
+    if (!UNI && (k & 1) == 0) {
+      ta_sr_lead_counter(b, (uint32_t)j, (uint32_t)(k >> 1), tid, step, c);
+      philox_rk(c[0], c[1], c[2], c[3], rk0, rk1, lead);
     }
     const float4 lq = scr4[k * 32 + lane];
     const float l4[4] = {lq.x, lq.y, lq.z, lq.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const float u = UNI ? suni[t0 + i] : ta_u01(rnd[i]);
+      const float u = UNI ? suni[t0 + i] : ta_sr_u(ta_sr_lead(lead, k, i), ta_sr_trail(trail, k, i));
       const float cc = __fmul_rn(div_by(__fsub_rn(l4[i], vmin), nspan, rspan), nbf);
       const float fl = floorf(cc);
       const float fr = __fsub_rn(cc, fl);
@@ -666,6 +670,19 @@ __device__ __forceinline__ uint32_t requant_quad_fast(float4 la, float4 w, float
   return __byte_perm(w01, w23, 0x5410);
 }
 
+// 0.5 - u_mid for the 4 elements of a quad from their 16-bit lead halves
+// (words a, b of the quad's lead draw): u_mid = (lead + 0.5) 2^-16 is within
+// 2^-17 of u. prmt puts a half into the low mantissa bits of 2^7 (giving
+// 2^7 + lead 2^-16); both subtractions are exact.
+__device__ __forceinline__ float4 lead_w4(uint32_t a, uint32_t b, const PK& P) {
+  const float2 f01 = make_float2(__uint_as_float(__byte_perm(a, 0x43000000u, 0x7610)),
+                                 __uint_as_float(__byte_perm(a, 0x43000000u, 0x7632)));
+  const float2 f23 = make_float2(__uint_as_float(__byte_perm(b, 0x43000000u, 0x7610)),
+                                 __uint_as_float(__byte_perm(b, 0x43000000u, 0x7632)));
+  const float2 c = dup2(128.5f), h = dup2(0x1p-17f);
+  return cat4(P.sub(P.sub(c, f01), h), P.sub(P.sub(c, f23), h));
+}
+
 // Exact indices of one quad of a full, unflagged block (rare: a quad whose
 // fast decision was uncertain). Recomputes v_new of the 4 elements from the
 // staged inputs exactly as phase A does, takes ta_logf and applies the
@@ -704,6 +721,31 @@ __device__ __noinline__ uint32_t p1_requant_quad_exact(const StageMeta& M, const
     word |= (uint32_t)r << (8 * i);
   }
   return word;
+}
+
+// A quad whose lead-bits decision was uncertain: draws the trail bits of its
+// uniforms, repeats the certified test with the exact u and, if that is
+// still uncertain, applies the exact rule with the exact log.
+template <int MK, int VK, int PT, bool UNI, bool TABLE>
+__device__ __noinline__ uint32_t p1_requant_quad_retry(
+    const StageMeta& M, const uint8_t* st, int bi, int k, int t0, const float* tab, float lmin,
+    float span, float4 la, uint32_t lead_a, uint32_t lead_b, uint64_t gb, int j,
+    const uint32_t* rk0, const uint32_t* rk1, float vmin, float nspan, float rspan, float k1,
+    float thr, float tops) {
+  const PK P(M.c.one, M.c.nzero);
+  uint32_t ctr[4], trail[4];
+  ta_sr_trail_counter(gb, (uint32_t)j, M.c.tid, M.c.step, ctr);
+  philox_rk(ctr[0], ctr[1], ctr[2], ctr[3], rk0, rk1, trail);
+  const float4 u4 = make_float4(ta_sr_u(lead_a & 0xffffu, ta_sr_trail(trail, k, 0)),
+                                ta_sr_u(lead_a >> 16, ta_sr_trail(trail, k, 1)),
+                                ta_sr_u(lead_b & 0xffffu, ta_sr_trail(trail, k, 2)),
+                                ta_sr_u(lead_b >> 16, ta_sr_trail(trail, k, 3)));
+  const float4 w4 = cat4(P.sub(dup2(0.5f), lo2(u4)), P.sub(dup2(0.5f), hi2(u4)));
+  float emax = 0.0f;
+  const uint32_t word = requant_quad_fast(la, w4, dup2(vmin), dup2(k1), tops, P, &emax);
+  if (emax < thr) return word;
+  return p1_requant_quad_exact<MK, VK, PT, UNI, TABLE>(M, st, bi, t0, tab, lmin, span, u4, vmin,
+                                                       nspan, rspan);
 }
 
 // One 128-element block per 8-lane group (quad layout above).
@@ -1032,8 +1074,12 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
       // block is equal (all C are 0 then)
       const float k1 = (vmax == vmin) ? 0.0f : __fmul_rn(rspan, c.nbf);
       const float thr = requant_threshold(k1, c.nbf);
+      // with only the lead bits of u known, u_mid is within 2^-17 of it
+      const float thr_lead = __fsub_rn(thr, 0x1p-17f);
       const float2 lmin2 = dup2(vmin), k12 = dup2(k1);
       const float tops = __fadd_rn(RINT_MAGIC, c.nbf - 1.0f);
+      const uint64_t gb = (uint64_t)(b + M.boff);
+      uint32_t lead[4] = {0, 0, 0, 0};
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         const int t0 = 4 * j + 32 * k;
@@ -1042,22 +1088,24 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
           u4 = *reinterpret_cast<const float4*>(suni + t0);
           w4 = cat4(P.sub(dup2(0.5f), lo2(u4)), P.sub(dup2(0.5f), hi2(u4)));
         } else {
-          uint32_t rnd[4], c0, c1, c2, c3;
-          ta_sr_counter((uint64_t)(b + M.boff), (uint32_t)(j + 8 * k), c.tid, c.step, &c0, &c1,
-                        &c2, &c3);
-          philox_rk(c0, c1, c2, c3, kp.rk0, kp.rk1, rnd);
-          // u = (x >> 8) 2^-24 (ta_u01); 0.5 - u is exact
-          const float2 x01 = make_float2((float)(rnd[0] >> 8), (float)(rnd[1] >> 8));
-          const float2 x23 = make_float2((float)(rnd[2] >> 8), (float)(rnd[3] >> 8));
-          w4 = cat4(fma2(x01, dup2(-0x1p-24f), dup2(0.5f)), fma2(x23, dup2(-0x1p-24f), dup2(0.5f)));
-          u4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);  // recovered from w4 if needed
+          if ((k & 1) == 0) {  // one draw per quad pair: the lead halves of 8 elements
+            uint32_t ctr[4];
+            ta_sr_lead_counter(gb, (uint32_t)j, (uint32_t)(k >> 1), c.tid, c.step, ctr);
+            philox_rk(ctr[0], ctr[1], ctr[2], ctr[3], kp.rk0, kp.rk1, lead);
+          }
+          w4 = lead_w4(lead[2 * (k & 1)], lead[2 * (k & 1) + 1], P);
         }
         float emax = 0.0f;
-        uint32_t word = requant_quad_fast(scr4[k * 32 + lane], w4, lmin2, k12, tops, P, &emax);
-        if (emax >= thr) {  // rare: some element of the quad is within E of a decision boundary
-          if (!UNI) u4 = cat4(P.sub(dup2(0.5f), lo2(w4)), P.sub(dup2(0.5f), hi2(w4)));
-          word = p1_requant_quad_exact<MK, VK, PT, UNI, TABLE>(M, st, bi, t0, tab, lmin, span, u4,
-                                                               vmin, nspan, rspan);
+        const float4 la = scr4[k * 32 + lane];
+        uint32_t word = requant_quad_fast(la, w4, lmin2, k12, tops, P, &emax);
+        if (emax >= (UNI ? thr : thr_lead)) {  // rare: an element near a decision boundary
+          if (UNI)
+            word = p1_requant_quad_exact<MK, VK, PT, UNI, TABLE>(M, st, bi, t0, tab, lmin, span,
+                                                                 u4, vmin, nspan, rspan);
+          else
+            word = p1_requant_quad_retry<MK, VK, PT, UNI, TABLE>(
+                M, st, bi, k, t0, tab, lmin, span, la, lead[2 * (k & 1)], lead[2 * (k & 1) + 1],
+                gb, j, kp.rk0, kp.rk1, vmin, nspan, rspan, k1, thr, tops);
         }
         *reinterpret_cast<uint32_t*>(gidx + t0) = word;
       }

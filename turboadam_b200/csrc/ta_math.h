@@ -266,23 +266,46 @@ TA_HD void ta_philox4x32_10(uint32_t c0, uint32_t c1, uint32_t c2, uint32_t c3,
   out[0] = c0; out[1] = c1; out[2] = c2; out[3] = c3;
 }
 
-/* Uniform in [0, 1) with 24-bit resolution (same grid as torch.rand). */
-TA_HD float ta_u01(uint32_t x) { return ta_mul((float)(x >> 8), 0x1p-24f); }
-
 /*
- * Stochastic-rounding counter layout (shared by kernel and checker).
- * Element e = b*128 + 4*Q + i of a tensor (block b, quad Q in 0..31, i in
- * 0..3) takes word i of the Philox block with counter
- *   (c0, c1, c2, c3) = (b*32 + Q, tensor_id, step, b >> 27)
- * and key (seed_lo, seed_hi). The draw depends only on (seed, tensor, step,
- * element), so it is the same however the tensor is split across GPUs.
+ * Stochastic-rounding draws (shared by kernel and checker).
+ * Every element takes a uniform u = (lead * 2^8 + trail) * 2^-24 on the
+ * 24-bit grid of torch.rand, with lead (16 bits) and trail (8 bits) from two
+ * separate Philox4x32-10 streams keyed by (seed_lo, seed_hi). Element
+ * t = 4Q + i of block b (quad Q = j + 8k: lane j of the block's 8-lane
+ * group, the lane's quad k, element i of the quad) reads
+ *   lead  = 16-bit half (h & 1) of word h >> 1, h = 4(k & 1) + i, of
+ *           Philox(b*16 + 2j + (k >> 1), tensor_id, step, b >> 28),
+ *   trail = byte i of word k of Philox(b*8 + j, tensor_id, step, (b >> 29) | 2^31).
+ * The lead bits alone decide all but about 2^-16 of the roundings (the
+ * kernel tests whether u's remaining 2^-16 uncertainty can matter) and the
+ * trail stream is drawn only where it can. The draw depends only on (seed,
+ * tensor, step, element), so it is the same however the tensor is split
+ * across GPUs.
  */
-TA_HD void ta_sr_counter(uint64_t block, uint32_t quad, uint32_t tensor_id, uint32_t step,
-                         uint32_t* c0, uint32_t* c1, uint32_t* c2, uint32_t* c3) {
-  *c0 = (uint32_t)(block * 32u + quad);
-  *c1 = tensor_id;
-  *c2 = step;
-  *c3 = (uint32_t)(block >> 27);
+TA_HD void ta_sr_lead_counter(uint64_t block, uint32_t lane, uint32_t pair, uint32_t tensor_id,
+                              uint32_t step, uint32_t c[4]) {
+  c[0] = (uint32_t)(block * 16u + 2u * lane + pair);
+  c[1] = tensor_id;
+  c[2] = step;
+  c[3] = (uint32_t)(block >> 28);
+}
+TA_HD void ta_sr_trail_counter(uint64_t block, uint32_t lane, uint32_t tensor_id, uint32_t step,
+                               uint32_t c[4]) {
+  c[0] = (uint32_t)(block * 8u + lane);
+  c[1] = tensor_id;
+  c[2] = step;
+  c[3] = (uint32_t)(block >> 29) | 0x80000000u;
+}
+/* lead half of element (k, i) from the lead words of quad pair k >> 1; trail
+ * byte from the lane's trail words */
+TA_HD uint32_t ta_sr_lead(const uint32_t w[4], int k, int i) {
+  const int h = 4 * (k & 1) + i;
+  return (w[h >> 1] >> (16 * (h & 1))) & 0xffffu;
+}
+TA_HD uint32_t ta_sr_trail(const uint32_t t[4], int k, int i) { return (t[k] >> (8 * i)) & 0xffu; }
+/* u from its two parts (exact: a 24-bit integer times a power of two) */
+TA_HD float ta_sr_u(uint32_t lead, uint32_t trail) {
+  return ta_mul((float)((lead << 8) | trail), 0x1p-24f);
 }
 
 #endif /* TA_MATH_H */
