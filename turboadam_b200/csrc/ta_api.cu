@@ -286,6 +286,7 @@ DevTensor make_dev(const ta_tensor& t, const ta_group& g, uint64_t seed) {
   D.nbits = g.v_bits;
   D.nbf = (float)(1 << g.v_bits);
   D.sqbs = (float)std::sqrt((double)g.block_size);
+  D.rsqbs = 1.0f / D.sqbs;
   uint32_t f = 0;
   if (t.flags & TA_M_COSTATE) f |= DF_M_COSTATE;
   if (t.flags & TA_V_ONEQ) f |= DF_V_ONEQ;

@@ -75,6 +75,7 @@ struct __align__(16) DevTensor {
   float b1, omb1, b2, omb2;
   float wdf, nlr, eps, bc1;
   float bc2, rbc2, nbf, sqbs;
+  float rsqbs;         // RN(1 / sqbs)
   int32_t nbits;
   uint32_t flags;
   uint32_t tid;

@@ -124,6 +124,7 @@ struct __align__(16) Sc {
   float one;    // 1 and -0 as runtime values: the identity operands of PK
   float nzero;
   float ginv;   // DF_AMP: RN(1 / loss scale)
+  float rsqbs;  // RN(1 / sqbs)
 };
 
 __device__ __forceinline__ Sc load_sc(const DevTensor& D) {
@@ -137,6 +138,7 @@ __device__ __forceinline__ Sc load_sc(const DevTensor& D) {
   s.one = D.one;
   s.nzero = -0.0f * D.one;
   s.ginv = D.ginv;
+  s.rsqbs = D.rsqbs;
   return s;
 }
 
@@ -475,6 +477,67 @@ __device__ __forceinline__ float2 adam_pair_fast(float2 w, float2 x, float2 m, c
   return P.add(w, fma2(fma2(nden, q, n), yr, q));                      // q + (n - den q)/den
 }
 
+// Three-input min / max (one instruction on sm_100; NaN operands are
+// skipped like fminf / fmaxf -- the fast paths only see finite values).
+__device__ __forceinline__ float fmin3(float a, float b, float c) {
+  float r;
+  asm("min.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+// RN(1/x) for a positive normal x with a normal reciprocal: rcp.approx plus
+// one Newton step (equal to the IEEE reciprocal on every such input, checked
+// exhaustively on the device by ta_selftest_fast_math).
+__device__ __forceinline__ float rcp_exact(float x) {
+  const float y0 = rcp_approx(x);
+  return __fmaf_rn(__fmaf_rn(-x, y0, 1.0f), y0, y0);
+}
+// binary16 <-> binary32 of finite values (no NaN canonicalisation)
+__device__ __forceinline__ float h2f_fin(uint16_t h) {
+  float f;
+  asm("cvt.f32.f16 %0, %1;" : "=f"(f) : "h"((unsigned short)h));
+  return f;
+}
+__device__ __forceinline__ uint16_t f2h_fin(float f) {
+  unsigned short h;
+  asm("cvt.rn.f16.f32 %0, %1;" : "=h"(h) : "f"(f));
+  return (uint16_t)h;
+}
+
+// ta_expf of two arguments in [-110, 100] (callers clamp; ta_expf is 0 below
+// and +inf above that range, where this gives the same): the same operations
+// as ta_expf without its special-case branches, paired.
+__device__ __forceinline__ float2 expf2_core(float2 x, const PK& P) {
+  const float2 t = P.mul(x, dup2(TA_LOG2E));
+  const float2 kf = make_float2(rintf(t.x), rintf(t.y));
+  float2 r = fma2(kf, dup2(-TA_LN2_HI), x);
+  r = fma2(kf, dup2(-TA_LN2_LO), r);
+  float2 p = dup2(TA_EXP_P0);
+  p = fma2(p, r, dup2(TA_EXP_P1));
+  p = fma2(p, r, dup2(TA_EXP_P2));
+  p = fma2(p, r, dup2(TA_EXP_P3));
+  p = fma2(p, r, dup2(TA_EXP_P4));
+  p = fma2(p, r, dup2(TA_EXP_P5));
+  const float2 r2 = P.mul(r, r);
+  const float2 s = P.add(P.one, r);
+  const float2 err = P.add(P.sub(P.one, s), r);
+  float2 y = P.add(s, fma2(r2, p, err));
+  const int32_t k0 = (int32_t)kf.x, k1 = (int32_t)kf.y;
+  const int32_t a0 = k0 / 2, a1 = k1 / 2;
+  y = P.mul(y, make_float2(__uint_as_float((uint32_t)(a0 + 127) << 23),
+                           __uint_as_float((uint32_t)(a1 + 127) << 23)));
+  return P.mul(y, make_float2(__uint_as_float((uint32_t)(k0 - a0 + 127) << 23),
+                              __uint_as_float((uint32_t)(k1 - a1 + 127) << 23)));
+}
+
+// the IEEE operations out of line, so a rarely taken select stays a branch
+__device__ __noinline__ float div_ieee(float a, float b) { return __fdiv_rn(a, b); }
+__device__ __noinline__ float rcp_ieee(float a) { return __frcp_rn(a); }
+
 // ---------------------------------------------------------------------------
 // Pass 1
 // ---------------------------------------------------------------------------
@@ -661,7 +724,7 @@ __device__ __forceinline__ uint32_t requant_quad_fast(float4 la, float4 w, float
   const float2 s0 = P.add(d0, dup2(RINT_MAGIC)), s1 = P.add(d1, dup2(RINT_MAGIC));
   const float2 e0 = P.sub(d0, P.sub(s0, dup2(RINT_MAGIC)));
   const float2 e1 = P.sub(d1, P.sub(s1, dup2(RINT_MAGIC)));
-  *emax = fmaxf(fmaxf(fmaxf(fabsf(e0.x), fabsf(e0.y)), fmaxf(fabsf(e1.x), fabsf(e1.y))), *emax);
+  *emax = fmax3(fmax3(fabsf(e0.x), fabsf(e0.y), fabsf(e1.x)), fabsf(e1.y), *emax);
   // the integer part of s is rint(d) (its low byte, 0..nb-1 after the clamp)
   const uint32_t w01 = __byte_perm(__float_as_uint(fminf(s0.x, tops)),
                                    __float_as_uint(fminf(s0.y, tops)), 0x0040);
@@ -794,7 +857,17 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
     const uint8_t lab = st[L::OFF_LAB + bi];
     const float nrm = reinterpret_cast<const float*>(st + L::OFF_NRM)[bi];
     const uint16_t amp = reinterpret_cast<const uint16_t*>(st + L::OFF_AMP)[bi];
-    cs_scale = costate_scale(lab, nrm, amp, c.sqbs);
+    if (FULL) {
+      // norm / sqrt(bs) by Markstein (exact for norms in [2^-100, 2^100], 0 and
+      // non-finite ones); the IEEE division otherwise
+      const float ph = (nrm > 0.0f && nrm < 0x1p-100f) || nrm > 0x1p100f
+                           ? div_ieee(nrm, c.sqbs)
+                           : div_by(nrm, c.sqbs, c.rsqbs);
+      const float am = f16_to_f32_dev(amp);
+      cs_scale = lab == 1 ? ph : (lab == 2 ? am : 0.0f);
+    } else {
+      cs_scale = costate_scale(lab, nrm, amp, c.sqbs);
+    }
     sgn4 = *reinterpret_cast<const uint4*>(st + L::OFF_SGN + bi * 16);
   }
   uint32_t sw0 = sgn4.x, sw1 = sgn4.y, sw2 = sgn4.z, sw3 = sgn4.w;  // rotated per quad
@@ -804,18 +877,38 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
 
   // ---- per-block 1Q decode scalars (quantize.py:252-256) and exp table
   float lmin = 0.0f, span = 0.0f;
+  bool hdr_bad = false;  // FULL: a non-finite header takes the exact path
   const int nb = 1 << c.nbits;
   float* tab = table + q * TABLE_STRIDE;
   if (VK == VK_ONEQ) {
     const uint16_t* hdr = reinterpret_cast<const uint16_t*>(st + L::OFF_HDR);
     if (active) {
-      lmin = f16_to_f32_dev(hdr[bi * 2]);
-      span = __fsub_rn(f16_to_f32_dev(hdr[bi * 2 + 1]), lmin);
+      if (FULL) {
+        const uint32_t hw = reinterpret_cast<const uint32_t*>(hdr)[bi];
+        lmin = h2f_fin((uint16_t)hw);
+        span = __fsub_rn(h2f_fin((uint16_t)(hw >> 16)), lmin);
+        hdr_bad = !(fabsf(span) <= 3.4028234663852886e38f);  // NaN or inf in either half
+      } else {
+        lmin = f16_to_f32_dev(hdr[bi * 2]);
+        span = __fsub_rn(f16_to_f32_dev(hdr[bi * 2 + 1]), lmin);
+      }
     }
     if (TABLE) {
-      for (int t = j; t < nb; t += 8) {
-        const float qv = __fmul_rn(__fadd_rn((float)t, 0.5f), c.rnbf);
-        tab[t] = ta_expf(__fadd_rn(lmin, __fmul_rn(qv, span)));
+      if (FULL) {  // entries t and t + 8 as a pair
+        for (int t = j; t < nb; t += 16) {
+          const float2 qv = P.mul(P.add(make_float2((float)t, (float)(t + 8)), dup2(0.5f)),
+                                  dup2(c.rnbf));
+          float2 x = P.add(dup2(lmin), P.mul(qv, dup2(span)));
+          x = make_float2(fminf(fmaxf(x.x, -110.0f), 100.0f), fminf(fmaxf(x.y, -110.0f), 100.0f));
+          const float2 e = expf2_core(x, P);
+          tab[t] = e.x;
+          if (t + 8 < nb) tab[t + 8] = e.y;
+        }
+      } else {
+        for (int t = j; t < nb; t += 8) {
+          const float qv = __fmul_rn(__fadd_rn((float)t, 0.5f), c.rnbf);
+          tab[t] = ta_expf(__fadd_rn(lmin, __fmul_rn(qv, span)));
+        }
       }
     }
     __syncwarp();
@@ -851,12 +944,11 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
                                         __uint_as_float(sc ^ ((sb << 1) & 0x80000000u)));
         const float2 sd23 = make_float2(__uint_as_float(sc ^ ((sb << 2) & 0x80000000u)),
                                         __uint_as_float(sc ^ ((sb << 3) & 0x80000000u)));
-        float2 mh01 = P.add(P.mul(dup2(alpha_old), g01), sd01);
-        float2 mh23 = P.add(P.mul(dup2(alpha_old), g23), sd23);
-        if (!has_state) {
-          mh01 = zero2;
-          mh23 = zero2;
-        }
+        // without a previous encoding alpha_old = 0, the scale is +0 and no sign
+        // bit is set, so m_hat = RN(0 g) + (+0) = +0 exactly as the reference's
+        // zeros (a non-finite g is flagged for the exact path)
+        const float2 mh01 = P.add(P.mul(dup2(alpha_old), g01), sd01);
+        const float2 mh23 = P.add(P.mul(dup2(alpha_old), g23), sd23);
         m01 = P.add(P.mul(dup2(c.b1), mh01), P.mul(dup2(c.omb1), g01));
         m23 = P.add(P.mul(dup2(c.b1), mh23), P.mul(dup2(c.omb1), g23));
         am = fma2(m01, g01, am);
@@ -893,8 +985,8 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
         // quantize.py:275: approximate ln v_new (certified re-quantisation);
         // the block extremes are taken over v_new and converted exactly later
         scr4[k * 32 + lane] = cat4(ln_approx2(v01, P), ln_approx2(v23, P));
-        vmin = fminf(fminf(v01.x, v01.y), fminf(fminf(v23.x, v23.y), vmin));
-        vmax = fmaxf(fmaxf(v01.x, v01.y), fmaxf(fmaxf(v23.x, v23.y), vmax));
+        vmin = fmin3(fmin3(v01.x, v01.y, v23.x), v23.y, vmin);
+        vmax = fmax3(fmax3(v01.x, v01.y, v23.x), v23.y, vmax);
       } else if (VK == VK_FP32) {
         const float4 s4 = *reinterpret_cast<const float4*>(seas + t0);
         v01 = fma2(P.mul(dup2(c.omb2), g01), g01, P.mul(lo2(s4), dup2(c.b2)));  // optimizer.py:166
@@ -935,7 +1027,8 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
     }
     const bool bad = (nanacc.x != nanacc.x) || (nanacc.y != nanacc.y);
     if (VK == VK_ONEQ) {
-      fix = bad || vmin < FAST_V_MIN || (TABLE && (idor & (0x01010101u * (uint32_t)(0xff & ~(nb - 1)))) != 0);
+      fix = bad || hdr_bad || vmin < FAST_V_MIN ||
+            (TABLE && (idor & (0x01010101u * (uint32_t)(0xff & ~(nb - 1)))) != 0);
       // the whole block takes one path: its extremes are of v_new (fast) or
       // of ln v_new (exact path), never a mix
       fix = (__ballot_sync(0xffffffffu, fix) >> (8 * q)) & 0xffu;
@@ -1062,11 +1155,12 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
     }
     if (active && j == 0)
       reinterpret_cast<uint32_t*>(M.v_hdr)[b] =
-          (uint32_t)f32_to_f16_dev(vmin) | ((uint32_t)f32_to_f16_dev(vmax) << 16);
+          (FULL && !fix) ? (uint32_t)f2h_fin(vmin) | ((uint32_t)f2h_fin(vmax) << 16)
+                         : (uint32_t)f32_to_f16_dev(vmin) | ((uint32_t)f32_to_f16_dev(vmax) << 16);
     // (L - min) / span: |L - min| is 0 or >= 2^-47 (ln of floats != 1 is
     // >= 5.9e-8 in magnitude), inside div_by's exact range.
     const float nspan = clamp_min(__fsub_rn(vmax, vmin), 1e-10f);
-    const float rspan = __frcp_rn(nspan);
+    const float rspan = (FULL && !fix) ? rcp_exact(nspan) : rcp_ieee(nspan);
     const float* suni = reinterpret_cast<const float*>(st + L::OFF_UNI + L::A4::off(bi));
     uint8_t* gidx = M.v_idx + e0;
     if (FULL && !fix) {
