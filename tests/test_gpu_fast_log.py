@@ -77,3 +77,55 @@ def test_boundary_heavy_blocks_bitexact(oracle, v_bits):
         np.testing.assert_array_equal(hdr.view(np.uint16).reshape(-1), ost.v_hdr, err_msg=tag)
         got = tp.detach().cpu().numpy()
         assert np.array_equal(got.view(np.uint32), op.data.view(np.uint32)), tag
+
+
+def test_nonfinite_headers_and_wild_indices_bitexact(oracle):
+    """State a checkpoint could hold but a step never writes -- NaN / inf /
+    huge log-scale headers and indices >= 2^v_bits -- must take the exact
+    path and still match the checker bit for bit."""
+    from turboadam_b200 import TurboAdam
+
+    rng = np.random.default_rng(21)
+    n = 128 * 48
+    kw = dict(lr=1e-3, betas=(0.9, 0.999), weight_decay=0.0, v_bits=4, compress_m=False)
+    init = (rng.standard_normal(n) * 0.02).astype(np.float32)
+    tp = torch.nn.Parameter(torch.from_numpy(init.copy()).cuda())
+    op = oracle.OracleParam(init.copy())
+    opt = TurboAdam([tp], seed=9, exact_params=True, **kw)
+    oopt = oracle.OracleTurboAdam([oracle.OracleTurboAdam.make_group([op], **kw)])
+    h16 = lambda x: np.float16(x).view(np.uint16)  # noqa: E731
+    for step in range(3):
+        g = (rng.standard_normal(n) * 1e-3).astype(np.float32)
+        tp.grad = torch.from_numpy(g.copy()).cuda()
+        op.grad = g.copy()
+        if step == 1:
+            st, ost = opt.state[tp], oopt.state[id(op)]
+            hdr = ost.v_hdr.reshape(-1, 2).copy()
+            hdr[0] = [h16(np.nan), h16(-10.0)]
+            hdr[1] = [h16(-20.0), h16(np.inf)]
+            hdr[2] = [h16(-np.inf), h16(-5.0)]
+            hdr[3] = [h16(-60000.0), h16(60000.0)]
+            hdr[4] = [h16(50.0), h16(90.0)]
+            idx = ost.v_idx.copy()
+            idx[5 * 128:5 * 128 + 7] = [16, 17, 100, 255, 31, 64, 200]
+            ost.v_hdr[:] = hdr.reshape(-1)
+            ost.v_idx[:] = idx
+            cv = st["compressed_v"]
+            cv["scales"].view(torch.int16).reshape(-1)[: hdr.size].copy_(
+                torch.from_numpy(hdr.reshape(-1).view(np.int16)))
+            cv["indices"][: idx.size].copy_(torch.from_numpy(idx))
+        opt.step()
+        oopt.step(uniforms=lambda i, st_, npad: oracle.sr_uniforms(op.n, i, st_, 9))
+        torch.cuda.synchronize()
+        st, ost = opt.state[tp], oopt.state[id(op)]
+        tag = f"step {step}"
+        np.testing.assert_array_equal(st["compressed_v"]["indices"].cpu().numpy()[: ost.v_idx.size],
+                                      ost.v_idx, err_msg=tag)
+        hdr = st["compressed_v"]["scales"].contiguous().view(torch.int16).cpu().numpy()
+        got_h = hdr.view(np.uint16).reshape(-1)[: ost.v_hdr.size]
+        nan_ref = np.isnan(ost.v_hdr.view(np.float16).astype(np.float32))
+        np.testing.assert_array_equal(got_h[~nan_ref], ost.v_hdr[~nan_ref], err_msg=tag)
+        assert np.isnan(got_h[nan_ref].view(np.float16).astype(np.float32)).all(), tag
+        got = tp.detach().cpu().numpy()
+        same = (got.view(np.uint32) == op.data.view(np.uint32)) | (np.isnan(got) & np.isnan(op.data))
+        assert same.all(), tag
