@@ -109,7 +109,8 @@ struct P2L {
   static constexpr int STAGE = (END + 127) / 128 * 128;
 };
 
-constexpr int TABLE_STRIDE = 65;     // per-group exp table (<= 64 entries), padded
+constexpr int TABLE_STRIDE = 72;     // per-group exp table (<= 64 entries); the 4 groups of
+                                     // a warp start 8 banks apart (72 = 8 mod 32)
 constexpr int SCR_FLOATS = 16 * 32;  // per-warp scratch: ln v_new, 4 quads x 32 lanes x 4
 
 // Per-tensor scalars (fp32 values of the Python hyper-parameters as torch
@@ -196,12 +197,17 @@ __device__ __forceinline__ int find_entry(const int64_t* lbeg, int nl, int64_t t
 // increase, so the entry only moves forward (one load per tensor change).
 struct EntryWalk {
   int en = -1;
-  int64_t next = 0;  // first tile of entry en + 1
-  __device__ __forceinline__ int at(const int64_t* lbeg, int nl, int64_t tile) {
+  int64_t first = 0;  // first tile of entry en
+  int64_t next = 0;   // first tile of entry en + 1
+  int t = -1;         // tensor index of entry en
+  __device__ __forceinline__ int at(const int64_t* lbeg, const int32_t* lidx, int nl,
+                                    int64_t tile) {
     if (en < 0 || tile >= next) {
       en = (en < 0) ? find_entry(lbeg, nl, tile) : en;
       while (en + 1 < nl && lbeg[en + 1] <= tile) ++en;
       next = (en + 1 < nl) ? lbeg[en + 1] : INT64_MAX;
+      first = lbeg[en];
+      t = lidx[en];
     }
     return en;
   }
@@ -1259,19 +1265,20 @@ __global__ void __launch_bounds__(NTHR, 4) k_pass1(const __grid_constant__ KPara
       int cur_t = -1;
       float cur_alpha = 0.0f;
       Sc cur_c;
+      DevTensor D;  // the current tensor's descriptor, copied once per tensor change
       for (int64_t tile = blockIdx.x; tile < kp.total; tile += gridDim.x, ++it) {
         const int s = it % NSTAGE;
         const uint32_t ph = (uint32_t)(it / NSTAGE) & 1u;
         uint8_t* st = stages + s * L::STAGE;
-        const int en = walk.at(kp.lbeg, kp.nl, tile);
-        const int t = kp.lidx[en];
-        const DevTensor& D = kp.T[t];
+        walk.at(kp.lbeg, kp.lidx, kp.nl, tile);
+        const int t = walk.t;
         if (t != cur_t) {  // per-tensor values, loaded once per tensor change
           cur_t = t;
+          D = kp.T[t];
           cur_c = load_sc(D);
           cur_alpha = (MK == MK_COSTATE && (D.flags & DF_M_HAS_STATE)) ? *D.alpha_state : 0.0f;
         }
-        const int64_t b0 = (tile - kp.lbeg[en]) * TB;
+        const int64_t b0 = (tile - walk.first) * TB;
         const int nblk = (int)min((int64_t)TB, D.nblk - b0);
         if (it >= NSTAGE && !wait_bar(&done[s], ph ^ 1u, kp.status)) break;
         StageMeta& m = meta[s];
@@ -1605,20 +1612,21 @@ __global__ void __launch_bounds__(NTHR, 6) k_pass2(const __grid_constant__ KPara
       int cur_t = -1;
       float cur_aold = 0.0f, cur_anew = 0.0f;
       Sc cur_c;
+      DevTensor D;  // the current tensor's descriptor, copied once per tensor change
       for (int64_t tile = blockIdx.x; tile < kp.total; tile += gridDim.x, ++it) {
         const int s = it % NSTAGE2;
         const uint32_t ph = (uint32_t)(it / NSTAGE2) & 1u;
         uint8_t* st = stages + s * L::STAGE;
-        const int en = walk.at(kp.lbeg, kp.nl, tile);
-        const int t = kp.lidx[en];
-        const DevTensor& D = kp.T[t];
+        walk.at(kp.lbeg, kp.lidx, kp.nl, tile);
+        const int t = walk.t;
         if (t != cur_t) {
           cur_t = t;
+          D = kp.T[t];
           cur_c = load_sc(D);
           cur_aold = (D.flags & DF_M_HAS_STATE) ? *D.alpha_state : 0.0f;
           cur_anew = *D.alpha_new;
         }
-        const int64_t b0 = (tile - kp.lbeg[en]) * TB;
+        const int64_t b0 = (tile - walk.first) * TB;
         const int nblk = (int)min((int64_t)TB, D.nblk - b0);
         const bool hs = D.flags & DF_M_HAS_STATE;
         const int64_t nfull = min((int64_t)nblk, (D.n - b0 * BS) / BS);
