@@ -62,7 +62,7 @@ def _declare(L):
         "orc_alpha": (_F, [_P, _P, _I64, _I]),
         "orc_costate_update": (
             None,
-            [_P, _P, _P, _P, _F, _I, _P, _I64, _I, _D, _D, _D, _P, _P, _P, _P, _P],
+            [_P, _P, _P, _P, _F, _I, _P, _I64, _I, _D, _D, _D, _P, _P, _P, _P, _P, _P, _I],
         ),
         "orc_weight_decay": (None, [_P, _I, _I64, _D, _D]),
         "orc_exp_avg": (None, [_P, _P, _I64, _D]),
@@ -229,6 +229,8 @@ class CoStateOracle:
     amp: np.ndarray = None  # fp16 bits
     last_ratios: np.ndarray = None
     last_tau: np.ndarray = None
+    error_feedback: bool = False
+    ef_residual: np.ndarray = None  # fp32 [n] once the first step has run
 
     def __post_init__(self):
         B = n_blocks(self.n, self.bs)
@@ -238,7 +240,7 @@ class CoStateOracle:
         self.amp = np.zeros(B, np.uint16)
 
     def update(self, g, beta1, alpha_inject=None):
-        """costate.py:367-464 (error_feedback=False). Returns m_new."""
+        """costate.py:367-464. Returns m_new."""
         g = np.ascontiguousarray(g, np.float32).reshape(-1)
         B = n_blocks(self.n, self.bs)
         m_new = np.empty(self.n, np.float32)
@@ -249,11 +251,16 @@ class CoStateOracle:
         if alpha_inject is not None:
             inj_arr = np.array([alpha_inject], np.float32)
             inj = _ptr(inj_arr)
+        ef_mode = 0
+        if self.error_feedback:
+            ef_mode = 2 if self.ef_residual is not None else 1
+            if self.ef_residual is None:
+                self.ef_residual = np.zeros(self.n, np.float32)
         lib().orc_costate_update(
             _ptr(self.labels), _ptr(self.signs), _ptr(self.norms), _ptr(self.amp),
             float(self.alpha), int(self.has_state), _ptr(g), self.n, self.bs, float(beta1),
             float(self.null_pct), float(self.amp_pct), inj, _ptr(m_new), _ptr(a_out),
-            _ptr(ratios), _ptr(tau))
+            _ptr(ratios), _ptr(tau), _ptr(self.ef_residual) if ef_mode else None, ef_mode)
         self.alpha = float(a_out[0])
         self.has_state = True
         self.last_ratios = ratios
@@ -306,11 +313,12 @@ class OracleTurboAdam:
     @staticmethod
     def make_group(params, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0,
                    block_size=128, v_bits=4, compress_m=True, compress_v=True, null_pct=0.10,
-                   amp_pct=0.90, min_m_compress_elements=4096):
+                   amp_pct=0.90, min_m_compress_elements=4096, error_feedback=False):
         return dict(params=list(params), lr=lr, betas=betas, eps=eps,
                     weight_decay=weight_decay, block_size=block_size, v_bits=v_bits,
                     compress_m=compress_m, compress_v=compress_v, null_pct=null_pct,
-                    amp_pct=amp_pct, min_m_compress_elements=min_m_compress_elements)
+                    amp_pct=amp_pct, min_m_compress_elements=min_m_compress_elements,
+                    error_feedback=error_feedback)
 
     def step(self, uniforms, alpha_inject=lambda i, s: None):
         pid = 0
@@ -331,7 +339,8 @@ class OracleTurboAdam:
                     st.compress_m = bool(group["compress_m"]
                                          and p.n >= group["min_m_compress_elements"])
                     if st.compress_m:
-                        st.mgr = CoStateOracle(p.n, bs, group["null_pct"], group["amp_pct"])
+                        st.mgr = CoStateOracle(p.n, bs, group["null_pct"], group["amp_pct"],
+                                               error_feedback=bool(group.get("error_feedback")))
                     else:
                         st.exp_avg = np.zeros(p.n, np.float32)
                     if not group["compress_v"]:

@@ -129,19 +129,28 @@ def gen_v_cases(mods, out_dir):
 # ---------------------------------------------------------------------------
 
 
-def gen_costate_cases(mods, out_dir):
+COSTATE_SPECS = [
+    (4096, 0.10, 0.90, 5),
+    (4133, 0.10, 0.90, 5),
+    (384, 0.10, 0.90, 4),
+    (300, 0.10, 0.90, 4),
+    (65536 + 11, 0.10, 0.90, 4),
+    (20000, 0.20, 0.70, 4),
+    (128, 0.10, 0.90, 3),
+]
+# error_feedback=True sequences (costate.py:410-437), written to costate_ef.npz
+COSTATE_EF_SPECS = [
+    (4096, 0.10, 0.90, 5),
+    (4133, 0.10, 0.90, 5),
+    (20000, 0.20, 0.70, 4),
+]
+
+
+def gen_costate_cases(mods, out_dir, ef=False):
     _, costate, _, _, _ = mods
-    rng = np.random.default_rng(99)
+    rng = np.random.default_rng(199 if ef else 99)
     cases = {}
-    specs = [
-        (4096, 0.10, 0.90, 5),
-        (4133, 0.10, 0.90, 5),
-        (384, 0.10, 0.90, 4),
-        (300, 0.10, 0.90, 4),
-        (65536 + 11, 0.10, 0.90, 4),
-        (20000, 0.20, 0.70, 4),
-        (128, 0.10, 0.90, 3),
-    ]
+    specs = COSTATE_EF_SPECS if ef else COSTATE_SPECS
     rec = {}
     orig_thr = costate.compute_thresholds
 
@@ -154,7 +163,8 @@ def gen_costate_cases(mods, out_dir):
     costate.compute_thresholds = thr
     try:
         for ci, (n, lo, hi, nsteps) in enumerate(specs):
-            mgr = costate.CoStateManager(block_size=128, null_pct=lo, amp_pct=hi)
+            mgr = costate.CoStateManager(block_size=128, null_pct=lo, amp_pct=hi,
+                                         error_feedback=ef)
             key = f"c{ci:03d}"
             for s in range(nsteps):
                 scale = 10.0 ** rng.uniform(-5, -2)
@@ -169,6 +179,8 @@ def gen_costate_cases(mods, out_dir):
                          signs=enc["sign_packed"].numpy().copy(),
                          norms=enc["block_norms"].numpy().copy(),
                          amp=h16(enc["scales"]), ratios=rec["ratios"], tau=rec["tau"])
+                if ef:
+                    d["ef_residual"] = mgr._ef_residual.numpy().copy()
                 for k, v in d.items():
                     cases[f"{key}_s{s}_{k}"] = v
             cases[f"{key}_meta"] = np.array([n, nsteps], np.int64)
@@ -176,8 +188,9 @@ def gen_costate_cases(mods, out_dir):
     finally:
         costate.compute_thresholds = orig_thr
     cases["n_cases"] = np.array([len(specs)], np.int64)
-    np.savez_compressed(os.path.join(out_dir, "costate.npz"), **cases)
-    print("costate cases:", len(specs))
+    name = "costate_ef.npz" if ef else "costate.npz"
+    np.savez_compressed(os.path.join(out_dir, name), **cases)
+    print(name, "cases:", len(specs))
 
 
 # ---------------------------------------------------------------------------
@@ -208,6 +221,12 @@ RUNS = {
         [((4096,), "f32", 0), ((130,), "f32", 0), ((4200,), "f32", 0)],
         [dict(lr=1e-3, weight_decay=0.02, v_bits=2, min_m_compress_elements=4100)],
         5, {(2, 1), (3, 0)},  # (step, param) pairs with grad None
+    ),
+    "ef": (
+        [((64, 80), "f32", 0), ((4133,), "f32", 0), ((90,), "f32", 0), ((48, 100), "f32", 1)],
+        [dict(lr=1e-3, weight_decay=0.01, v_bits=4, error_feedback=True),
+         dict(lr=5e-4, weight_decay=0.0, v_bits=3, error_feedback=True, compress_v=False)],
+        5, {(2, 1)},
     ),
 }
 
@@ -275,6 +294,8 @@ def gen_optimizer_runs(mods, out_dir):
                     data[f"s{s}_vsq{pi}"] = st["exp_avg_sq"].numpy().copy()
                 if "m_mgr" in st:
                     mg = st["m_mgr"]
+                    if mg._ef_residual is not None:
+                        data[f"s{s}_ef{pi}"] = mg._ef_residual.numpy().copy()
                     data[f"s{s}_alpha{pi}"] = np.array([float(mg._alpha)], np.float32)
                     data[f"s{s}_labels{pi}"] = mg._encoded["labels"].numpy().copy()
                     data[f"s{s}_signs{pi}"] = mg._encoded["sign_packed"].numpy().copy()
@@ -297,6 +318,7 @@ def main():
     mods = _import_reference(a.ref)
     gen_v_cases(mods, a.out)
     gen_costate_cases(mods, a.out)
+    gen_costate_cases(mods, a.out, ef=True)
     gen_optimizer_runs(mods, a.out)
 
 

@@ -89,6 +89,27 @@ def test_costate_golden(oracle, inject):
                 break  # later steps of an un-injected run legitimately diverge
 
 
+def test_costate_error_feedback_golden(oracle):
+    """CoStateManager(error_feedback=True) sequences (costate.py:410-437) with the
+    reference's alpha injected: every encoding and the fp32 residual bit-exact."""
+    d = GU.load("costate_ef.npz")
+    for c in range(int(d["n_cases"][0])):
+        k = f"c{c:03d}"
+        n, ns = (int(x) for x in d[k + "_meta"])
+        lo, hi = (float(x) for x in d[k + "_pct"])
+        mgr = oracle.CoStateOracle(n, 128, lo, hi, error_feedback=True)
+        for s in range(ns):
+            m = mgr.update(d[f"{k}_s{s}_g"], 0.9, float(d[f"{k}_s{s}_alpha"][0]))
+            tag = f"{k} step {s}"
+            np.testing.assert_array_equal(m, d[f"{k}_s{s}_m_new"], err_msg=tag)
+            np.testing.assert_array_equal(mgr.labels, d[f"{k}_s{s}_labels"], err_msg=tag)
+            np.testing.assert_array_equal(mgr.signs, d[f"{k}_s{s}_signs"], err_msg=tag)
+            np.testing.assert_array_equal(mgr.norms, d[f"{k}_s{s}_norms"], err_msg=tag)
+            np.testing.assert_array_equal(mgr.amp, d[f"{k}_s{s}_amp"], err_msg=tag)
+            np.testing.assert_array_equal(mgr.ef_residual.view(np.uint32),
+                                          d[f"{k}_s{s}_ef_residual"].view(np.uint32), err_msg=tag)
+
+
 def replay_optimizer_run(oracle, name, inject_alpha=True):
     """Replays one golden optimizer run in the checker; yields per-step
     (step, params, oracle_state, fixture)."""
@@ -113,7 +134,7 @@ def replay_optimizer_run(oracle, name, inject_alpha=True):
         yield s, params, opt, d
 
 
-@pytest.mark.parametrize("name", ["block", "groups", "bf16", "gradnone"])
+@pytest.mark.parametrize("name", ["block", "groups", "bf16", "gradnone", "ef"])
 def test_optimizer_runs_golden(oracle, name):
     pspecs = GU.runs()[name][0]
     prev, scale = {}, {}
@@ -144,6 +165,10 @@ def test_optimizer_runs_golden(oracle, name):
                 np.testing.assert_array_equal(st.mgr.signs, d[f"s{s}_signs{pi}"], err_msg=tag)
                 np.testing.assert_array_equal(st.mgr.norms, d[f"s{s}_norms{pi}"], err_msg=tag)
                 np.testing.assert_array_equal(st.mgr.amp, d[f"s{s}_amp{pi}"], err_msg=tag)
+                if f"s{s}_ef{pi}" in d:
+                    np.testing.assert_array_equal(st.mgr.ef_residual.view(np.uint32),
+                                                  d[f"s{s}_ef{pi}"].reshape(-1).view(np.uint32),
+                                                  err_msg=tag)
             if st.exp_avg is not None:
                 np.testing.assert_array_equal(st.exp_avg, d[f"s{s}_m{pi}"].reshape(-1),
                                               err_msg=tag)
