@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define TA_ABI_VERSION 2
+#define TA_ABI_VERSION 3
 
 typedef enum ta_status {
   TA_OK = 0,
@@ -50,6 +50,11 @@ enum {
   TA_NO_PARAM = 1u << 3,    /* skip weight decay and the parameter update         */
   TA_M_SPANNING = 1u << 4,  /* CoState shard of a tensor split over ranks:
                                alpha and thresholds reduced via ta_step_phase     */
+  TA_M_EF = 1u << 6,        /* CoState error feedback (costate.py:410-437): m's
+                               EMA takes g + m_ef_dev, and after the encode the
+                               residual becomes the EMA of what it lost       */
+  TA_M_EF_STATE = 1u << 7,  /* m_ef_dev holds a residual (the reference's
+                               _ef_residual is not None)                       */
   TA_EXACT_PARAM = 1u << 5  /* parameter update with correctly rounded v / bc2,
                                sqrt and division: bit-identical to the
                                reference's op sequence (optimizer.py:163-170).
@@ -118,6 +123,8 @@ typedef struct ta_tensor {
   int64_t global_blocks;      /* blocks of the whole tensor (0: this tensor's)     */
   int64_t exch_chunk_off;     /* TA_M_SPANNING: this tensor's slot in the exchange */
   int64_t exch_hist_off;      /*   regions (ta_exchange_layout), in elements       */
+  float* m_ef_dev;            /* TA_M_EF: [n] fp32 error-feedback residual, read
+                                 (with TA_M_EF_STATE) and rewritten by the step  */
 } ta_tensor;
 
 /* shard boundaries of a spanning tensor fall on multiples of this many blocks

@@ -34,7 +34,7 @@ def test_header_symbols_exported(lib):
     assert sorted(_lib.EXPORTED) == names
     for n in names:
         assert hasattr(lib, n), n
-    assert lib.ta_abi_version() == 2
+    assert lib.ta_abi_version() == 3
 
 
 def test_struct_layout_matches_header(lib):

@@ -35,6 +35,10 @@ def _same(oa, a, ob, b):
             for k in ("labels", "sign_packed", "block_norms"):
                 assert torch.equal(sa["m_mgr"]._encoded[k].view(torch.uint8),
                                    sb["m_mgr"]._encoded[k].view(torch.uint8)), k
+            ea, eb = sa["m_mgr"]._ef_residual, sb["m_mgr"]._ef_residual
+            assert (ea is None) == (eb is None)
+            if ea is not None:
+                assert torch.equal(ea.view(torch.int32), eb.view(torch.int32))
         if "exp_avg" in sa:
             assert torch.equal(sa["exp_avg"], sb["exp_avg"])
 
@@ -58,11 +62,13 @@ def test_capturable_eager_matches_default():
     assert isinstance(ob.state[b[0]]["step"], torch.Tensor)
 
 
-def test_cuda_graph_replay_matches_default():
+@pytest.mark.parametrize("error_feedback", [False, True])
+def test_cuda_graph_replay_matches_default(error_feedback):
     from turboadam_b200 import TurboAdam
 
     a, b = _params(), _params()
-    oa, ob = TurboAdam(a, **KW), TurboAdam(b, capturable=True, **KW)
+    kw = dict(KW, error_feedback=error_feedback)
+    oa, ob = TurboAdam(a, **kw), TurboAdam(b, capturable=True, **kw)
     for p, g in zip(b, _grads(b, 0)):
         p.grad = g  # static gradient storage for the graph
     for p, g in zip(a, _grads(a, 0)):

@@ -41,11 +41,11 @@ def _grads(ps, step):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("pack", [False, True])
-def test_bitexact_resume_from_portable_checkpoint(pack):
+@pytest.mark.parametrize("pack,ef", [(False, False), (True, False), (False, True)])
+def test_bitexact_resume_from_portable_checkpoint(pack, ef):
     from turboadam_b200 import TurboAdam
 
-    kw = dict(lr=6e-4, weight_decay=0.01, v_bits=3)
+    kw = dict(lr=6e-4, weight_decay=0.01, v_bits=3, error_feedback=ef)
     a = _make()
     oa = TurboAdam(a, seed=1234, **kw)
     for s in range(5):
@@ -82,5 +82,9 @@ def test_bitexact_resume_from_portable_checkpoint(pack):
             ea, ec = sa["m_mgr"]._encoded, sc["m_mgr"]._encoded
             for k in ("labels", "sign_packed", "block_norms"):
                 assert torch.equal(ea[k].view(torch.uint8), ec[k].view(torch.uint8)), k
+            ra, rc = sa["m_mgr"]._ef_residual, sc["m_mgr"]._ef_residual
+            assert (ra is None) == (rc is None) and (ra is not None) == ef
+            if ef:
+                assert torch.equal(ra.view(torch.int32), rc.view(torch.int32))
         if "exp_avg" in sa:
             assert torch.equal(sa["exp_avg"], sc["exp_avg"])

@@ -189,6 +189,10 @@ def run_compare(oracle, shapes, groups_kw, nsteps, dtype=torch.float32, parity=F
                 np.testing.assert_array_equal(to_np(enc["block_norms"]).view(np.uint32),
                                               om.norms.view(np.uint32), err_msg=tag)
                 np.testing.assert_array_equal(bits16(enc["scales"]), om.amp, err_msg=tag)
+                if om.ef_residual is not None:
+                    np.testing.assert_array_equal(
+                        to_np(mg._ef_residual).reshape(-1).view(np.uint32),
+                        om.ef_residual.view(np.uint32), err_msg=tag)
             if "exp_avg" in st:
                 np.testing.assert_array_equal(to_np(st["exp_avg"]).reshape(-1).view(np.uint32),
                                               ost.exp_avg.view(np.uint32), err_msg=tag)
@@ -246,7 +250,7 @@ def test_sparse_embedding_rows(oracle, exact_params):
 # ---------------------------------------------------------------------------
 
 
-@pytest.mark.parametrize("name", ["block", "groups", "bf16", "gradnone"])
+@pytest.mark.parametrize("name", ["block", "groups", "bf16", "gradnone", "ef"])
 def test_reference_golden_on_gpu(name):
     from turboadam_b200 import TurboAdam
 
@@ -317,6 +321,12 @@ def test_reference_golden_on_gpu(name):
                                               err_msg=tag)
                 np.testing.assert_array_equal(bits16(enc["scales"]), d[f"s{s}_amp{pi}"],
                                               err_msg=tag)
+                if f"s{s}_ef{pi}" in d:  # error-feedback residual (costate.py:428-437)
+                    ef = st["m_mgr"]._ef_residual
+                    assert tuple(ef.shape) == tuple(pspecs[pi][0]), tag
+                    np.testing.assert_array_equal(to_np(ef).reshape(-1).view(np.uint32),
+                                                  d[f"s{s}_ef{pi}"].reshape(-1).view(np.uint32),
+                                                  err_msg=tag)
             if "exp_avg" in st:
                 np.testing.assert_array_equal(to_np(st["exp_avg"]).reshape(-1),
                                               d[f"s{s}_m{pi}"].reshape(-1), err_msg=tag)
@@ -350,6 +360,45 @@ def test_reference_costate_golden_on_gpu():
             np.testing.assert_array_equal(to_np(enc["block_norms"]), d[f"{k}_s{s}_norms"],
                                           err_msg=tag)
             np.testing.assert_array_equal(bits16(enc["scales"]), d[f"{k}_s{s}_amp"], err_msg=tag)
+
+
+def test_reference_costate_ef_golden_on_gpu():
+    """CoStateManager(error_feedback=True).update seam on the GPU vs the
+    reference, alpha injected: encodings, m_new and the residual bit-exact."""
+    from turboadam_b200.costate import CoStateManager
+    from turboadam_b200.optimizer import _single_costate_update
+
+    d = GU.load("costate_ef.npz")
+    for c in range(int(d["n_cases"][0])):
+        k = f"c{c:03d}"
+        n, ns = (int(x) for x in d[k + "_meta"])
+        lo, hi = (float(x) for x in d[k + "_pct"])
+        mgr = CoStateManager(128, error_feedback=True, null_pct=lo, amp_pct=hi)
+        for s in range(ns):
+            m = _single_costate_update(mgr, cuda(d[f"{k}_s{s}_g"]), 0.9,
+                                       alpha_inject=cuda(d[f"{k}_s{s}_alpha"]))
+            torch.cuda.synchronize()
+            tag = f"{k} step {s}"
+            enc = mgr._encoded
+            np.testing.assert_array_equal(to_np(m), d[f"{k}_s{s}_m_new"], err_msg=tag)
+            np.testing.assert_array_equal(to_np(enc["labels"]), d[f"{k}_s{s}_labels"], err_msg=tag)
+            np.testing.assert_array_equal(to_np(enc["sign_packed"]), d[f"{k}_s{s}_signs"],
+                                          err_msg=tag)
+            np.testing.assert_array_equal(bits16(enc["scales"]), d[f"{k}_s{s}_amp"], err_msg=tag)
+            np.testing.assert_array_equal(to_np(mgr._ef_residual).view(np.uint32),
+                                          d[f"{k}_s{s}_ef_residual"].view(np.uint32), err_msg=tag)
+
+
+@pytest.mark.parametrize("exact_params", [True, False])
+def test_error_feedback_vs_checker(oracle, exact_params):
+    """error_feedback=True over mixed kinds, Philox draws and the GPU's own
+    alpha: packed state and residuals bit-exact vs the checker."""
+    opt = run_compare(oracle, [(96, 70), (4133,), (300,), (64, 80)],
+                      [dict(lr=1e-3, weight_decay=0.01, v_bits=4, error_feedback=True),
+                       dict(lr=5e-4, v_bits=3, error_feedback=True, compress_v=False)],
+                      nsteps=4, assign=[0, 0, 0, 1], exact_params=exact_params)
+    assert all(st["m_mgr"]._ef_residual is not None
+               for st in opt.state.values() if "m_mgr" in st)
 
 
 def test_v_update_golden_on_gpu():

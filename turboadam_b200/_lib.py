@@ -24,6 +24,8 @@ TA_M_HAS_STATE = 1 << 2
 TA_NO_PARAM = 1 << 3
 TA_M_SPANNING = 1 << 4
 TA_EXACT_PARAM = 1 << 5
+TA_M_EF = 1 << 6
+TA_M_EF_STATE = 1 << 7
 TA_PHASE_PASS1, TA_PHASE_PASS2, TA_PHASE_SEL1, TA_PHASE_SEL2, TA_PHASE_LABELS = range(5)
 TA_SHARD_ALIGN_BLOCKS = 4096
 TA_STATUS_NONFINITE_GRAD = 1 << 0
@@ -95,6 +97,7 @@ class TaTensor(ctypes.Structure):
         ("global_blocks", ctypes.c_int64),
         ("exch_chunk_off", ctypes.c_int64),
         ("exch_hist_off", ctypes.c_int64),
+        ("m_ef_dev", ctypes.c_void_p),
     ]
 
 

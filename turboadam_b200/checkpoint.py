@@ -81,6 +81,8 @@ def portable_state_dict(opt, pack: bool = False) -> dict:
                     "original_numel": int(v._original_numel),
                     "error_feedback": bool(v._error_feedback),
                     "encoded": None if enc is None else {kk: _compact(t) for kk, t in enc.items()},
+                    "ef_residual": (None if v._ef_residual is None
+                                    else _compact(v._ef_residual)),
                 }
             elif isinstance(v, torch.Tensor):
                 o[name] = _compact(v)
@@ -113,6 +115,7 @@ def load_portable_state_dict(opt, sd: dict) -> None:
                 mgr._alpha = v["alpha"]
                 mgr._original_numel = v["original_numel"]
                 mgr._encoded = None if v["encoded"] is None else dict(v["encoded"])
+                mgr._ef_residual = v.get("ef_residual")
                 o[name] = mgr
             else:
                 o[name] = v

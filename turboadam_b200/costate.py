@@ -51,7 +51,7 @@ class CoStateManager:
         self._bufs = None  # padded device buffers
 
     # -- storage ---------------------------------------------------------
-    def allocate(self, n: int, device) -> None:
+    def allocate(self, n: int, device, shape=None) -> None:
         bs = self.block_size
         B = _n_blocks(n, bs)
         P = padded_blocks(n, bs)
@@ -63,8 +63,11 @@ class CoStateManager:
             "scales": torch.zeros(P, dtype=torch.float16, **z),
             "alpha": torch.zeros(1, dtype=torch.float32, **z),
         }
+        if self._error_feedback:  # the residual (costate.py:428-437), fp32 like g
+            self._bufs["ef"] = torch.zeros(n, dtype=torch.float32, **z)
         self._n = n
         self._B = B
+        self._shape = tuple(shape) if shape is not None else (n,)
 
     def _views(self):
         b = self._bufs
@@ -80,19 +83,32 @@ class CoStateManager:
         if self._encoded is None:
             self._encoded = self._views()
             self._alpha = self._bufs["alpha"].view(())
+        if self._error_feedback and self._ef_residual is None:
+            # the reference keeps the residual in the gradient's shape
+            self._ef_residual = self._bufs["ef"].view(self._shape)
         self._original_numel = self._n
         self._has_state = True
+
+    def ef_pointer(self) -> int:
+        """Device address of the error-feedback residual buffer (0 without)."""
+        ef = self._bufs.get("ef") if self._bufs else None
+        return ef.data_ptr() if ef is not None else 0
 
     def pointers(self):
         b = self._bufs
         return (b["labels"].data_ptr(), b["sign_packed"].data_ptr(), b["block_norms"].data_ptr(),
                 b["scales"].data_ptr(), b["alpha"].data_ptr())
 
-    def adopt(self, n: int, device) -> None:
+    def adopt(self, n: int, device, shape=None) -> None:
         """Re-home loaded state (any dtype/device, unpadded) into padded buffers."""
         enc = self._encoded
         alpha = self._alpha
-        self.allocate(n, device)
+        ef = getattr(self, "_ef_residual", None)
+        self._ef_residual = None
+        self.allocate(n, device, shape)
+        if ef is not None and self._error_feedback:
+            self._bufs["ef"].copy_(ef.reshape(-1).to(device=device, dtype=torch.float32))
+            self._ef_residual = self._bufs["ef"].view(self._shape)
         if enc is not None:
             for k, v in self._views().items():
                 src = enc[k].reshape(-1).to(device=device)

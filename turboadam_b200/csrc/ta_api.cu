@@ -55,10 +55,10 @@ void threshold_ranks(int64_t B, double null_pct, double amp_pct, int64_t* lo, in
 }
 
 // ---- workspace layout ---------------------------------------------------
-constexpr int kMaxLists = 32;
+constexpr int kMaxLists = 40;
 
 struct CsSlot {
-  size_t part, ratios, hist, sel, alpha, chunk;
+  size_t part, ratios, hist, sel, alpha, chunk, efd;
 };
 
 struct Layout {
@@ -72,6 +72,8 @@ struct Layout {
   size_t total = 0;
 };
 
+// cs_bpad: padded blocks of each CoState tensor, negative for one with error
+// feedback (which also gets a delta buffer of that many blocks).
 Layout layout_for(int nT, const std::vector<int64_t>& cs_bpad) {
   Layout L;
   size_t off = 0;
@@ -86,7 +88,8 @@ Layout layout_for(int nT, const std::vector<int64_t>& cs_bpad) {
   L.sel_bytes = al256(cs_bpad.size() * 16 * 4);
   off += L.sel_bytes;
   size_t ci = 0;
-  for (int64_t bp : cs_bpad) {
+  for (int64_t sbp : cs_bpad) {
+    const int64_t bp = sbp < 0 ? -sbp : sbp;
     CsSlot s;
     s.sel = L.sel_block + 16 * 4 * ci++;
     s.part = off;
@@ -99,6 +102,11 @@ Layout layout_for(int nT, const std::vector<int64_t>& cs_bpad) {
     off = al256(off + 4 * 4);
     s.chunk = off;
     off = al256(off + (size_t)2 * cdiv(bp / TB, FIN_THREADS) * 8);
+    s.efd = 0;
+    if (sbp < 0) {
+      s.efd = off;
+      off = al256(off + (size_t)bp * BS * 4);
+    }
     L.cs.push_back(s);
   }
   L.total = off;
@@ -110,7 +118,10 @@ bool is_costate(const ta_tensor& t) { return (t.flags & TA_M_COSTATE) != 0; }
 std::vector<int64_t> cs_bpads(const ta_tensor* ts, int n) {
   std::vector<int64_t> v;
   for (int i = 0; i < n; ++i)
-    if (ts[i].numel > 0 && is_costate(ts[i])) v.push_back(cdiv(cdiv(ts[i].numel, BS), TB) * TB);
+    if (ts[i].numel > 0 && is_costate(ts[i])) {
+      const int64_t bp = cdiv(cdiv(ts[i].numel, BS), TB) * TB;
+      v.push_back((ts[i].flags & TA_M_EF) ? -bp : bp);
+    }
   return v;
 }
 
@@ -230,6 +241,8 @@ ta_status validate(const ta_tensor& t, int i, int n_groups, const ta_group* grou
   const int64_t nb_local = cdiv(t.numel, BS);
   if (t.global_blocks && t.block_offset + nb_local > t.global_blocks)
     return bad("shard extends past global_blocks");
+  if ((t.flags & TA_M_EF) && (mk != MK_COSTATE || !t.m_ef_dev))
+    return bad("TA_M_EF needs a CoState first moment and m_ef_dev");
   if (t.flags & TA_M_SPANNING) {
     if (mk != MK_COSTATE) return bad("TA_M_SPANNING needs a CoState first moment");
     if (t.block_offset % TA_SHARD_ALIGN_BLOCKS)
@@ -239,7 +252,7 @@ ta_status validate(const ta_tensor& t, int i, int n_groups, const ta_group* grou
   }
   const void* al[] = {t.param_dev, t.grad_dev, t.v_idx_dev, t.v_hdr_dev, t.exp_avg_sq_dev,
                       t.m_labels_dev, t.m_signs_dev, t.m_norms_dev, t.m_amp_dev, t.exp_avg_dev,
-                      t.sr_uniforms_dev};
+                      t.sr_uniforms_dev, t.m_ef_dev};
   for (const void* p : al)
     if (p && !aligned16(p))
       return fail(TA_ERR_ALIGN, "tensor " + std::to_string(i) + ": pointer not 16-byte aligned");
@@ -264,6 +277,7 @@ DevTensor make_dev(const ta_tensor& t, const ta_group& g, uint64_t seed) {
   D.alpha_inj = t.alpha_inject_dev;
   D.m_out = t.m_out_dev;
   D.v_out = t.v_out_dev;
+  D.ef = t.m_ef_dev;
   D.n = t.numel;
   D.nblk = cdiv(t.numel, BS);
   D.bpad = cdiv(D.nblk, TB) * TB;
@@ -300,6 +314,8 @@ DevTensor make_dev(const ta_tensor& t, const ta_group& g, uint64_t seed) {
   if (t.dtype == TA_BF16) f |= DF_BF16;
   if (t.flags & TA_M_SPANNING) f |= DF_SPAN;
   if (t.flags & TA_EXACT_PARAM) f |= DF_EXACT_P;
+  if (t.flags & TA_M_EF) f |= DF_EF;
+  if ((t.flags & TA_M_EF) && (t.flags & TA_M_EF_STATE)) f |= DF_EF_STATE;
   D.flags = f;
   D.tid = t.tensor_id;
   D.step = t.step;
@@ -319,13 +335,22 @@ DevTensor make_dev(const ta_tensor& t, const ta_group& g, uint64_t seed) {
 // `st` before pass 1, after pass 1, after alpha, after pass 2, after labels.
 struct P1Key { int mk, vk, pt; bool uni, table; };
 
+// Error-feedback residual update of the EF tensors (after the labels).
+ta_status launch_ef(const KParams& efk, cudaStream_t st) {
+  if (!efk.total) return TA_OK;
+  const int64_t grid = std::min<int64_t>(efk.total, (int64_t)sm_count() * 8);
+  k_ef<<<(unsigned)grid, 256, 0, st>>>(efk);
+  TA_CU(cudaGetLastError());
+  return TA_OK;
+}
+
 // One phase of a sharded step (TA_PHASE_*), after the descriptors are uploaded.
 ta_status run_phase(int phase, const std::vector<std::pair<P1Key, LaunchList>>& p1,
                     const std::vector<KParams>& p1k, const KParams* p2k, const SelParams& ap,
                     int64_t achunks, const SelParams& sp, int64_t nchunks, const SelParams& xap,
                     unsigned xa_chunks, const SelParams& xsp, unsigned xsel_chunks,
-                    const SelParams& xp, unsigned nx, uint8_t* exch, size_t chunk_bytes,
-                    size_t hist_bytes, cudaStream_t st) {
+                    const SelParams& xp, unsigned nx, const KParams& efk, uint8_t* exch,
+                    size_t chunk_bytes, size_t hist_bytes, cudaStream_t st) {
   uint8_t* xh = exch + chunk_bytes;
   switch (phase) {
     case TA_PHASE_PASS1:
@@ -368,12 +393,15 @@ ta_status run_phase(int phase, const std::vector<std::pair<P1Key, LaunchList>>& 
         else k_hist<2><<<xsel_chunks, SEL_THREADS, 0, st>>>(xsp);
       }
       break;
-    case TA_PHASE_LABELS:
+    case TA_PHASE_LABELS: {
       if (nx) {
         k_pick<2><<<nx, SEL_THREADS, 0, st>>>(xp);
         k_labels<<<xsel_chunks, SEL_THREADS, 0, st>>>(xsp);
       }
+      ta_status r = launch_ef(efk, st);  // every label is final here
+      if (r != TA_OK) return r;
       break;
+    }
     default:
       return fail(TA_ERR_INVALID, "unknown phase " + std::to_string(phase));
   }
@@ -431,6 +459,7 @@ ta_status run_step(const ta_tensor* ts, int nT, const ta_group* groups, uint64_t
       H[i].sel = reinterpret_cast<uint32_t*>(ws + s.sel);
       H[i].alpha_new = reinterpret_cast<float*>(ws + s.alpha);
       H[i].chunk = reinterpret_cast<double*>(ws + s.chunk);
+      if (s.efd) H[i].efd = reinterpret_cast<float*>(ws + s.efd);
       cs_list.push_back(i);
       if (is_spanning(ts[i])) {
         H[i].xchunk = reinterpret_cast<double*>(exch) + ts[i].exch_chunk_off;
@@ -452,7 +481,8 @@ ta_status run_step(const ta_tensor* ts, int nT, const ta_group* groups, uint64_t
   LaunchList p2[2];
   p2[0].beg.push_back(0);
   p2[1].beg.push_back(0);
-  LaunchList sel, alist, xsel, xalist, xlist;  // x*: spanning tensors
+  LaunchList sel, alist, xsel, xalist, xlist, efl;  // x*: spanning tensors
+  efl.beg.push_back(0);
   sel.beg.push_back(0);
   alist.beg.push_back(0);
   xsel.beg.push_back(0);
@@ -480,6 +510,10 @@ ta_status run_step(const ta_tensor* ts, int nT, const ta_group* groups, uint64_t
       if (is_spanning(ts[i])) {
         xlist.idx.push_back(i);
         xlist.beg.push_back(xlist.beg.back() + 1);
+      }
+      if (D.flags & DF_EF) {
+        efl.idx.push_back(i);
+        efl.beg.push_back(efl.beg.back() + cdiv(D.n, TE));
       }
     }
   }
@@ -550,6 +584,13 @@ ta_status run_step(const ta_tensor* ts, int nT, const ta_group* groups, uint64_t
   put(xlist, &xp.cbeg, &xp.cidx);
   xp.ncs = (int32_t)xlist.idx.size();
   const unsigned nx = (unsigned)xlist.idx.size();
+  KParams efk;
+  put(efl, &efk.lbeg, &efk.lidx);
+  efk.T = dT;
+  efk.nl = (int32_t)efl.idx.size();
+  efk.total = efl.beg.back();
+  efk.status = status;
+  efk.skip = skip;
   const unsigned xsel_chunks = (unsigned)xsel.beg.back();
   const unsigned xa_chunks = (unsigned)xalist.beg.back();
 
@@ -577,7 +618,8 @@ ta_status run_step(const ta_tensor* ts, int nT, const ta_group* groups, uint64_t
     TA_CU(cudaGetLastError());
   }
   if (phase >= 0) return run_phase(phase, p1, p1k, p2k, ap, achunks, sp, nchunks, xap, xa_chunks,
-                                   xsp, xsel_chunks, xp, nx, exch, chunk_bytes, hist_bytes, st);
+                                   xsp, xsel_chunks, xp, nx, efk, exch, chunk_bytes, hist_bytes,
+                                   st);
   TA_CU(mark(0));
   for (size_t i = 0; i < p1.size(); ++i) {
     const P1Key& k = p1[i].first;
@@ -603,6 +645,8 @@ ta_status run_step(const ta_tensor* ts, int nT, const ta_group* groups, uint64_t
     k_select<2><<<(unsigned)nchunks, SEL_THREADS, 0, st>>>(sp);
     k_labels<<<(unsigned)nchunks, SEL_THREADS, 0, st>>>(sp);
     TA_CU(cudaGetLastError());
+    ta_status r = launch_ef(efk, st);
+    if (r != TA_OK) return r;
   } else {
     TA_CU(mark(2));
     TA_CU(mark(3));

@@ -42,6 +42,8 @@ enum : uint32_t {
   DF_SPAN = 1u << 4,  // == TA_M_SPANNING
   DF_AMP = 1u << 14,  // gradients are multiplied by ginv on load
   DF_EXACT_P = 1u << 15,  // correctly rounded parameter update (TA_EXACT_PARAM)
+  DF_EF = 1u << 16,        // CoState error feedback (TA_M_EF)
+  DF_EF_STATE = 1u << 17,  // the residual holds a value (TA_M_EF_STATE)
 };
 
 // Per-tensor descriptor, built on the host, uploaded into the workspace.
@@ -61,6 +63,8 @@ struct __align__(16) DevTensor {
   const float* alpha_inj;
   float* m_out;
   float* v_out;
+  float* ef;         // DF_EF: [n] residual
+  float* efd;        // DF_EF: [n] this step's delta (workspace)
   // workspace (CoState tensors)
   float* part;       // [2][bpad] per-block fp32 partial dots (m.g, g.g)
   float* ratios;     // [bpad]

@@ -243,6 +243,17 @@ __device__ __forceinline__ float costate_m(float g, float alpha_old, float scale
   return __fadd_rn(__fmul_rn(b1, mh), __fmul_rn(omb1, g));
 }
 
+// The same with error feedback (costate.py:410-416): m_hat decodes with the
+// gradient g, the EMA takes gm = g + residual.
+__device__ __forceinline__ float costate_m_ef(float g, float gm, float alpha_old, float scale,
+                                              uint32_t bit, bool has_state, float b1,
+                                              float omb1) {
+  const float sd = __uint_as_float(__float_as_uint(scale) ^ (bit << 31));
+  float mh = __fadd_rn(__fmul_rn(alpha_old, g), sd);
+  mh = has_state ? mh : 0.0f;
+  return __fadd_rn(__fmul_rn(b1, mh), __fmul_rn(omb1, gm));
+}
+
 // IEEE conversions between binary32 and binary16 in one instruction each;
 // identical to ta_f32_to_f16 / ta_f16_to_f32 for every non-NaN input (all
 // 2^32 and 2^16 inputs compared on sm_100a), NaNs take the portable
@@ -1064,7 +1075,12 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
           const uint32_t bit = has_state && active
                                    ? (st[L::OFF_SGN + bi * 16 + (t >> 3)] >> (7 - (t & 7))) & 1u
                                    : 0u;
-          m = costate_m(g, alpha_old, cs_scale, bit, has_state, c.b1, c.omb1);
+          if (c.flags & DF_EF_STATE) {
+            const float gm = ve ? __fadd_rn(g, D->ef[e]) : g;
+            m = costate_m_ef(g, gm, alpha_old, cs_scale, bit, has_state, c.b1, c.omb1);
+          } else {
+            m = costate_m(g, alpha_old, cs_scale, bit, has_state, c.b1, c.omb1);
+          }
           if (ve) {
             if (i & 1) {
               am1 = __fmaf_rn(m, g, am1);
@@ -1314,7 +1330,7 @@ __global__ void __launch_bounds__(NTHR, 4) k_pass1(const __grid_constant__ KPara
     const int bi = 4 * (lane >> 3) + warp;
     const bool mine_full = bi < pm.nblk && pm.n - (pm.b0 + bi) * BS >= BS;
     const bool fast =
-        __all_sync(0xffffffffu, mine_full) && !(pm.c.flags & (DF_M_OUT | DF_V_OUT));
+        __all_sync(0xffffffffu, mine_full) && !(pm.c.flags & (DF_M_OUT | DF_V_OUT | DF_EF));
     if (fast)
       p1_block<MK, VK, PT, UNI, TABLE, true>(kp.T, pm, st, table, scr, kp);
     else
@@ -1533,8 +1549,15 @@ __device__ __forceinline__ void p2_block(const DevTensor* T, const StageMeta& M,
         else g = ve ? to_f32<PT>(D->g, e0 + t) : 0.0f;
         if (flags & DF_AMP) g = amp_unscale<PT>(g, ginv);
         const uint32_t bit = (sw >> (8 * i + 7 - j)) & 1u;
-        const float m = costate_m(g, alpha_old, cs_scale, bit, has_state, b1, omb1);
+        float m;
+        if (flags & DF_EF_STATE) {
+          const float gm = ve ? __fadd_rn(g, D->ef[e0 + t]) : g;
+          m = costate_m_ef(g, gm, alpha_old, cs_scale, bit, has_state, b1, omb1);
+        } else {
+          m = costate_m(g, alpha_old, cs_scale, bit, has_state, b1, omb1);
+        }
         const float dl = ve ? __fsub_rn(m, __fmul_rn(alpha, g)) : 0.0f;  // costate.py:42
+        if (ve && (flags & DF_EF)) D->efd[e0 + t] = dl;
         const float mm = ve ? m : 0.0f;
         accd = __fadd_rn(accd, __fmul_rn(dl, dl));
         accm = __fadd_rn(accm, __fmul_rn(mm, mm));
@@ -1669,7 +1692,7 @@ __global__ void __launch_bounds__(NTHR, 6) k_pass2(const __grid_constant__ KPara
     const uint8_t* st = stages + s * L::STAGE;
     const int bi = 4 * (lane >> 3) + warp;
     const bool mine_full = bi < pm.nblk && pm.n - (pm.b0 + bi) * BS >= BS;
-    const bool fast = __all_sync(0xffffffffu, mine_full) && !(pm.c.flags & DF_M_OUT);
+    const bool fast = __all_sync(0xffffffffu, mine_full) && !(pm.c.flags & (DF_M_OUT | DF_EF));
     if (fast && (pm.c.flags & DF_AMP)) p2_block<PT, true, true>(kp.T, pm, st, wbufs + warp * 8);
     else if (fast) p2_block<PT, true, false>(kp.T, pm, st, wbufs + warp * 8);
     else p2_block_general<PT>(kp.T, pm, st);
@@ -1682,6 +1705,37 @@ template <int PT>
 constexpr size_t p2_smem_bytes() {
   return (size_t)NSTAGE2 * P2L<PT>::STAGE + 2 * NSTAGE2 * 8 + NSTAGE2 * sizeof(StageMeta) +
          NCW * 8 * sizeof(uint2);
+}
+
+// ---------------------------------------------------------------------------
+// Error-feedback residual (costate.py:428-437), after the labels are final:
+// delta_hat = decode(new encoding, alpha = 0, g) = RN(RN(0 g) + scale sign),
+// err = RN(delta - delta_hat), residual = err on the first step, else
+// RN(RN(b1 r) + RN((1 - b1) err)). One 2048-element tile per CTA iteration.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) k_ef(const __grid_constant__ KParams kp) {
+  if (step_skipped(kp.skip)) return;
+  for (int64_t tile = blockIdx.x; tile < kp.total; tile += gridDim.x) {
+    const int en = find_entry(kp.lbeg, kp.nl, tile);
+    const DevTensor& D = kp.T[kp.lidx[en]];
+    const int64_t e0 = (tile - kp.lbeg[en]) * TE;
+    const bool bf = D.flags & DF_BF16;
+    for (int t = threadIdx.x; t < TE; t += blockDim.x) {
+      const int64_t e = e0 + t;
+      if (e >= D.n) break;
+      const int64_t b = e / BS;
+      float g = bf ? to_f32<1>(D.g, e) : to_f32<0>(D.g, e);
+      if (D.flags & DF_AMP) g = bf ? amp_unscale<1>(g, D.ginv) : amp_unscale<0>(g, D.ginv);
+      const float scale = costate_scale(D.lab[b], D.nrm[b], D.amp[b], D.sqbs);
+      const uint32_t bit = (D.sgn[e >> 3] >> (7 - (e & 7))) & 1u;
+      const float dh = __fadd_rn(__fmul_rn(0.0f, g),
+                                 __uint_as_float(__float_as_uint(scale) ^ (bit << 31)));
+      const float err = __fsub_rn(D.efd[e], dh);
+      D.ef[e] = (D.flags & DF_EF_STATE)
+                    ? __fadd_rn(__fmul_rn(D.b1, D.ef[e]), __fmul_rn(D.omb1, err))
+                    : err;
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -1899,6 +1953,8 @@ __global__ void __launch_bounds__(256) k_advance(const __grid_constant__ AdvPara
     if (D.flags & DF_M_COSTATE) {  // a previous encoding exists from step 2 on
       if (s > 1) D.flags |= DF_M_HAS_STATE;
       else D.flags &= ~DF_M_HAS_STATE;
+      if ((D.flags & DF_EF) && s > 1) D.flags |= DF_EF_STATE;  // and so does the residual
+      else D.flags &= ~DF_EF_STATE;
     }
     if (a.lr != nullptr) {  // optimizer.py:106, 170 with the scalars rounded as torch does
       const double lr = a.lr[D.group];

@@ -196,7 +196,7 @@ class TurboAdam(Optimizer):
                     st["compressed_v"] = adopt_compressed_v(st["compressed_v"], p.device)
                 mgr = st.get("m_mgr")
                 if isinstance(mgr, CoStateManager):
-                    mgr.adopt(p.numel(), p.device)
+                    mgr.adopt(p.numel(), p.device, p.shape)
                 for k in ("exp_avg", "exp_avg_sq"):
                     if k in st:
                         st[k] = st[k].to(device=p.device, dtype=torch.float32).contiguous()
@@ -222,7 +222,7 @@ class TurboAdam(Optimizer):
                 mgr = CoStateManager(block_size=block_size, null_pct=group["null_pct"],
                                      amp_pct=group["amp_pct"],
                                      error_feedback=group["error_feedback"])
-                mgr.allocate(p.numel(), p.device)
+                mgr.allocate(p.numel(), p.device, p.shape)
                 state["m_mgr"] = mgr
             else:
                 state["exp_avg"] = torch.zeros_like(p, dtype=torch.float32,
@@ -297,8 +297,6 @@ class TurboAdam(Optimizer):
                         "bfloat16 parameters")
                 if group["block_size"] != 128:
                     raise NotImplementedError("block_size != 128 is not built for the device step")
-                if group["error_feedback"]:
-                    raise NotImplementedError("error_feedback=True is not built for the device step")
                 self._init_state(gi, group, p)
                 work.append((gi, p))
         if not work:
@@ -385,6 +383,9 @@ class TurboAdam(Optimizer):
                 lab, sgn, nrm, amp, alpha = mgr.pointers()
                 r["m_labels_dev"], r["m_signs_dev"], r["m_norms_dev"] = lab, sgn, nrm
                 r["m_amp_dev"], r["m_alpha_dev"] = amp, alpha
+                if mgr._error_feedback:
+                    flags |= _lib.TA_M_EF
+                    r["m_ef_dev"] = mgr.ef_pointer()
             else:
                 r["exp_avg_dev"] = st["exp_avg"].data_ptr()
             if group["compress_v"]:
@@ -446,10 +447,12 @@ class TurboAdam(Optimizer):
             st["step"] += 1  # optimizer.py:103
             grad_ptr[i] = g.data_ptr()
             steps[i] = st["step"]
-            f = int(flags[i]) & ~_lib.TA_M_HAS_STATE
+            f = int(flags[i]) & ~(_lib.TA_M_HAS_STATE | _lib.TA_M_EF_STATE)
             mgr = st.get("m_mgr")
             if mgr is not None and mgr._has_state:
                 f |= _lib.TA_M_HAS_STATE
+            if mgr is not None and mgr._ef_residual is not None:
+                f |= _lib.TA_M_EF_STATE
             flags[i] = f
             if parity is not None:
                 u = parity.get("uniforms", {}).get(p)
@@ -636,7 +639,7 @@ def _single_costate_update(mgr: CoStateManager, g: torch.Tensor, beta1: float,
     gf = gf.contiguous()
     n = gf.numel()
     if mgr._bufs is None:
-        mgr.allocate(n, dev)
+        mgr.allocate(n, dev, g.shape)
     arr = np.zeros(1, dtype=_lib.TENSOR_DTYPE)
     r = arr[0]
     r["grad_dev"] = gf.data_ptr()
@@ -644,6 +647,9 @@ def _single_costate_update(mgr: CoStateManager, g: torch.Tensor, beta1: float,
     r["dtype"] = _DTYPES[gf.dtype]
     r["flags"] = _lib.TA_M_COSTATE | _lib.TA_NO_PARAM | (
         _lib.TA_M_HAS_STATE if mgr._has_state else 0)
+    if mgr._error_feedback:
+        r["flags"] |= _lib.TA_M_EF | (_lib.TA_M_EF_STATE if mgr._ef_residual is not None else 0)
+        r["m_ef_dev"] = mgr.ef_pointer()
     r["step"] = 1
     lab, sgn, nrm, amp, alpha = mgr.pointers()
     r["m_labels_dev"], r["m_signs_dev"], r["m_norms_dev"] = lab, sgn, nrm
