@@ -164,6 +164,7 @@ struct __align__(16) StageMeta {
   int64_t boff;     // global block index of the tensor's block 0 (shards)
   int32_t t;        // tensor index
   int32_t nblk;     // blocks of this tile
+  int32_t nfull;    // leading full blocks of this tile
   float alpha_old;  // CoState alpha of the previous step (state)
   float alpha_new;  // this step's alpha (pass 2)
 };
@@ -1249,6 +1250,7 @@ __device__ __forceinline__ void fill_meta_common(StageMeta& m, const DevTensor& 
   m.boff = D.boff;
   m.t = t;
   m.nblk = nblk;
+  m.nfull = (int32_t)min((int64_t)nblk, (D.n - b0 * BS) / BS);
   m.alpha_old = aold;
 }
 
@@ -1325,12 +1327,9 @@ __global__ void __launch_bounds__(NTHR, 4) k_pass1(const __grid_constant__ KPara
     if (!wait_bar(&full[s], ph, kp.status)) break;
     const StageMeta& pm = meta[s];
     const uint8_t* st = stages + s * L::STAGE;
-    // the fast path needs all 4 blocks of this warp present and full, and no
-    // seam outputs; decided per warp so the shuffles stay convergent
-    const int bi = 4 * (lane >> 3) + warp;
-    const bool mine_full = bi < pm.nblk && pm.n - (pm.b0 + bi) * BS >= BS;
-    const bool fast =
-        __all_sync(0xffffffffu, mine_full) && !(pm.c.flags & (DF_M_OUT | DF_V_OUT | DF_EF));
+    // the fast path needs all 4 blocks of this warp (w, w + 4, w + 8, w + 12)
+    // full, and no seam outputs; uniform per warp, so the shuffles stay convergent
+    const bool fast = pm.nfull >= 13 + warp && !(pm.c.flags & (DF_M_OUT | DF_V_OUT | DF_EF));
     if (fast)
       p1_block<MK, VK, PT, UNI, TABLE, true>(kp.T, pm, st, table, scr, kp);
     else
@@ -1500,7 +1499,14 @@ __device__ __forceinline__ void p2_block(const DevTensor* T, const StageMeta& M,
     const uint8_t lab = st[L::OFF_LAB + bi];
     const float nrm = reinterpret_cast<const float*>(st + L::OFF_NRM)[bi];
     const uint16_t amp = reinterpret_cast<const uint16_t*>(st + L::OFF_AMP)[bi];
-    cs_scale = costate_scale(lab, nrm, amp, sqbs);
+    if (FULL) {  // as in pass 1: Markstein for norms in [2^-100, 2^100], 0, non-finite
+      const float ph = (nrm > 0.0f && nrm < 0x1p-100f) || nrm > 0x1p100f
+                           ? __fdiv_rn(nrm, sqbs)
+                           : div_by(nrm, sqbs, M.c.rsqbs);
+      cs_scale = lab == 1 ? ph : (lab == 2 ? f16_to_f32_dev(amp) : 0.0f);
+    } else {
+      cs_scale = costate_scale(lab, nrm, amp, sqbs);
+    }
   }
   float accd = 0.0f, accm = 0.0f;
   uint32_t myw = 0;
@@ -1594,8 +1600,14 @@ __device__ __forceinline__ void p2_block(const DevTensor* T, const StageMeta& M,
     reinterpret_cast<uint16_t*>(M.sgn + b * 16)[j] = (uint16_t)(by0 | (by1 << 8));
     if (j == 0) {
       M.nrm[b] = dn;
-      M.amp[b] = f32_to_f16_dev(__fdiv_rn(dn, sqbs));
-      M.ratios[b] = (mnorm == 0.0f) ? 0.0f : __fdiv_rn(dn, mnorm);
+      if (FULL && dn >= 0x1p-60f && dn <= 0x1p60f && mnorm >= 0x1p-60f && mnorm <= 0x1p60f) {
+        // Markstein quotients (y = RN(1/b): exact for these ranges); dn finite
+        M.amp[b] = f2h_fin(div_by(dn, sqbs, M.c.rsqbs));
+        M.ratios[b] = div_by(dn, mnorm, rcp_exact(mnorm));
+      } else {
+        M.amp[b] = f32_to_f16_dev(__fdiv_rn(dn, sqbs));
+        M.ratios[b] = (mnorm == 0.0f) ? 0.0f : __fdiv_rn(dn, mnorm);
+      }
     }
   }
 }
@@ -1690,9 +1702,7 @@ __global__ void __launch_bounds__(NTHR, 6) k_pass2(const __grid_constant__ KPara
     if (!wait_bar(&full[s], ph, kp.status)) break;
     const StageMeta& pm = meta[s];
     const uint8_t* st = stages + s * L::STAGE;
-    const int bi = 4 * (lane >> 3) + warp;
-    const bool mine_full = bi < pm.nblk && pm.n - (pm.b0 + bi) * BS >= BS;
-    const bool fast = __all_sync(0xffffffffu, mine_full) && !(pm.c.flags & (DF_M_OUT | DF_EF));
+    const bool fast = pm.nfull >= 13 + warp && !(pm.c.flags & (DF_M_OUT | DF_EF));
     if (fast && (pm.c.flags & DF_AMP)) p2_block<PT, true, true>(kp.T, pm, st, wbufs + warp * 8);
     else if (fast) p2_block<PT, true, false>(kp.T, pm, st, wbufs + warp * 8);
     else p2_block_general<PT>(kp.T, pm, st);
