@@ -58,10 +58,12 @@ enum {
   TA_EXACT_PARAM = 1u << 5  /* parameter update with correctly rounded v / bc2,
                                sqrt and division: bit-identical to the
                                reference's op sequence (optimizer.py:163-170).
-                               Without it those three ops use the hardware
-                               estimates plus one correction each (within about
-                               one ulp per op); no state depends on them, so
-                               every packed state bit is the same either way  */
+                               Without it they use the hardware estimates
+                               (rsqrt, and rcp with one correction of the
+                               quotient): the update is within about 3e-7
+                               relative of the reference's; no state depends
+                               on it, so every packed state bit is the same
+                               either way                                      */
 };
 
 /* ta_step_phase phases (in call order; the caller all-reduces (sum) the
@@ -346,9 +348,13 @@ TA_API size_t ta_aux_workspace_size(int64_t n);
  *   out_dev[1] = number of adjacent normal pairs x < x' with
  *                ta_logf(x') < ta_logf(x) (the step assumes 0),
  *   out_dev[2] = number of x with a normal 1/x where rcp.approx plus one
- *                Newton step differs from RN(1/x) (the default parameter
- *                update assumes 0).
- * out_dev: 3 uint64 in device memory, zeroed by the caller.
+ *                Newton step differs from RN(1/x) (the fast reciprocals of
+ *                the step assume 0),
+ *   out_dev[3] = bits of the double max relative error of rsqrt.approx(x),
+ *   out_dev[4] = bits of the double max relative error of rcp.approx(x) over
+ *                x with a normal 1/x (the default parameter update assumes
+ *                both <= 2^-22).
+ * out_dev: 5 uint64 in device memory, zeroed by the caller.
  */
 TA_API ta_status ta_selftest_fast_math(uint64_t* out_dev, void* stream);
 

@@ -18,7 +18,7 @@ def test_fast_math_properties_exhaustive():
     from turboadam_b200 import _lib
 
     lib = _lib.load()
-    out = torch.zeros(3, dtype=torch.int64, device="cuda")
+    out = torch.zeros(5, dtype=torch.int64, device="cuda")
     _lib.check(lib.ta_selftest_fast_math(out.data_ptr(), torch.cuda.current_stream().cuda_stream),
                "ta_selftest_fast_math")
     torch.cuda.synchronize()
@@ -27,6 +27,9 @@ def test_fast_math_properties_exhaustive():
     assert int(words[1]) == 0, "ta_logf is not monotone on the normal floats"
     assert 0.0 < max_err <= 2.0 ** -16, f"lg2.approx error {max_err} (2^{math.log2(max_err):.2f})"
     assert int(words[2]) == 0, "rcp.approx + one Newton step is not RN(1/x) everywhere"
+    rs, rc = (float(x) for x in words[3:5].view(np.float64))
+    assert 0.0 < rs <= 2.0 ** -22, f"rsqrt.approx relative error 2^{math.log2(rs):.2f}"
+    assert 0.0 < rc <= 2.0 ** -22, f"rcp.approx relative error 2^{math.log2(rc):.2f}"
 
 
 @pytest.mark.parametrize("v_bits", [2, 4, 8])

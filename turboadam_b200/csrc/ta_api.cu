@@ -1013,7 +1013,7 @@ ta_status noalloc_scratch(cudaStream_t st, void** out) {
   return TA_OK;
 }
 __global__ void __launch_bounds__(256) k_selftest_fast_math(unsigned long long* out) {
-  unsigned long long me = 0, nm = 0, nr = 0;
+  unsigned long long me = 0, nm = 0, nr = 0, ers = 0, erc = 0;
   const uint64_t lo = 0x00800000u, hi = 0x7f800000u;  // the normal binary32 numbers
   for (uint64_t u = lo + blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; u < hi;
        u += (uint64_t)gridDim.x * blockDim.x) {
@@ -1030,11 +1030,19 @@ __global__ void __launch_bounds__(256) k_selftest_fast_math(unsigned long long* 
       const float y0 = rcp_approx(x);
       const float y = __fmaf_rn(__fmaf_rn(-x, y0, 1.0f), y0, y0);
       if (__float_as_uint(y) != __float_as_uint(__frcp_rn(x))) ++nr;
+      const double rc = fabs((double)y0 * (double)x - 1.0);  // relative error of the estimate
+      const unsigned long long rcb = (unsigned long long)__double_as_longlong(rc);
+      erc = rcb > erc ? rcb : erc;
     }
+    const double rs = fabs((double)rsqrt_approx(x) * sqrt((double)x) - 1.0);
+    const unsigned long long rsb = (unsigned long long)__double_as_longlong(rs);
+    ers = rsb > ers ? rsb : ers;
   }
   atomicMax(&out[0], me);
   atomicAdd(&out[1], nm);
   atomicAdd(&out[2], nr);
+  atomicMax(&out[3], ers);
+  atomicMax(&out[4], erc);
 }
 
 }  // namespace

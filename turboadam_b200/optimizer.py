@@ -71,10 +71,11 @@ class TurboAdam(Optimizer):
     leaves every packed bit equal to the unsharded step's.
     ``exact_params=True`` computes the parameter update's v / bc2, square root
     and division correctly rounded, so parameters equal the reference's op
-    sequence bit for bit; by default those three ops use the hardware
-    estimates with one correction each (about one ulp per op: parameters
-    agree to a few ulp of the update, far inside 1e-6 relative). No state
-    depends on the parameters: every packed state bit is the same either way.
+    sequence bit for bit; by default they use the hardware rsqrt / rcp
+    estimates (one correction of the quotient): the update is within about
+    3e-7 relative of the reference's, inside the 1e-6 parameter tolerance.
+    No state depends on the parameters: every packed state bit is the same
+    either way.
     """
 
     # torch.amp.GradScaler hands over `grad_scale` / `found_inf` instead of
