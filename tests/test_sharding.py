@@ -283,3 +283,55 @@ def test_zero1_phased_step_matches_unsharded(world):
                 assert torch.equal(ea["sign_packed"], eb["sign_packed"][e0 // 8:(e1 + 7) // 8]), tag
                 assert torch.equal(ea["block_norms"].view(torch.int32),
                                    eb["block_norms"][B0:B1].view(torch.int32)), tag
+
+
+def _gather_rank(rank, world, port, flat, q):
+    import sys
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.abspath(__file__)), ".."))
+    from turboadam_b200.sharding import Zero1ParamGather
+
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        shapes = [(1000, 300), (777,), (4100, 256), (96, 70)]
+        numels = [int(np.prod(s)) for s in shapes]
+        if flat:
+            buf = torch.zeros(sum(numels))
+            params, off = [], 0
+            for s, n in zip(shapes, numels):
+                params.append(buf[off:off + n].view(s))
+                off += n
+        else:
+            params = [torch.zeros(s) for s in shapes]
+        zg = Zero1ParamGather(params, block_size=128)
+        assert (zg._flat is not None) == flat
+        shard_params, kw = zg.optimizer_args()
+        # a stand-in for the step: each rank writes its own marks into its shards
+        for sp, (t, e0, e1, _, _) in zip(shard_params, zg.partition[rank]):
+            sp.data.copy_(torch.arange(e0, e1, dtype=torch.float32) + 1e6 * (t + 1))
+        zg.gather()
+        ok = all(torch.equal(p.view(-1), torch.arange(n, dtype=torch.float32) + 1e6 * (t + 1))
+                 for t, (p, n) in enumerate(zip(params, numels)))
+        q.put((rank, ok, len(kw["spanning"])))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("flat", [True, False])
+@pytest.mark.parametrize("world", [2, 3])
+def test_zero1_param_gather_gloo(world, flat):
+    """Post-step all-gather of ZeRO-1 ranges (flat buffer: one broadcast per
+    rank; separate tensors: one per shard) leaves every rank with every
+    rank's updates."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_gather_rank, args=(r, world, port, flat, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+    assert all(ok for _, ok, _ in res), res

@@ -1,7 +1,9 @@
 """ZeRO-1 over real NCCL: world-2 ranks on two GPUs step their shards with
 TurboAdam(shards=..., spanning=...) (alpha chunk sums and threshold
 histograms all-reduced between the phases) and compare every shard bit for
-bit with an unsharded step computed on the same GPU. Skipped with fewer
+bit with an unsharded step computed on the same GPU; then, with full
+parameter replicas, step the shard views and gather after every step
+(Zero1ParamGather), and compare every full parameter. Skipped with fewer
 than two GPUs."""
 import datetime
 import os
@@ -87,6 +89,22 @@ def _rank_body(rank, world, port, out):
                     bad.append(f"rank {rank} tensor {t} labels")
                 if not torch.equal(ea["sign_packed"], eb["sign_packed"][e0 // 8:(e1 + 7) // 8]):
                     bad.append(f"rank {rank} tensor {t} signs")
+        # ZeRO-1 with full replicas: step the shard views, gather after each step
+        from turboadam_b200.sharding import Zero1ParamGather
+
+        rep = [torch.nn.Parameter(x.clone().to(dev)) for x in init]
+        zg = Zero1ParamGather(rep)
+        sps, zkw = zg.optimizer_args()
+        zopt = TurboAdam(sps, **zkw, **kw)
+        for s in range(3):
+            for (t, e0, e1, _, _), p in zip(zg.partition[rank], sps):
+                p.grad = grads[s][t][e0:e1].to(dev)
+            zopt.step()
+            zg.gather()
+        torch.cuda.synchronize()
+        for t, (p, ref) in enumerate(zip(rep, full)):
+            if not torch.equal(p.data.view(-1).view(torch.int32), ref.data.view(-1).view(torch.int32)):
+                bad.append(f"rank {rank} tensor {t} gathered params")
         out.put((rank, bad))
         dist.barrier()
     finally:

@@ -101,3 +101,103 @@ def zero1_spanning(partition):
             count[t] = count.get(t, 0) + 1
             numel[t] = gn
     return [(t, numel[t]) for t in sorted(count) if count[t] > 1]
+
+
+class Zero1ParamGather:
+    """ZeRO-1 around TurboAdam: every rank holds the full parameters, steps
+    the ``zero1_partition`` range it owns, and gathers the others' updated
+    ranges after the step (the post-step parameter all-gather).
+
+    ``params`` is the full parameter list, identically ordered and shaped on
+    every rank. :meth:`optimizer_args` gives this rank's shard parameters --
+    views into the full tensors, so the step updates them in place -- with
+    the ``tensor_ids`` / ``shards`` / ``spanning`` arguments of TurboAdam.
+    :meth:`gather` then broadcasts each rank's updated ranges to all ranks
+    (``torch.distributed``; NCCL on GPUs, gloo on CPU). When the parameters
+    are consecutive views of one flat buffer (the usual ZeRO layout) each
+    rank's range is one contiguous span and the gather is one broadcast per
+    rank; otherwise one broadcast per shard. Each rank receives the
+    (world - 1) / world of the parameter bytes it does not own -- the
+    NVLink-bound part of ZeRO-1, which no fusion with the step reduces.
+    The step needs every shard to start 16-byte aligned: in a flat buffer,
+    pad each tensor to a multiple of 4 (fp32) or 8 (bf16) elements.
+    """
+
+    def __init__(self, params, world: int | None = None, rank: int | None = None,
+                 process_group=None, block_size: int = 128):
+        import torch.distributed as dist
+
+        self.params = list(params)
+        self.group = process_group
+        self.world = dist.get_world_size(process_group) if world is None else int(world)
+        self.rank = dist.get_rank(process_group) if rank is None else int(rank)
+        numels = [p.numel() for p in self.params]
+        self.partition = zero1_partition(numels, self.world, block_size)
+        self.spanning = zero1_spanning(self.partition)
+        self._flat = self._flat_spans(numels)
+
+    def _flat_spans(self, numels):
+        """(base tensor, [(lo, hi)] per rank) when the parameters are
+        consecutive slices of one contiguous storage, else None."""
+        ps = self.params
+        if not ps or any(not p.is_contiguous() for p in ps):
+            return None
+        esz = ps[0].element_size()
+        if any(p.dtype != ps[0].dtype or p.device != ps[0].device for p in ps):
+            return None
+        for a, b in zip(ps, ps[1:]):
+            if b.data_ptr() != a.data_ptr() + a.numel() * esz:
+                return None
+        starts = [0]
+        for n in numels:
+            starts.append(starts[-1] + n)
+        base = ps[0].detach().view(-1)
+        base = base.as_strided((starts[-1],), (1,), base.storage_offset())
+        spans = []
+        for shards in self.partition:
+            if not shards:
+                spans.append((0, 0))
+                continue
+            t0, e0 = shards[0][0], shards[0][1]
+            t1, e1 = shards[-1][0], shards[-1][2]
+            spans.append((starts[t0] + e0, starts[t1] + e1))
+        return base, spans
+
+    def optimizer_args(self):
+        """(shard params, kwargs for TurboAdam) of this rank."""
+        import torch
+
+        mine = self.partition[self.rank]
+        shard_params = [torch.nn.Parameter(self.params[t].detach().view(-1)[e0:e1])
+                        for t, e0, e1, _, _ in mine]
+        kw = dict(tensor_ids=[t for t, *_ in mine],
+                  shards=[(boff, gn) for _, _, _, boff, gn in mine],
+                  spanning=self.spanning, process_group=self.group)
+        return shard_params, kw
+
+    def gather(self) -> None:
+        """Broadcast every rank's updated ranges to all ranks."""
+        import torch.distributed as dist
+
+        work = []
+        if self._flat is not None:
+            base, spans = self._flat
+            for r, (lo, hi) in enumerate(spans):
+                if hi > lo:
+                    work.append(dist.broadcast(base[lo:hi], src=self._global_rank(r),
+                                               group=self.group, async_op=True))
+        else:
+            for r, shards in enumerate(self.partition):
+                for t, e0, e1, _, _ in shards:
+                    work.append(dist.broadcast(self.params[t].detach().view(-1)[e0:e1],
+                                               src=self._global_rank(r), group=self.group,
+                                               async_op=True))
+        for w in work:
+            w.wait()
+
+    def _global_rank(self, r: int) -> int:
+        import torch.distributed as dist
+
+        if self.group is None:
+            return r
+        return dist.get_global_rank(self.group, r)
