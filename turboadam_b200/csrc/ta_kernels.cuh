@@ -1367,11 +1367,24 @@ __device__ __forceinline__ void alpha_chunk_sum(const DevTensor& D, int64_t c, d
   const int64_t t = c * FIN_THREADS + tid;
   double tm = 0.0, tg = 0.0;
   if (t < ntile) {
-    const int64_t bend = min(D.nblk, (t + 1) * TB);
-    for (int64_t b = t * TB; b < bend; ++b) {
-      tm += (double)D.part[b];
-      tg += (double)D.part[D.bpad + b];
+    // the tile's 16 partials of each dot as 4 16-byte loads (the arrays are
+    // padded to whole tiles), summed in block order
+    const int nb = (int)min((int64_t)TB, D.nblk - t * TB);
+    const float4* pm = reinterpret_cast<const float4*>(D.part + t * TB);
+    const float4* pg = reinterpret_cast<const float4*>(D.part + D.bpad + t * TB);
+    float am[TB], ag[TB];
+#pragma unroll
+    for (int q = 0; q < TB / 4; ++q) {
+      const float4 a = __ldcg(pm + q), g = __ldcg(pg + q);
+      am[4 * q] = a.x; am[4 * q + 1] = a.y; am[4 * q + 2] = a.z; am[4 * q + 3] = a.w;
+      ag[4 * q] = g.x; ag[4 * q + 1] = g.y; ag[4 * q + 2] = g.z; ag[4 * q + 3] = g.w;
     }
+#pragma unroll
+    for (int i = 0; i < TB; ++i)
+      if (i < nb) {
+        tm += (double)am[i];
+        tg += (double)ag[i];
+      }
   }
 #pragma unroll
   for (int off = 16; off >= 1; off >>= 1) {
