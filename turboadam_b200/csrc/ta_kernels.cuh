@@ -833,7 +833,9 @@ __device__ __noinline__ uint32_t p1_requant_quad_retry(
 // general path: per-element bounds, global loads for the ragged tail block,
 // IEEE divisions and exact special cases everywhere. ln v_new goes through a
 // per-lane smem scratch between the v update and the re-quantisation.
-template <int MK, int VK, int PT, bool UNI, bool TABLE, bool FULL>
+// EX (fast path only): TA_EXACT_PARAM as a compile-time value, so the default
+// update's hot loop carries no code of the correctly rounded one.
+template <int MK, int VK, int PT, bool UNI, bool TABLE, bool FULL, bool EX = false>
 __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
                                          const uint8_t* st, float* table, float* scr,
                                          const KParams& kp) {
@@ -1019,7 +1021,7 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
         float2 x01 = P.mul(v01, dup2(c.rbc2)), x23 = P.mul(v23, dup2(c.rbc2));
         nanacc = fma2(x01, zero2, fma2(x23, zero2, nanacc));  // v or v / bc2 not finite
         float2 p01, p23;
-        if (c.flags & DF_EXACT_P) {
+        if (EX) {
           // v / bc2 by Markstein with y = RN(1/bc2): exact for v in the unflagged range
           x01 = fma2(fma2(x01, dup2(-c.bc2), v01), dup2(c.rbc2), x01);
           x23 = fma2(fma2(x23, dup2(-c.bc2), v23), dup2(c.rbc2), x23);
@@ -1327,8 +1329,10 @@ __global__ void __launch_bounds__(NTHR, 4) k_pass1(const __grid_constant__ KPara
     // the fast path needs all 4 blocks of this warp (w, w + 4, w + 8, w + 12)
     // full, and no seam outputs; uniform per warp, so the shuffles stay convergent
     const bool fast = pm.nfull >= 13 + warp && !(pm.c.flags & (DF_M_OUT | DF_V_OUT | DF_EF));
-    if (fast)
-      p1_block<MK, VK, PT, UNI, TABLE, true>(kp.T, pm, st, table, scr, kp);
+    if (fast && (pm.c.flags & DF_EXACT_P))
+      p1_block<MK, VK, PT, UNI, TABLE, true, true>(kp.T, pm, st, table, scr, kp);
+    else if (fast)
+      p1_block<MK, VK, PT, UNI, TABLE, true, false>(kp.T, pm, st, table, scr, kp);
     else
       p1_block_general<MK, VK, PT, UNI, TABLE>(kp.T, pm, st, table, scr, kp);
     __syncwarp();
@@ -1480,7 +1484,9 @@ __global__ void __launch_bounds__(FIN_THREADS) k_alpha_fin(const __grid_constant
 // ---------------------------------------------------------------------------
 // Pass 2: CoState encode (costate.py:419-425, :51-86, :213-258)
 // ---------------------------------------------------------------------------
-template <int PT, bool FULL, bool AMP = false>
+// HS (fast path only): the tensor holds a previous encoding (has_state as a
+// compile-time value, so the m_hat select of the first step is not paid later).
+template <int PT, bool FULL, bool AMP = false, bool HS = true>
 __device__ __forceinline__ void p2_block(const DevTensor* T, const StageMeta& M,
                                          const uint8_t* st, uint2* wb) {
   using L = P2L<PT>;
@@ -1501,7 +1507,7 @@ __device__ __forceinline__ void p2_block(const DevTensor* T, const StageMeta& M,
   const uint32_t* sgnw = reinterpret_cast<const uint32_t*>(st + L::OFF_SGN + bi * 16);
   const DevTensor* D = FULL ? nullptr : &T[M.t];  // tail loads and seam outputs only
 
-  const bool has_state = flags & DF_M_HAS_STATE;
+  const bool has_state = FULL ? HS : (flags & DF_M_HAS_STATE) != 0;
   float cs_scale = 0.0f;
   const float alpha_old = M.alpha_old;
   const float alpha = M.alpha_new;
@@ -1713,8 +1719,15 @@ __global__ void __launch_bounds__(NTHR, 6) k_pass2(const __grid_constant__ KPara
     const StageMeta& pm = meta[s];
     const uint8_t* st = stages + s * L::STAGE;
     const bool fast = pm.nfull >= 13 + warp && !(pm.c.flags & (DF_M_OUT | DF_EF));
-    if (fast && (pm.c.flags & DF_AMP)) p2_block<PT, true, true>(kp.T, pm, st, wbufs + warp * 8);
-    else if (fast) p2_block<PT, true, false>(kp.T, pm, st, wbufs + warp * 8);
+    const bool hs = pm.c.flags & DF_M_HAS_STATE;
+    uint2* wb = wbufs + warp * 8;
+    if (fast && (pm.c.flags & DF_AMP)) {
+      if (hs) p2_block<PT, true, true, true>(kp.T, pm, st, wb);
+      else p2_block<PT, true, true, false>(kp.T, pm, st, wb);
+    } else if (fast) {
+      if (hs) p2_block<PT, true, false, true>(kp.T, pm, st, wb);
+      else p2_block<PT, true, false, false>(kp.T, pm, st, wb);
+    }
     else p2_block_general<PT>(kp.T, pm, st);
     __syncwarp();
     if (lane == 0) mbar_arrive(&done[s]);
