@@ -989,11 +989,18 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
           vo[1] = tab[(w >> 8) & (uint32_t)(nb - 1)];
           vo[2] = tab[(w >> 16) & (uint32_t)(nb - 1)];
           vo[3] = tab[(w >> 24) & (uint32_t)(nb - 1)];
-        } else {
+        } else {  // no table (8 bits): paired branch-free ta_expf (non-finite headers are flagged)
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float qv = __fmul_rn(__fadd_rn((float)((w >> (8 * i)) & 0xffu), 0.5f), c.rnbf);
-            vo[i] = ta_expf(__fadd_rn(lmin, __fmul_rn(qv, span)));
+          for (int i = 0; i < 4; i += 2) {
+            const float2 qv = P.mul(P.add(make_float2((float)((w >> (8 * i)) & 0xffu),
+                                                      (float)((w >> (8 * i + 8)) & 0xffu)),
+                                          dup2(0.5f)),
+                                    dup2(c.rnbf));
+            float2 x = P.add(dup2(lmin), P.mul(qv, dup2(span)));
+            x = make_float2(fminf(fmaxf(x.x, -110.0f), 100.0f), fminf(fmaxf(x.y, -110.0f), 100.0f));
+            const float2 e = expf2_core(x, P);
+            vo[i] = e.x;
+            vo[i + 1] = e.y;
           }
         }
         // quantize.py:270: v = b2 * v_old + (1 - b2) * g^2
