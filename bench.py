@@ -92,10 +92,25 @@ CONFIGS = {
                        grad_std=1e-3, dtype="fp32"),
     "gpt2-124m": dict(shapes=gpt2_124m_shapes, kw=dict(lr=6e-4, weight_decay=0.01, v_bits=4),
                       grad_std=1e-3, dtype="fp32"),
+    # Student-t (nu = 3) gradients scaled by 1e-3
     "flat-vonly": dict(shapes=lambda: [("flat", (2 ** 30 + 37,))],
                        kw=dict(lr=1e-3, compress_m=False, v_bits=4), grad_std=1e-3,
-                       dtype="fp32"),
+                       dtype="fp32", grad_dist="student_t3"),
 }
+
+
+def student_t3_(out, scale, gen, chunk=1 << 26):
+    """out <- scale * Z / sqrt(chi2_3 / 3) (Student-t, 3 degrees of freedom),
+    generated on the device in chunks."""
+    import torch
+
+    flat = out.view(-1)
+    for lo in range(0, flat.numel(), chunk):
+        n = min(chunk, flat.numel() - lo)
+        z = torch.randn(4, n, device=out.device, generator=gen)
+        chi = (z[1] * z[1] + z[2] * z[2] + z[3] * z[3]) / 3.0
+        flat[lo:lo + n].copy_(z[0] / chi.sqrt() * scale)
+    return out
 
 
 def numel(shape):
@@ -356,7 +371,10 @@ def run_ours(args, rank, world, local_rank):
         p = torch.empty(shp, dtype=pdtype, device=dev)
         p.normal_(0.0, 0.02, generator=gen)
         p = torch.nn.Parameter(p)
-        p.grad = torch.empty_like(p).normal_(0.0, cfg["grad_std"], generator=gen)
+        if cfg.get("grad_dist") == "student_t3":
+            p.grad = student_t3_(torch.empty_like(p), cfg["grad_std"], gen)
+        else:
+            p.grad = torch.empty_like(p).normal_(0.0, cfg["grad_std"], generator=gen)
         params.append(p)
     opt = TurboAdam(params, betas=(0.9, 0.999), seed=2024, tensor_ids=[t for _, t, _ in local],
                     shards=[sh for _, _, sh in local] if part == "zero1" else None,
@@ -504,8 +522,10 @@ def run_ours(args, rank, world, local_rank):
         "scaling": "strong" if world > 1 else "strong",
         "vs_baseline": None,
         "dtype": "bf16" if psize == 2 else "f32",
-        "data": "synthetic: random-init params N(0,0.02), seeded N(0,%g) grads generated on "
-                "device once and reused each step" % cfg["grad_std"],
+        "data": ("synthetic: random-init params N(0,0.02), seeded %s grads generated on "
+                 "device once and reused each step"
+                 % ("Student-t(3) x %g" % cfg["grad_std"] if cfg.get("grad_dist") == "student_t3"
+                    else "N(0,%g)" % cfg["grad_std"])),
         "config": {"workload": args.config, "params": total_params, "tensors": len(shapes),
                    "v_bits": kw["v_bits"], "costate": kw.get("compress_m", True),
                    "parallelism": (f"ZeRO-1 flat partition over {world} GPU(s); tensors split "
