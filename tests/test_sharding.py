@@ -212,12 +212,13 @@ ZSHAPES = [(5000, 300), (777,), (4100, 256), (96, 70), (3000, 700)]
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("ef", [False, True])
 @pytest.mark.parametrize("world", [2, 3, 5])
-def test_zero1_phased_step_matches_unsharded(world):
+def test_zero1_phased_step_matches_unsharded(world, ef):
     """ZeRO-1 shards stepped through the phased C ABI, ranks emulated in one
     process (their exchange regions summed between phases, what the NCCL
-    all-reduce does across GPUs): every parameter and packed-state bit equals
-    the unsharded step's."""
+    all-reduce does across GPUs): every parameter and packed-state bit --
+    with error feedback, every residual bit -- equals the unsharded step's."""
     from turboadam_b200 import TurboAdam
     from turboadam_b200.sharding import zero1_partition, zero1_spanning
 
@@ -226,7 +227,7 @@ def test_zero1_phased_step_matches_unsharded(world):
             for i, n in enumerate(numels)]
     grads = [[torch.randn(n, generator=torch.Generator().manual_seed(1000 * s + i)) * 1e-3
               for i, n in enumerate(numels)] for s in range(3)]
-    kw = dict(lr=6e-4, weight_decay=0.01, v_bits=4, seed=9)
+    kw = dict(lr=6e-4, weight_decay=0.01, v_bits=4, seed=9, error_feedback=ef)
 
     full = [torch.nn.Parameter(x.clone().cuda()) for x in init]
     ofull = TurboAdam(full, **kw)
@@ -283,6 +284,10 @@ def test_zero1_phased_step_matches_unsharded(world):
                 assert torch.equal(ea["sign_packed"], eb["sign_packed"][e0 // 8:(e1 + 7) // 8]), tag
                 assert torch.equal(ea["block_norms"].view(torch.int32),
                                    eb["block_norms"][B0:B1].view(torch.int32)), tag
+                if ef:
+                    ra, rb = a["m_mgr"]._ef_residual, b["m_mgr"]._ef_residual
+                    assert torch.equal(ra.reshape(-1).view(torch.int32),
+                                       rb.reshape(-1)[e0:e1].view(torch.int32)), tag
 
 
 def _gather_rank(rank, world, port, flat, q):
