@@ -20,7 +20,7 @@ constexpr int NSTAGE2 = 4;          // pass-2 depth (small stages, little comput
 constexpr uint32_t WAIT_LIMIT = 1u << 27;  // bounded mbarrier polling
 
 constexpr int FIN_THREADS = 256;    // alpha chunk CTA (tiles per chunk)
-constexpr int SEL_CHUNK = 4096;     // ratios per radix-select CTA
+constexpr int SEL_CHUNK = 16384;    // ratios per radix-select CTA (amortises the histogram clear / flush)
 constexpr int SEL_THREADS = 256;
 constexpr int HBINS = 2048;
 
