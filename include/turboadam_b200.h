@@ -353,8 +353,13 @@ TA_API size_t ta_aux_workspace_size(int64_t n);
  *   out_dev[3] = bits of the double max relative error of rsqrt.approx(x),
  *   out_dev[4] = bits of the double max relative error of rcp.approx(x) over
  *                x with a normal 1/x (the default parameter update assumes
- *                both <= 2^-22).
- * out_dev: 5 uint64 in device memory, zeroed by the caller.
+ *                both <= 2^-22),
+ *   out_dev[5] = number of non-NaN binary32 x (either sign, zeros,
+ *                subnormals and infinities included) whose hardware
+ *                bfloat16 rounding (cvt.rn.bf16x2.f32, used by the bf16
+ *                parameter stores) differs from the portable
+ *                round-to-nearest-even (the step assumes 0).
+ * out_dev: 6 uint64 in device memory, zeroed by the caller.
  */
 TA_API ta_status ta_selftest_fast_math(uint64_t* out_dev, void* stream);
 

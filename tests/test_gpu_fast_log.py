@@ -2,8 +2,10 @@
 certified re-quantisation (exact indices from an approximate log plus a
 per-quad error test) needs the hardware lg2 estimate within its assumed bound
 and the checker's log monotone; the default parameter update uses a
-reciprocal that is correctly rounded after one Newton step. All three are
-checked over every normal binary32 input.
+reciprocal that is correctly rounded after one Newton step; bf16 parameters
+are rounded by the hardware pair conversion, which must equal the portable
+round-to-nearest-even. All are checked over every normal binary32 input (the
+bf16 rounding over every non-NaN one).
 """
 import math
 
@@ -18,7 +20,7 @@ def test_fast_math_properties_exhaustive():
     from turboadam_b200 import _lib
 
     lib = _lib.load()
-    out = torch.zeros(5, dtype=torch.int64, device="cuda")
+    out = torch.zeros(6, dtype=torch.int64, device="cuda")
     _lib.check(lib.ta_selftest_fast_math(out.data_ptr(), torch.cuda.current_stream().cuda_stream),
                "ta_selftest_fast_math")
     torch.cuda.synchronize()
@@ -30,6 +32,7 @@ def test_fast_math_properties_exhaustive():
     rs, rc = (float(x) for x in words[3:5].view(np.float64))
     assert 0.0 < rs <= 2.0 ** -22, f"rsqrt.approx relative error 2^{math.log2(rs):.2f}"
     assert 0.0 < rc <= 2.0 ** -22, f"rcp.approx relative error 2^{math.log2(rc):.2f}"
+    assert int(words[5]) == 0, "cvt.rn.bf16x2.f32 differs from the portable bf16 rounding"
 
 
 @pytest.mark.parametrize("v_bits", [2, 4, 8])

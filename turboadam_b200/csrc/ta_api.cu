@@ -1012,8 +1012,13 @@ ta_status noalloc_scratch(cudaStream_t st, void** out) {
   *out = g_noalloc_ptr[dev];
   return TA_OK;
 }
+// 1 when the hardware pair rounding of (x, -x) differs from the portable one.
+__device__ __forceinline__ unsigned long long bf16_mismatch(float x) {
+  const uint32_t sw = (uint32_t)ta_f32_to_bf16(x) | ((uint32_t)ta_f32_to_bf16(-x) << 16);
+  return bf16x2_rn(x, -x) != sw;
+}
 __global__ void __launch_bounds__(256) k_selftest_fast_math(unsigned long long* out) {
-  unsigned long long me = 0, nm = 0, nr = 0, ers = 0, erc = 0;
+  unsigned long long me = 0, nm = 0, nr = 0, ers = 0, erc = 0, nb = 0;
   const uint64_t lo = 0x00800000u, hi = 0x7f800000u;  // the normal binary32 numbers
   for (uint64_t u = lo + blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; u < hi;
        u += (uint64_t)gridDim.x * blockDim.x) {
@@ -1034,15 +1039,22 @@ __global__ void __launch_bounds__(256) k_selftest_fast_math(unsigned long long* 
       const unsigned long long rcb = (unsigned long long)__double_as_longlong(rc);
       erc = rcb > erc ? rcb : erc;
     }
+    nb += bf16_mismatch(x);
     const double rs = fabs((double)rsqrt_approx(x) * sqrt((double)x) - 1.0);
     const unsigned long long rsb = (unsigned long long)__double_as_longlong(rs);
     ers = rsb > ers ? rsb : ers;
   }
+  // the rest of the non-NaN patterns for the bf16 rounding: zeros,
+  // subnormals and infinity
+  for (uint32_t u = blockIdx.x * blockDim.x + threadIdx.x; u <= lo;
+       u += gridDim.x * blockDim.x)
+    nb += bf16_mismatch(__uint_as_float(u < lo ? u : hi));
   atomicMax(&out[0], me);
   atomicAdd(&out[1], nm);
   atomicAdd(&out[2], nr);
   atomicMax(&out[3], ers);
   atomicMax(&out[4], erc);
+  atomicAdd(&out[5], nb);
 }
 
 }  // namespace

@@ -433,12 +433,26 @@ __device__ __forceinline__ float4 ld_quad(const uint8_t* base, int t0) {
   return *reinterpret_cast<const float4*>(base + 4 * t0);
 }
 
+// Round-to-nearest-even binary32 -> bfloat16 of a pair, packed (lo in the low
+// half) by the hardware conversion, which equals ta_f32_to_bf16 on every
+// non-NaN input (checked exhaustively by ta_selftest_fast_math); a NaN input
+// takes the portable routine out of line, for its NaN encoding.
+__device__ __noinline__ uint32_t bf16x2_portable(float lo, float hi) {
+  return (uint32_t)ta_f32_to_bf16(lo) | ((uint32_t)ta_f32_to_bf16(hi) << 16);
+}
+__device__ __forceinline__ uint32_t bf16x2_rn(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  if (isnan(lo) || isnan(hi)) r = bf16x2_portable(lo, hi);
+  return r;
+}
+
 template <int PT>
 __device__ __forceinline__ void st_quad(void* p, int64_t e, float4 v) {
   if (PT) {
     uint2 w;
-    w.x = (uint32_t)ta_f32_to_bf16(v.x) | ((uint32_t)ta_f32_to_bf16(v.y) << 16);
-    w.y = (uint32_t)ta_f32_to_bf16(v.z) | ((uint32_t)ta_f32_to_bf16(v.w) << 16);
+    w.x = bf16x2_rn(v.x, v.y);
+    w.y = bf16x2_rn(v.z, v.w);
     *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(p) + e) = w;
   } else {
     *reinterpret_cast<float4*>(reinterpret_cast<float*>(p) + e) = v;
@@ -457,7 +471,10 @@ __device__ __forceinline__ float amp_unscale(float g, float ginv) {
 
 template <int PT>
 __device__ __forceinline__ float2 round_param2(float2 v) {
-  if (PT) return make_float2(ta_bf16_to_f32(ta_f32_to_bf16(v.x)), ta_bf16_to_f32(ta_f32_to_bf16(v.y)));
+  if (PT) {
+    const uint32_t r = bf16x2_rn(v.x, v.y);
+    return make_float2(__uint_as_float(r << 16), __uint_as_float(r & 0xffff0000u));
+  }
   return v;
 }
 
