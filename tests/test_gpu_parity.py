@@ -422,3 +422,46 @@ def test_v_update_golden_on_gpu():
             rv = d[f"{k}_s{s}_v_out"]
             rel = np.abs(to_np(v).astype(np.float64) - rv) / np.maximum(np.abs(rv), 1e-45)
             assert rel.max() <= 1e-6, tag
+
+
+BF16_SPECIALS = np.array([0x7FC0, 0xFFC1, 0x7FA5, 0x7F80, 0xFF80, 0x0000, 0x8000, 0x0001,
+                          0x8001, 0x007F, 0x807F, 0x0080, 0x7F7F, 0xFF7F], np.uint16)
+
+
+def test_bf16_special_parameter_values(oracle):
+    """bf16 parameters at the edges of the format -- quiet NaNs with payloads
+    and either sign, +-inf, +-0, subnormals, the smallest normal and the
+    largest finite values -- in full blocks (fast path: hardware pair
+    rounding, NaN inputs through the portable routine) and in the ragged tail
+    (general path). No state depends on the parameters, so the blocks stay on
+    their paths; every parameter bit must equal the checker's, except that a
+    NaN only has to stay NaN (the device's arithmetic returns the canonical
+    NaN, the host's keeps the payload)."""
+    from turboadam_b200 import TurboAdam
+
+    rng = np.random.default_rng(77)
+    n = 2 * 2048 + 77
+    kw = dict(lr=1e-3, betas=(0.9, 0.999), weight_decay=0.01, v_bits=3)
+    init = torch.from_numpy((rng.standard_normal(n) * 0.02).astype(np.float32)).bfloat16()
+    bits = init.view(torch.int16).numpy().view(np.uint16).copy()
+    for pos in (0, 5, 130, 1000, 2047 + 64, n - 77, n - 3):
+        bits[pos:pos + BF16_SPECIALS.size] = BF16_SPECIALS[: min(BF16_SPECIALS.size, n - pos)]
+    tp = torch.nn.Parameter(torch.from_numpy(bits.view(np.int16).copy()).view(torch.bfloat16).cuda())
+    op = oracle.OracleParam(bits.copy(), bf16=True)
+    opt = TurboAdam([tp], seed=5, exact_params=True, **kw)
+    oopt = oracle.OracleTurboAdam([oracle.OracleTurboAdam.make_group([op], **kw)])
+    for step in range(3):
+        g = torch.from_numpy((rng.standard_normal(n) * 1e-4).astype(np.float32)).bfloat16()
+        tp.grad = g.cuda()
+        op.grad = g.float().numpy().reshape(-1).copy()
+        opt.step()
+        oopt.step(uniforms=lambda i, st, npad: oracle.sr_uniforms(n, i, st, 5))
+        torch.cuda.synchronize()
+        got = bits16(tp.data).reshape(-1)
+        nan_ref = (op.data & 0x7FFF) > 0x7F80
+        nan_got = (got & 0x7FFF) > 0x7F80
+        np.testing.assert_array_equal(nan_got, nan_ref, err_msg=f"step {step}")
+        np.testing.assert_array_equal(got[~nan_ref], op.data[~nan_ref], err_msg=f"step {step}")
+        assert nan_ref.sum() == 3 * 7, f"step {step}"  # the planted NaNs stay NaN
+        st, ost = opt.state[tp], oopt.state[id(op)]
+        np.testing.assert_array_equal(to_np(st["compressed_v"]["indices"]), ost.v_idx)
