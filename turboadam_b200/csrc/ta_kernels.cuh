@@ -954,6 +954,12 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
   bool fix = false;              // FULL: this group's block needs the exact path
   if (FULL) {
     float2 am = dup2(0.0f), ag = dup2(0.0f), nanacc = dup2(0.0f);
+    // CoState + 1Q: the range flags come from per-lane reductions instead of a
+    // per-element test. v_new is not finite only for a non-finite g (then the
+    // g.g partial is not finite) or an infinite decoded v (then the largest
+    // v_new is infinite), and v / bc2 overflows only where the largest v_new
+    // times RN(1/bc2) does.
+    constexpr bool RBE = MK == MK_COSTATE && VK == VK_ONEQ;
     float vmin_fp = INFINITY;  // VK_FP32: smallest v_new
     uint32_t idor = 0;
     const float2 zero2 = dup2(0.0f);
@@ -1001,11 +1007,13 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
         const uint32_t w = *reinterpret_cast<const uint32_t*>(sidx + t0);
         float vo[4];
         if (TABLE) {
+          // unmasked index bytes: one >= nb flags the block (idor) and reads at
+          // most 255 entries past its table, inside this CTA's tables + scratch
           idor |= w;
-          vo[0] = tab[w & (uint32_t)(nb - 1)];
-          vo[1] = tab[(w >> 8) & (uint32_t)(nb - 1)];
-          vo[2] = tab[(w >> 16) & (uint32_t)(nb - 1)];
-          vo[3] = tab[(w >> 24) & (uint32_t)(nb - 1)];
+          vo[0] = tab[w & 0xffu];
+          vo[1] = tab[__byte_perm(w, 0u, 0x4441)];
+          vo[2] = tab[__byte_perm(w, 0u, 0x4442)];
+          vo[3] = tab[__byte_perm(w, 0u, 0x4443)];
         } else {  // no table (8 bits): paired branch-free ta_expf (non-finite headers are flagged)
 #pragma unroll
           for (int i = 0; i < 4; i += 2) {
@@ -1035,7 +1043,7 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
         *reinterpret_cast<float4*>(geas + e) = cat4(v01, v23);
         vmin_fp = fminf(fminf(v01.x, v01.y), fminf(fminf(v23.x, v23.y), vmin_fp));
       }
-      if (VK != VK_NONE && !param) nanacc = fma2(v01, zero2, fma2(v23, zero2, nanacc));
+      if (VK != VK_NONE && !param && !RBE) nanacc = fma2(v01, zero2, fma2(v23, zero2, nanacc));
       if (param) {
         // optimizer.py:106-107, 163/167, 170:
         // p = fl(p * (1 - lr wd)); d = sqrt(v / bc2) + eps; p += fl(-lr m) / fl(d bc1)
@@ -1043,7 +1051,7 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
         const float2 w01 = round_param2<PT>(P.mul(lo2(p4), dup2(c.wdf)));
         const float2 w23 = round_param2<PT>(P.mul(hi2(p4), dup2(c.wdf)));
         float2 x01 = P.mul(v01, dup2(c.rbc2)), x23 = P.mul(v23, dup2(c.rbc2));
-        nanacc = fma2(x01, zero2, fma2(x23, zero2, nanacc));  // v or v / bc2 not finite
+        if (!RBE) nanacc = fma2(x01, zero2, fma2(x23, zero2, nanacc));  // v, v / bc2 not finite
         float2 p01, p23;
         if (EX) {
           // v / bc2 by Markstein with y = RN(1/bc2): exact for v in the unflagged range
@@ -1066,7 +1074,9 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
       mgs = __fadd_rn(am.x, am.y);
       ggs = __fadd_rn(ag.x, ag.y);
     }
-    const bool bad = (nanacc.x != nanacc.x) || (nanacc.y != nanacc.y);
+    const bool bad = (nanacc.x != nanacc.x) || (nanacc.y != nanacc.y) ||
+                     (RBE && !(fabsf(ggs) <= 3.4028234663852886e38f &&
+                               __fmul_rn(vmax, c.rbc2) <= 3.4028234663852886e38f));
     if (VK == VK_ONEQ) {
       fix = bad || hdr_bad || vmin < FAST_V_MIN ||
             (TABLE && (idor & (0x01010101u * (uint32_t)(0xff & ~(nb - 1)))) != 0);
