@@ -491,22 +491,19 @@ __device__ __forceinline__ float rcp_approx(float x) {
 
 // Parameter update of a pair without TA_EXACT_PARAM (optimizer.py:163-170):
 // p = w + fl(-lr m) / fl(d bc1), d = sqrt(x) + eps, x = fl(v * RN(1/bc2)).
-// sqrt(x) = x * rsqrt.approx(x); the quotient n / den from y = rcp.approx(den)
-// with Markstein's residual correction q + (n - den q) y. Short dependency
-// chains (the step is latency-bound here) at the price of accuracy: the
-// relative error of the update is at most the rsqrt estimate's (<= 2^-22,
-// checked exhaustively on the device by ta_selftest_fast_math) plus a few
-// roundings, about 3e-7 -- inside the 1e-6 parameter tolerance; no state
-// depends on it. Inputs come from unflagged blocks: x is a finite normal
-// number, den a positive normal number.
+// d = RN(x * rsqrt.approx(x) + eps) in one fma, the quotient n * rcp.approx(den):
+// the shortest chain (the step is latency-bound here). The relative error of
+// the update is at most the two estimates' (each <= 2^-22, checked
+// exhaustively on the device by ta_selftest_fast_math) plus a few roundings,
+// about 5e-7 -- inside the 1e-6 parameter tolerance; no state depends on it.
+// Inputs come from unflagged blocks: x is a finite normal number, den a
+// positive normal number.
 __device__ __forceinline__ float2 adam_pair_fast(float2 w, float2 x, float2 m, const Sc& c,
                                                  const PK& P) {
   const float2 y = make_float2(rsqrt_approx(x.x), rsqrt_approx(x.y));
-  const float2 nden = P.mul(P.add(P.mul(x, y), dup2(c.eps)), dup2(-c.bc1));  // -(d bc1)
+  const float2 nden = P.mul(fma2(x, y, dup2(c.eps)), dup2(-c.bc1));  // -(d bc1)
   const float2 yr = make_float2(rcp_approx(-nden.x), rcp_approx(-nden.y));
-  const float2 n = P.mul(dup2(c.nlr), m);
-  const float2 q = P.mul(n, yr);
-  return P.add(w, fma2(fma2(nden, q, n), yr, q));                            // q + (n - den q) y
+  return P.add(w, P.mul(P.mul(dup2(c.nlr), m), yr));
 }
 
 // Three-input min / max (one instruction on sm_100; NaN operands are
