@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define TA_ABI_VERSION 3
+#define TA_ABI_VERSION 4
 
 typedef enum ta_status {
   TA_OK = 0,
@@ -283,9 +283,13 @@ TA_API ta_status ta_v_update(const uint8_t* idx_dev, const uint16_t* hdr_dev, co
  * file-scope static device array of TA_V_UPDATE_NOALLOC_SCRATCH_BYTES per
  * device, so the call allocates no device memory. n above
  * TA_V_UPDATE_NOALLOC_MAX_N is rejected with TA_ERR_UNSUPPORTED.
- * The first call on a device (with that device current) looks up the array
- * and zeroes it on `stream`; make it before any stream capture. The status
- * word at the start of the array starts at zero that way; every other
+ * Every call looks up the array's device address on the current device (no
+ * allocation); the first call on a device, and the first after a context
+ * reset reloaded the module, zeroes the whole array on `stream` -- make that
+ * call before any stream capture. Each call then clears the array's status
+ * word (its first 4 bytes) and the kernels OR into it what the workspace
+ * entry points report through ta_read_status (TA_STATUS_NONFINITE_GRAD,
+ * TA_STATUS_WAIT_TIMEOUT); ta_v_update_noalloc_status reads it. Every other
  * scratch byte is written by the call before it is read.
  * All calls on one device share the array: calls that can overlap (other
  * streams, other host threads, without ordering) race; serialise them.
@@ -299,6 +303,15 @@ TA_API ta_status ta_v_update_noalloc(const uint8_t* idx_dev, const uint16_t* hdr
                                      const float* uniforms_dev, uint64_t seed,
                                      uint32_t tensor_id, uint32_t step, uint8_t* out_idx_dev,
                                      uint16_t* out_hdr_dev, float* v_out_dev, void* stream);
+
+/*
+ * Device status of the last ta_v_update_noalloc call on the current device
+ * (TA_STATUS_* bits), read from the static array's status word after
+ * `stream` is synchronised; clear != 0 zeroes the word afterwards. No
+ * counterpart in the reference; ta_read_status's counterpart for the entry
+ * point that has no caller workspace.
+ */
+TA_API ta_status ta_v_update_noalloc_status(int32_t clear, uint32_t* status_out, void* stream);
 
 /* 1Q state of a fresh tensor: compress_v_logscale(full(1e-30)) as done at
  * optimizer.py:273-280 (all indices 0, both headers fp16(ln 1e-30)). */
@@ -362,6 +375,19 @@ TA_API size_t ta_aux_workspace_size(int64_t n);
  * out_dev: 6 uint64 in device memory, zeroed by the caller.
  */
 TA_API ta_status ta_selftest_fast_math(uint64_t* out_dev, void* stream);
+
+/*
+ * Device self-test of the bounded waits of the step's pipelines. No
+ * counterpart in the reference. One CTA shaped like the pass kernels arms a
+ * stage for a copy that never lands (none is issued): its consumer warps'
+ * waits run out after limit_ns (0 < limit_ns <= 2e9; the step uses 2 s) and
+ * they skip the stage, the producer's wait for them runs out too, and every
+ * thread returns. It ORs TA_STATUS_WAIT_TIMEOUT into *status_dev and writes
+ * out_dev[0] = the CTA's elapsed nanoseconds (%globaltimer), out_dev[1] =
+ * the number of waits that ran out (5). The context stays usable.
+ */
+TA_API ta_status ta_selftest_wait_timeout(uint64_t limit_ns, uint32_t* status_dev,
+                                          uint64_t* out_dev, void* stream);
 
 #ifdef __cplusplus
 }

@@ -69,6 +69,7 @@ def _declare(L):
         "orc_exp_avg_sq": (None, [_P, _P, _I64, _D]),
         "orc_adam_apply": (None, [_P, _I, _P, _P, _I64, _D, _D, _F, _F]),
         "orc_sr_uniforms": (None, [_I64, _I, _U32, _U32, _U64, _P]),
+        "orc_sr_uniforms_at": (None, [_I64, _I64, _I, _U32, _U32, _U64, _P]),
         "orc_philox": (None, [_U32, _U32, _U32, _U32, _U32, _U32, _P]),
         "orc_logf_array": (None, [_P, _I64, _P]),
         "orc_logf_fast_array": (None, [_P, _I64, _P]),
@@ -152,6 +153,39 @@ def sr_uniforms(n: int, tensor_id: int, step: int, seed: int, bs: int = BLOCK_SI
     lib().orc_sr_uniforms(B, bs, tensor_id & 0xFFFFFFFF, step & 0xFFFFFFFF,
                           seed & 0xFFFFFFFFFFFFFFFF, _ptr(u))
     return u
+
+
+def sr_uniforms_at(b0: int, n_blocks: int, tensor_id: int, step: int, seed: int,
+                   bs: int = BLOCK_SIZE):
+    """The draws of blocks b0 .. b0 + n_blocks - 1 of a tensor (a slice)."""
+    u = np.empty(n_blocks * bs, np.float32)
+    lib().orc_sr_uniforms_at(int(b0), int(n_blocks), bs, tensor_id & 0xFFFFFFFF,
+                             step & 0xFFFFFFFF, seed & 0xFFFFFFFFFFFFFFFF, _ptr(u))
+    return u
+
+
+def costate_decode(labels, signs, norms, amp_bits, alpha, g, bs: int = BLOCK_SIZE):
+    """decode_blocks (costate.py:261-323): m_hat = alpha g + scale sign."""
+    g = np.ascontiguousarray(g, np.float32).reshape(-1)
+    out = np.empty(g.size, np.float32)
+    lib().orc_decode(_ptr(np.ascontiguousarray(labels, np.uint8)),
+                     _ptr(np.ascontiguousarray(signs, np.uint8)),
+                     _ptr(np.ascontiguousarray(norms, np.float32)),
+                     _ptr(np.ascontiguousarray(amp_bits, np.uint16)), float(alpha), _ptr(g),
+                     g.size, bs, _ptr(out))
+    return out
+
+
+def costate_encode(delta, bs: int = BLOCK_SIZE):
+    """encode_blocks (costate.py:213-258): (MSB-first sign bytes, block norms,
+    fp16 scale bits)."""
+    d = np.ascontiguousarray(delta, np.float32).reshape(-1)
+    B = n_blocks(d.size, bs)
+    signs = np.zeros((d.size + 7) // 8, np.uint8)
+    norms = np.empty(B, np.float32)
+    amp = np.empty(B, np.uint16)
+    lib().orc_encode(_ptr(d), d.size, bs, _ptr(signs), _ptr(norms), _ptr(amp))
+    return signs, norms, amp
 
 
 def threads() -> int:

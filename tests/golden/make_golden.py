@@ -124,6 +124,31 @@ def gen_v_cases(mods, out_dir):
     print("v_update cases:", ci)
 
 
+def gen_v_decode_cases(mods, out_dir):
+    """decompress_v (oneq.py:51-67 -> quantize.py:183-214) of states made by
+    compress_v_logscale (oneq.py:13-48) from random v, every v_bits."""
+    _, _, oneq, _, _ = mods
+    rng = np.random.default_rng(4321)
+    cases = {}
+    ci = 0
+    for nbits in (2, 3, 4, 6, 8):
+        for n in (1, 129, 16384 + 37):
+            v0 = torch.from_numpy(
+                (rng.random(n) * 10.0 ** rng.uniform(-14, 0, n)).astype(np.float32))
+            cv = oneq.compress_v_logscale(v0, n_bits=nbits, block_size=128,
+                                          stochastic_round=False)
+            v = oneq.decompress_v(cv)
+            key = f"c{ci:03d}"
+            cases[f"{key}_idx"] = cv["indices"].numpy().copy()
+            cases[f"{key}_hdr"] = h16(cv["scales"])
+            cases[f"{key}_v"] = v.reshape(-1).numpy().copy()
+            cases[f"{key}_meta"] = np.array([nbits, n], np.int64)
+            ci += 1
+    cases["n_cases"] = np.array([ci], np.int64)
+    np.savez_compressed(os.path.join(out_dir, "v_decode.npz"), **cases)
+    print("v_decode cases:", ci)
+
+
 # ---------------------------------------------------------------------------
 # B. CoStateManager.update sequences (costate.py:367-464)
 # ---------------------------------------------------------------------------
@@ -306,20 +331,102 @@ def gen_optimizer_runs(mods, out_dir):
         print("optimizer run:", name)
 
 
+# ---------------------------------------------------------------------------
+# D. A reference checkpoint and its continuation (optimizer.py:194-218)
+# ---------------------------------------------------------------------------
+
+CKPT_SPEC = (
+    [((64, 64), 0), ((96, 50), 0), ((130,), 0), ((4133,), 1), ((80, 64), 1)],
+    [dict(lr=6e-4, betas=(0.9, 0.999), weight_decay=0.01, v_bits=4),
+     dict(lr=1e-3, weight_decay=0.0, v_bits=3, error_feedback=True)],
+    3, 2,  # steps before the checkpoint, steps after it
+)
+
+
+def gen_checkpoint_run(mods, out_dir):
+    """torch.save of the reference optimizer's state_dict() after 3 steps
+    (ref_ckpt.pt: pickled turboadam.costate.CoStateManager objects), then the
+    reference's next 2 steps from that state (ckpt_cont.npz: gradients,
+    uniforms, alpha and every output), all with injected uniforms."""
+    turboadam, _, _, _, _ = mods
+    pspecs, gkw, n_before, n_after = CKPT_SPEC
+    rng = np.random.default_rng(777)
+    feed = UniformFeed()
+    params = [torch.nn.Parameter(torch.from_numpy(
+        (rng.standard_normal(shape) * 0.02).astype(np.float32))) for shape, _ in pspecs]
+    groups = [dict(params=[params[i] for i, s in enumerate(pspecs) if s[1] == gi], **kw)
+              for gi, kw in enumerate(gkw)]
+    opt = turboadam.TurboAdam(groups)
+    order = [i for gi in range(len(gkw)) for i, s in enumerate(pspecs) if s[1] == gi]
+    data = {}
+
+    def one_step(s, record):
+        for pi, p in enumerate(params):
+            g = (rng.standard_normal(p.shape) * 10.0 ** rng.uniform(-4, -2)).astype(np.float32)
+            p.grad = torch.from_numpy(g)
+            if record:
+                data[f"s{s}_g{pi}"] = g
+        for pi in order:  # the reference draws in step (group, param) order
+            B = (params[pi].numel() + 127) // 128
+            u = rng.random(B * 128).astype(np.float32)
+            feed.push(u)
+            if record:
+                data[f"s{s}_u{pi}"] = u
+        with feed.active():
+            opt.step()
+
+    for s in range(n_before):
+        one_step(s, False)
+    torch.save(opt.state_dict(), os.path.join(out_dir, "ref_ckpt.pt"))
+    for pi, p in enumerate(params):
+        data[f"p{pi}_ckpt"] = p.data.numpy().copy()
+    for s in range(n_after):
+        one_step(s, True)
+        for pi, p in enumerate(params):
+            st = opt.state[p]
+            data[f"s{s}_p{pi}"] = p.data.numpy().copy()
+            data[f"s{s}_step{pi}"] = np.array([st["step"]], np.int64)
+            data[f"s{s}_vidx{pi}"] = st["compressed_v"]["indices"].numpy().copy()
+            data[f"s{s}_vhdr{pi}"] = h16(st["compressed_v"]["scales"])
+            if "exp_avg" in st:
+                data[f"s{s}_m{pi}"] = st["exp_avg"].numpy().copy()
+            if "m_mgr" in st:
+                mg = st["m_mgr"]
+                data[f"s{s}_alpha{pi}"] = np.array([float(mg._alpha)], np.float32)
+                data[f"s{s}_labels{pi}"] = mg._encoded["labels"].numpy().copy()
+                data[f"s{s}_signs{pi}"] = mg._encoded["sign_packed"].numpy().copy()
+                data[f"s{s}_norms{pi}"] = mg._encoded["block_norms"].numpy().copy()
+                data[f"s{s}_amp{pi}"] = h16(mg._encoded["scales"])
+                if mg._ef_residual is not None:
+                    data[f"s{s}_ef{pi}"] = mg._ef_residual.numpy().copy()
+    np.savez_compressed(os.path.join(out_dir, "ckpt_cont.npz"), **data)
+    print("checkpoint run: ref_ckpt.pt + ckpt_cont.npz")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("TURBOADAM_REF"),
                     help="checkout of the reference repository (or set TURBOADAM_REF)")
     ap.add_argument("--out", default=os.path.dirname(os.path.abspath(__file__)))
+    ap.add_argument("--only", nargs="*", default=None,
+                    help="generate only these sets (v, v_decode, costate, costate_ef, runs, "
+                         "checkpoint)")
     a = ap.parse_args()
     if not a.ref:
         ap.error("--ref (or TURBOADAM_REF) must name the reference checkout")
     torch.set_num_threads(1)
     mods = _import_reference(a.ref)
-    gen_v_cases(mods, a.out)
-    gen_costate_cases(mods, a.out)
-    gen_costate_cases(mods, a.out, ef=True)
-    gen_optimizer_runs(mods, a.out)
+    sets = {
+        "v": lambda: gen_v_cases(mods, a.out),
+        "v_decode": lambda: gen_v_decode_cases(mods, a.out),
+        "costate": lambda: gen_costate_cases(mods, a.out),
+        "costate_ef": lambda: gen_costate_cases(mods, a.out, ef=True),
+        "runs": lambda: gen_optimizer_runs(mods, a.out),
+        "checkpoint": lambda: gen_checkpoint_run(mods, a.out),
+    }
+    for name, fn in sets.items():
+        if a.only is None or name in a.only:
+            fn()
 
 
 if __name__ == "__main__":

@@ -11,13 +11,19 @@ def load(name):
     return np.load(os.path.join(GOLDEN, name))
 
 
-def runs():
-    """RUNS table of make_golden.py (imported without running the generator)."""
+def load_module(name):
+    """A module of tests/golden/ (make_golden.py: its tables, without running
+    the generator, which needs the reference checkout)."""
     spec = importlib.util.spec_from_file_location(
-        "_make_golden", os.path.join(GOLDEN, "make_golden.py"))
+        "_golden_" + name.replace(".py", ""), os.path.join(GOLDEN, name))
     m = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(m)
-    return m.RUNS
+    return m
+
+
+def runs():
+    """RUNS table of make_golden.py."""
+    return load_module("make_golden.py").RUNS
 
 
 def bf16_to_f32(bits):

@@ -30,11 +30,11 @@ def test_header_symbols_exported(lib):
     from turboadam_b200 import _lib
 
     names = declared_symbols()
-    assert len(names) == 20
+    assert len(names) == 22
     assert sorted(_lib.EXPORTED) == names
     for n in names:
         assert hasattr(lib, n), n
-    assert lib.ta_abi_version() == 3
+    assert lib.ta_abi_version() == 4
 
 
 def test_struct_layout_matches_header(lib):

@@ -135,3 +135,29 @@ def test_nonfinite_headers_and_wild_indices_bitexact(oracle):
         got = tp.detach().cpu().numpy()
         same = (got.view(np.uint32) == op.data.view(np.uint32)) | (np.isnan(got) & np.isnan(op.data))
         assert same.all(), tag
+
+
+@pytest.mark.gpu
+def test_bounded_wait_runs_out_and_reports():
+    """The pipelines' bounded mbarrier wait (ta_selftest_wait_timeout): a
+    stage armed for a copy that never lands makes every consumer warp's wait
+    and then the producer's run out after the limit; the kernel returns, the
+    status word reads TA_STATUS_WAIT_TIMEOUT and the context stays usable."""
+    from turboadam_b200 import _lib
+
+    lib = _lib.load()
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    out = torch.zeros(2, dtype=torch.int64, device="cuda")
+    limit_ns = 20_000_000  # 20 ms
+    rc = lib.ta_selftest_wait_timeout(limit_ns, status.data_ptr(), out.data_ptr(),
+                                      _lib.stream_ptr(torch.device("cuda")))
+    assert rc == 0, lib.ta_last_error().decode()
+    torch.cuda.synchronize()
+    assert int(status.item()) == _lib.TA_STATUS_WAIT_TIMEOUT
+    elapsed, timeouts = (int(x) for x in out.tolist())
+    assert timeouts == 5  # 4 consumer warps + the producer
+    assert limit_ns <= elapsed < 1_000_000_000
+    assert torch.ones(4, device="cuda").sum().item() == 4.0
+    assert lib.ta_selftest_wait_timeout(0, status.data_ptr(), out.data_ptr(), None) == 1
+    assert lib.ta_selftest_wait_timeout(3_000_000_000, status.data_ptr(), out.data_ptr(),
+                                        None) == 1

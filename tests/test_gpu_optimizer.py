@@ -1,8 +1,6 @@
 """Reference behaviour of TurboAdam (reference tests/test_optimizer.py,
 test_costate.py, test_oneq.py semantics) on the sm_100a path."""
-import math
 
-import numpy as np
 import pytest
 import torch
 import torch.nn as nn
@@ -252,9 +250,10 @@ def test_nonfinite_grad_flag():
     assert opt.read_status() & TA_STATUS_NONFINITE_GRAD
 
 
-def test_thresholds_and_codec_seams():
-    """compute_thresholds / decode / encode seams vs the reference formulas."""
-    from turboadam_b200.costate import compute_thresholds, decode_blocks, encode_blocks
+def test_thresholds_seam():
+    """compute_thresholds seam vs torch.sort indexing (costate.py:94-118); the
+    codec seams are checked bit for bit in test_gpu_seams.py."""
+    from turboadam_b200.costate import compute_thresholds
 
     torch.manual_seed(1)
     r = torch.rand(10007, device="cuda")
@@ -263,19 +262,3 @@ def test_thresholds_and_codec_seams():
     n = r.numel()
     assert t0.item() == s[max(0, int(0.1 * n) - 1)].item()
     assert t1.item() == s[min(n - 1, int(0.9 * n))].item()
-    delta = torch.randn(300, device="cuda")
-    labels = torch.tensor([0, 1, 2], dtype=torch.uint8, device="cuda")
-    enc = encode_blocks(delta, labels)
-    assert enc["sign_packed"].numel() == math.ceil(300 / 8)
-    g = torch.randn(300, device="cuda")
-    m = decode_blocks(enc, 1.5, g, 128, 300)
-    exp = 1.5 * g.clone()
-    for i, lab in enumerate([0, 1, 2]):
-        blk = delta[i * 128:(i + 1) * 128]
-        if lab == 1:
-            exp[i * 128:(i + 1) * 128] += blk.norm() / math.sqrt(128) * torch.sign(blk)
-        elif lab == 2:
-            sc = (blk.norm() / math.sqrt(128)).half().float()
-            exp[i * 128:(i + 1) * 128] += sc * torch.sign(blk)
-    assert torch.allclose(m, exp, atol=1e-2)
-    assert np.isfinite(m.cpu().numpy()).all()

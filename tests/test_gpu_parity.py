@@ -111,16 +111,19 @@ def assert_params_close(got, ref, before, bf16, tag):
 
 
 def run_compare(oracle, shapes, groups_kw, nsteps, dtype=torch.float32, parity=False,
-                seed=1234, grad_scale=1e-3, assign=None, zero_rows=None, exact_params=True):
+                seed=1234, grad_scale=1e-3, assign=None, zero_rows=None, exact_params=True,
+                init_kinds=None):
     """Runs TurboAdam on the GPU and the checker replay side by side and
     asserts bit equality of every state tensor after each step, and of every
     parameter with exact_params (else parameters within the tolerance above:
-    no state depends on them)."""
+    no state depends on them). init_kinds: per shape "normal" (N(0, 0.02),
+    the default), "ones" or "zeros"."""
     from turboadam_b200 import TurboAdam
 
     rng = np.random.default_rng(seed)
     assign = assign or [0] * len(shapes)
-    inits = [_init_np(s, rng, "normal") for s in shapes]
+    init_kinds = init_kinds or ["normal"] * len(shapes)
+    inits = [_init_np(s, rng, k) for s, k in zip(shapes, init_kinds)]
     bf = dtype == torch.bfloat16
     tparams = []
     oparams = []
@@ -210,6 +213,22 @@ def test_gpt2_block_bitexact(oracle, parity, exact_params):
     run_compare(oracle, GPT2_BLOCK, [dict(lr=6e-4, betas=(0.9, 0.999), weight_decay=0.01,
                                           v_bits=4)], nsteps=3, parity=parity,
                 exact_params=exact_params)
+
+
+# BASELINE config 1 exactly: LayerNorm weights 1, biases 0, matrices N(0, 0.02)
+GPT2_BLOCK_INIT = ["ones", "zeros", "normal", "zeros", "normal", "zeros", "ones", "zeros",
+                   "normal", "zeros", "normal", "zeros"]
+
+
+@pytest.mark.parametrize("exact_params", [True, False])
+def test_gpt2_block_200_steps(oracle, exact_params):
+    """Config 1 for its full 200 steps (lr 6e-4, wd 0.01, 4-bit v + CoState,
+    fresh N(0, 1e-3) gradients each step, Philox draws, the GPU's own alpha):
+    every packed state tensor and alpha bit-exact after every step, parameters
+    bit-exact (exact_params) or within 1e-6 relative."""
+    run_compare(oracle, GPT2_BLOCK, [dict(lr=6e-4, betas=(0.9, 0.999), weight_decay=0.01,
+                                          v_bits=4)], nsteps=200, seed=2001,
+                exact_params=exact_params, init_kinds=GPT2_BLOCK_INIT)
 
 
 @pytest.mark.parametrize("exact_params", [True, False])

@@ -1,0 +1,185 @@
+"""Parity at the benchmarked sizes: the packed state the kernels produce for
+the largest tensors of the bench workloads, bit for bit against the CPU
+checker.
+
+* One Llama-3-8B embedding-shaped tensor (128256 x 4096 = 525,336,576 fp32
+  elements, 4,104,192 blocks: the radix select runs over 4.1 M ratios, the
+  alpha reduction over 1,003 chunks, the Philox block counters pass 2^22),
+  CoState + 4-bit 1Q, the production Philox draws and the GPU's own alpha,
+  2 steps: indices, headers, labels, sign bits, norms, fp16 scales and alpha
+  bit-exact, parameters within 1e-6 relative (default update).
+* BASELINE config 3's flat tensor of 2^30 + 37 elements (v-only, 4-bit,
+  Student-t(3) x 1e-3 gradients), 2 steps: byte offsets past 2^32 and the
+  37-element tail block; indices, headers, exp_avg and parameters bit-exact
+  (exact_params). v-only blocks are independent, so the checker replays it
+  slice by slice (each slice with the Philox draws of its global blocks) and
+  the host never holds the whole tensor.
+
+Inputs are generated on the device from seeded generators (slice by slice,
+so a slice can be generated again bit-identically for the checker).
+"""
+import gc
+
+import numpy as np
+import pytest
+import torch
+
+import golden_util as GU
+
+pytestmark = pytest.mark.gpu
+
+GiB = 1 << 30
+
+
+def _need_host(gib):
+    """Skip unless the host has `gib` GiB available (the checker keeps
+    full-size fp32 arrays on the host)."""
+    try:
+        import psutil
+
+        avail = psutil.virtual_memory().available
+    except Exception:  # pragma: no cover
+        return
+    if avail < gib * GiB:
+        pytest.skip(f"needs {gib} GiB of free host memory for the CPU checker "
+                    f"({avail / GiB:.0f} GiB free)")
+
+
+def _need_device(gib):
+    free, _ = torch.cuda.mem_get_info()
+    if free < gib * GiB:
+        pytest.skip(f"needs {gib} GiB of free device memory ({free / GiB:.0f} GiB free)")
+
+
+def to_np(t):
+    return t.detach().cpu().numpy()
+
+
+def bits16(t):
+    return to_np(t.contiguous().view(torch.int16)).view(np.uint16)
+
+
+def _gen(seed, n, dev, kind, scale):
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    if kind == "student_t3":  # Z / sqrt(chi2_3 / 3), as bench.py config 3
+        z = torch.randn(4, n, device=dev, generator=g)
+        return z[0] / ((z[1] * z[1] + z[2] * z[2] + z[3] * z[3]) / 3.0).sqrt() * scale
+    return torch.randn(n, device=dev, generator=g) * scale
+
+
+def test_llama3_embed_costate_2_steps(oracle):
+    """525 M-element CoState + 4-bit tensor, Philox draws, own alpha."""
+    from turboadam_b200 import TurboAdam
+
+    _need_device(12)
+    _need_host(40)
+    oracle.set_threads(len(__import__("os").sched_getaffinity(0)))
+    dev = torch.device("cuda")
+    shape = (128256, 4096)
+    n = shape[0] * shape[1]
+    seed = 8008
+    kw = dict(lr=6e-4, betas=(0.9, 0.999), weight_decay=0.01, v_bits=4)
+    p = torch.nn.Parameter(_gen(11, n, dev, "normal", 0.02).view(shape))
+    op = oracle.OracleParam(to_np(p.data).reshape(-1).copy())
+    opt = TurboAdam([p], seed=seed, **kw)
+    oopt = oracle.OracleTurboAdam([oracle.OracleTurboAdam.make_group([op], **kw)])
+    for s in range(2):
+        g = _gen(100 + s, n, dev, "normal", 1e-4).view(shape)
+        p.grad = g
+        op.grad = to_np(g).reshape(-1)
+        before = op.data.copy()
+        opt.step()
+        torch.cuda.synchronize()
+        oopt.step(uniforms=lambda i, st, npad: oracle.sr_uniforms(n, i, st, seed))
+        tag = f"embed step {s}"
+        st, ost = opt.state[p], oopt.state[id(op)]
+        got = to_np(p.data).reshape(-1)
+        bad = 0
+        for a in range(0, n, 1 << 24):  # float64 temporaries a slice at a time
+            r = op.data[a:a + (1 << 24)]
+            scale = np.abs(r.astype(np.float64) - before[a:a + (1 << 24)])
+            bad += int((~GU.p_close(got[a:a + (1 << 24)], r, scale)).sum())
+        assert bad == 0, f"{tag}: {bad} params beyond 1e-6 relative"
+        del before
+        op.data[:] = got  # both sides continue from the same parameters
+        del got
+        cv = st["compressed_v"]
+        assert np.array_equal(to_np(cv["indices"]), ost.v_idx), f"{tag}: 1Q indices"
+        assert np.array_equal(bits16(cv["scales"]).reshape(-1), ost.v_hdr), f"{tag}: headers"
+        mg, om = st["m_mgr"], ost.mgr
+        enc = mg._encoded
+        assert float(mg._alpha) == om.alpha, f"{tag}: alpha {float(mg._alpha)} vs {om.alpha}"
+        assert np.array_equal(to_np(enc["labels"]), om.labels), f"{tag}: labels"
+        assert np.array_equal(to_np(enc["sign_packed"]), om.signs), f"{tag}: sign bits"
+        assert np.array_equal(to_np(enc["block_norms"]).view(np.uint32),
+                              om.norms.view(np.uint32)), f"{tag}: block norms"
+        assert np.array_equal(bits16(enc["scales"]), om.amp), f"{tag}: fp16 scales"
+        # the thresholds are the exact order statistics of the 4.1 M ratios
+        srt = np.sort(om.last_ratios)
+        klo, khi = oracle.threshold_ranks(srt.size, 0.10, 0.90)
+        assert om.last_tau[0] == srt[klo] and om.last_tau[1] == srt[khi], tag
+        del srt
+        p.grad = None
+        del g
+        gc.collect()
+
+
+def test_flat_vonly_2_30_plus_37_2_steps(oracle):
+    """BASELINE config 3 tensor (2^30 + 37 elements), 4-bit v-only, 2 steps,
+    compared slice by slice (64 Mi elements each, then the 37-element tail)."""
+    from turboadam_b200 import TurboAdam
+
+    _need_device(20)
+    _need_host(12)
+    oracle.set_threads(len(__import__("os").sched_getaffinity(0)))
+    dev = torch.device("cuda")
+    n = (1 << 30) + 37
+    SL = 1 << 26
+    bounds = [(a, min(a + SL, n)) for a in range(0, n, SL)]
+    assert bounds[-1] == (1 << 30, n)  # the tail block is a slice of its own
+    seed = 3003
+    kw = dict(lr=1e-3, betas=(0.9, 0.999), weight_decay=0.01, compress_m=False, v_bits=4)
+
+    def p0(k, a, b):
+        return _gen(7000 + k, b - a, dev, "normal", 0.02)
+
+    def grad(step, k, a, b):
+        return _gen(9000 + 100 * step + k, b - a, dev, "student_t3", 1e-3)
+
+    p = torch.nn.Parameter(torch.empty(n, device=dev))
+    with torch.no_grad():
+        for k, (a, b) in enumerate(bounds):
+            p[a:b] = p0(k, a, b)
+    opt = TurboAdam([p], seed=seed, exact_params=True, **kw)
+    for step in range(2):
+        g = torch.empty(n, device=dev)
+        for k, (a, b) in enumerate(bounds):
+            g[a:b] = grad(step, k, a, b)
+        p.grad = g
+        opt.step()
+        torch.cuda.synchronize()
+        p.grad = None
+        del g
+        st = opt.state[p]
+        for k, (a, b) in enumerate(bounds):
+            tag = f"flat step {step} slice {k} [{a}, {b})"
+            b0, nb = a // 128, (b - a + 127) // 128
+            op = oracle.OracleParam(to_np(p0(k, a, b)).copy())
+            oopt = oracle.OracleTurboAdam([oracle.OracleTurboAdam.make_group([op], **kw)])
+            for s in range(step + 1):
+                op.grad = to_np(grad(s, k, a, b))
+                oopt.step(uniforms=lambda i, st_, npad: oracle.sr_uniforms_at(b0, nb, 0, st_,
+                                                                             seed))
+            ost = oopt.state[id(op)]
+            assert np.array_equal(to_np(p.data[a:b]).view(np.uint32),
+                                  op.data.view(np.uint32)), f"{tag}: params"
+            assert np.array_equal(to_np(st["exp_avg"][a:b]).view(np.uint32),
+                                  ost.exp_avg.view(np.uint32)), f"{tag}: exp_avg"
+            cv = st["compressed_v"]
+            assert np.array_equal(to_np(cv["indices"][a:a + nb * 128]), ost.v_idx), \
+                f"{tag}: 1Q indices"
+            assert np.array_equal(bits16(cv["scales"][b0:b0 + nb]).reshape(-1), ost.v_hdr), \
+                f"{tag}: headers"
+            del op, oopt, ost
+        gc.collect()

@@ -46,6 +46,22 @@ def test_v_update_golden(oracle):
     assert n_idx > 500_000
 
 
+def test_v_decode_golden(oracle):
+    """decompress_v (oneq.py:51-67, quantize.py:183-214): the checker's
+    decode within 1 ulp of torch's exp for every v_bits, odd tails included."""
+    d = GU.load("v_decode.npz")
+    n_el = 0
+    for c in range(int(d["n_cases"][0])):
+        k = f"c{c:03d}"
+        nbits, n = (int(x) for x in d[k + "_meta"])
+        v = oracle.v_decode(d[f"{k}_idx"], d[f"{k}_hdr"], n, nbits)
+        rv = d[f"{k}_v"]
+        assert v.shape == rv.shape == (n,), k
+        assert _ulps(v, rv).max() <= 1, f"{k}: decoded v differs by > 1 ulp"
+        n_el += n
+    assert n_el > 80_000
+
+
 def test_v_init_matches_reference(oracle):
     d = GU.load("v_update.npz")
     for c in range(int(d["n_cases"][0])):

@@ -1,10 +1,17 @@
-"""ZeRO-1 over real NCCL: world-2 ranks on two GPUs step their shards with
+"""ZeRO-1 across processes: world-2 ranks step their shards with
 TurboAdam(shards=..., spanning=...) (alpha chunk sums and threshold
 histograms all-reduced between the phases) and compare every shard bit for
 bit with an unsharded step computed on the same GPU; then, with full
 parameter replicas, step the shard views and gather after every step
-(Zero1ParamGather), and compare every full parameter. Skipped with fewer
-than two GPUs."""
+(Zero1ParamGather), and compare every full parameter.
+
+Two transports: NCCL with one GPU per rank (skipped with fewer than two
+GPUs), and gloo with both ranks on cuda:0 (gloo all-reduces and broadcasts
+CUDA tensors through host memory), which runs the same host logic -- the
+phase generator, the exchange layout, the all-reduces between phases, the
+post-step gather -- as separate processes on a one-GPU machine. The ranks'
+kernels never wait on one another (the exchanges are host-side collectives
+between launches), so sharing a GPU is safe."""
 import datetime
 import os
 import socket
@@ -26,24 +33,29 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank(rank, world, port, out):
+def _rank(rank, world, port, out, backend="nccl"):
     import traceback
 
     try:
-        _rank_body(rank, world, port, out)
+        _rank_body(rank, world, port, out, backend)
     except Exception:
         out.put((rank, ["exception: " + traceback.format_exc()]))
         raise
 
 
-def _rank_body(rank, world, port, out):
+def _rank_body(rank, world, port, out, backend):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     os.environ["NCCL_NVLS_ENABLE"] = "0"
-    torch.cuda.set_device(rank)
-    dev = torch.device("cuda", rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world,
-                            timeout=datetime.timedelta(seconds=60), device_id=dev)
+    gpu = rank if backend == "nccl" else 0
+    torch.cuda.set_device(gpu)
+    dev = torch.device("cuda", gpu)
+    if backend == "nccl":
+        dist.init_process_group("nccl", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60), device_id=dev)
+    else:
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60))
     try:
         from turboadam_b200 import TurboAdam
         from turboadam_b200.sharding import zero1_partition, zero1_spanning
@@ -111,13 +123,12 @@ def _rank_body(rank, world, port, out):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_zero1_over_nccl_matches_unsharded():
+def _run_world(backend):
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_rank, args=(r, world, port, q, backend)) for r in range(world)]
     for p in procs:
         p.start()
     results = dict(q.get(timeout=240) for _ in range(world))
@@ -125,3 +136,12 @@ def test_zero1_over_nccl_matches_unsharded():
         p.join(timeout=120)
         assert p.exitcode == 0
     assert results == {0: [], 1: []}, results
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_zero1_over_nccl_matches_unsharded():
+    _run_world("nccl")
+
+
+def test_zero1_two_processes_one_gpu_gloo_matches_unsharded():
+    _run_world("gloo")

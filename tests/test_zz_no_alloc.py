@@ -80,6 +80,36 @@ def test_noalloc_matches_workspace_entry_point(n, v_bits, dtype, use_uni):
         b_idx, b_hdr = rb[0], rb[1]
 
 
+def test_noalloc_status_reports_nonfinite_gradient_per_call():
+    """A NaN gradient sets TA_STATUS_NONFINITE_GRAD in the static array's
+    status word; the next call (finite gradient) starts from a clear word, and
+    clear=1 zeroes it after the read."""
+    lib = _lib.load()
+    n, v_bits = 5000, 4
+    gen = torch.Generator().manual_seed(3)
+    idx, hdr = _state(n, v_bits, gen)
+    stream = _lib.stream_ptr(torch.device("cuda"))
+
+    def status(clear):
+        v = ctypes.c_uint32(0)
+        rc = lib.ta_v_update_noalloc_status(int(clear), ctypes.byref(v), stream)
+        assert rc == 0, lib.ta_last_error().decode()
+        return v.value
+
+    g = (1e-3 * torch.randn(n, generator=gen)).cuda()
+    g_bad = g.clone()
+    g_bad[17] = float("nan")   # full block: fast path flags it, exact path reports it
+    g_bad[n - 3] = float("inf")  # ragged tail block: general path
+    _call(lib, "ta_v_update_noalloc", idx, hdr, g_bad, n, v_bits, None, 5, 1)
+    assert status(clear=False) & _lib.TA_STATUS_NONFINITE_GRAD
+    assert status(clear=True) & _lib.TA_STATUS_NONFINITE_GRAD  # still set, then cleared
+    assert status(clear=False) == 0
+    _call(lib, "ta_v_update_noalloc", idx, hdr, g_bad, n, v_bits, None, 5, 2)
+    assert status(clear=False) & _lib.TA_STATUS_NONFINITE_GRAD
+    _call(lib, "ta_v_update_noalloc", idx, hdr, g, n, v_bits, None, 5, 3)
+    assert status(clear=False) == 0  # each call reports only itself
+
+
 def test_noalloc_rejects_oversize():
     lib = _lib.load()
     rc = lib.ta_v_update_noalloc(None, None, None, _lib.TA_F32, MAX_N + 1, BS, 4, 0.999, None,

@@ -51,6 +51,7 @@ EXPORTED = (
     "ta_read_status",
     "ta_v_update",
     "ta_v_update_noalloc",
+    "ta_v_update_noalloc_status",
     "ta_v_init",
     "ta_v_decode",
     "ta_costate_decode",
@@ -62,6 +63,7 @@ EXPORTED = (
     "ta_plan_prepare",
     "ta_step_prepared",
     "ta_selftest_fast_math",
+    "ta_selftest_wait_timeout",
 )
 
 
@@ -172,6 +174,8 @@ _SIG = {
                                            ctypes.c_int32, ctypes.c_int32, ctypes.c_double, _P,
                                            ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32,
                                            _P, _P, _P, _P]),
+    "ta_v_update_noalloc_status": (ctypes.c_int, [ctypes.c_int32,
+                                                  ctypes.POINTER(ctypes.c_uint32), _P]),
     "ta_v_init": (ctypes.c_int, [ctypes.c_int64, ctypes.c_int32, _P, _P, _P]),
     "ta_v_decode": (ctypes.c_int, [_P, _P, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, _P,
                                    _P]),
@@ -192,6 +196,7 @@ _SIG = {
     "ta_step_prepared": (ctypes.c_int, [_P, ctypes.c_int32, _P, ctypes.c_int32, ctypes.c_uint64,
                                         _P, ctypes.c_size_t, ctypes.POINTER(TaDynamic), _P]),
     "ta_selftest_fast_math": (ctypes.c_int, [_P, _P]),
+    "ta_selftest_wait_timeout": (ctypes.c_int, [ctypes.c_uint64, _P, _P, _P]),
 }
 
 _lib = None

@@ -2,7 +2,12 @@
 
 ``TurboAdam.state_dict()`` already has the reference's keys, dtypes and
 shapes (views of the padded device buffers), and ``load_state_dict`` adopts a
-reference checkpoint. This module adds the on-disk form:
+reference checkpoint. This module adds the on-disk forms:
+
+* ``load_reference_state_dict(f)``: reads a ``torch.save``'d state dict of the
+  reference optimizer without the reference package installed (its
+  ``turboadam.costate.CoStateManager`` objects unpickle as a plain stand-in
+  with the same attributes, which ``TurboAdam.load_state_dict`` converts);
 
 * ``portable_state_dict(opt, pack=False)``: compact tensors (no tile padding),
   each ``CoStateManager`` replaced by a plain dict (so the file loads without
@@ -25,6 +30,47 @@ from .costate import CoStateManager
 from .oneq import adopt_compressed_v
 
 FORMAT = "turboadam_b200/portable-1"
+
+
+class ReferenceCoStateManager:
+    """What a pickled reference ``turboadam.costate.CoStateManager`` loads as
+    without the reference installed: an attribute bag with the reference's
+    attribute names (costate.py:350-365); ``TurboAdam.load_state_dict``
+    turns it into this package's manager."""
+
+    def __setstate__(self, state):
+        self.__dict__.update(state)
+
+
+# classes of the reference package that an optimizer state dict may hold
+_REFERENCE_CLASSES = {("turboadam.costate", "CoStateManager"): ReferenceCoStateManager}
+
+
+def load_reference_state_dict(f, map_location="cpu"):
+    """``torch.load`` of a reference TurboAdam ``state_dict()`` (a path or a
+    file object) that does not need the reference package: its
+    CoStateManager objects come back as :class:`ReferenceCoStateManager`.
+    Any other class of the reference package is refused. Like
+    ``torch.load(weights_only=False)`` this unpickles general Python objects:
+    load only checkpoints you trust."""
+    import pickle
+    import types
+
+    class _Unpickler(pickle.Unpickler):
+        def find_class(self, module, name):
+            if module == "turboadam" or module.startswith("turboadam."):
+                cls = _REFERENCE_CLASSES.get((module, name))
+                if cls is None:
+                    raise pickle.UnpicklingError(
+                        f"{module}.{name} is not part of a TurboAdam optimizer state")
+                return cls
+            return super().find_class(module, name)
+
+    mod = types.ModuleType("turboadam_b200_reference_pickle")
+    mod.Unpickler = _Unpickler
+    mod.load = lambda file, **kw: _Unpickler(file, **kw).load()
+    mod.__dict__.update({k: getattr(pickle, k) for k in ("UnpicklingError", "HIGHEST_PROTOCOL")})
+    return torch.load(f, map_location=map_location, pickle_module=mod, weights_only=False)
 
 
 def pack_indices(idx: torch.Tensor, n_bits: int) -> torch.Tensor:

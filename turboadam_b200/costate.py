@@ -13,7 +13,6 @@ CUDA tensors only.
 """
 from __future__ import annotations
 
-import ctypes
 import math
 
 import torch
@@ -49,6 +48,25 @@ class CoStateManager:
         self._error_feedback = error_feedback
         self._ef_residual = None
         self._bufs = None  # padded device buffers
+
+    @classmethod
+    def from_reference(cls, obj) -> "CoStateManager":
+        """A manager holding the state of another object with the reference's
+        CoStateManager attributes (costate.py:350-365) -- the reference's own
+        class, when a checkpoint was loaded with the reference installed, or
+        the stand-in of ``checkpoint.load_reference_state_dict``. The tensors
+        move to the device on :meth:`adopt`."""
+        mgr = cls(block_size=int(getattr(obj, "block_size", BLOCK_SIZE)),
+                  error_feedback=bool(getattr(obj, "_error_feedback", False)),
+                  null_pct=float(getattr(obj, "_null_pct", 0.10)),
+                  amp_pct=float(getattr(obj, "_amp_pct", 0.90)))
+        mgr._has_state = bool(getattr(obj, "_has_state", False))
+        mgr._alpha = getattr(obj, "_alpha", 0.0)
+        enc = getattr(obj, "_encoded", None)
+        mgr._encoded = None if enc is None else dict(enc)
+        mgr._original_numel = int(getattr(obj, "_original_numel", 0))
+        mgr._ef_residual = getattr(obj, "_ef_residual", None)
+        return mgr
 
     # -- storage ---------------------------------------------------------
     def allocate(self, n: int, device, shape=None) -> None:
@@ -205,5 +223,3 @@ def _select(ratios, null_pct, amp_pct, want_labels):
 def sqrt_block(block_size: int = BLOCK_SIZE) -> float:
     return math.sqrt(block_size)
 
-
-_ = ctypes  # keep the import for type users

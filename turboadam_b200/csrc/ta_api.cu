@@ -982,8 +982,11 @@ ta_status ta_thresholds(const float* ratios_dev, int64_t n_blocks, double null_p
 }  // extern "C"
 
 // ---- ta_v_update_noalloc: ta_v_update's scratch in a static device array --
-// One instance per device (module globals are per context). The pointer is
-// looked up once per device, with that device current, and cached.
+// One instance per device (module globals are per context). Its device
+// address is looked up on every call, with the caller's device current
+// (cudaGetSymbolAddress allocates nothing); the first call that sees a new
+// address -- the first call on a device, or the first after the module was
+// loaded again by a context reset -- zeroes the whole array once.
 static __device__ __align__(256) uint8_t g_noalloc_scratch[TA_V_UPDATE_NOALLOC_SCRATCH_BYTES];
 
 namespace {
@@ -991,25 +994,25 @@ constexpr int kNoAllocMaxDevices = 64;
 std::mutex g_noalloc_mu;
 void* g_noalloc_ptr[kNoAllocMaxDevices] = {};
 
-// Set-up on the first call per device: symbol address (return code checked)
-// and one zeroing of the array on the caller's stream.
+// Device address of the static scratch on the current device (return code
+// checked); zeroes the array on `st` when the address is new.
 ta_status noalloc_scratch(cudaStream_t st, void** out) {
   int dev = -1;
   TA_CU(cudaGetDevice(&dev));
   if (dev < 0 || dev >= kNoAllocMaxDevices)
     return fail(TA_ERR_UNSUPPORTED, "device ordinal " + std::to_string(dev) +
                                         " above the static scratch table");
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess || !p)
+    return fail(TA_ERR_CUDA, std::string("cudaGetSymbolAddress(static scratch): ") +
+                                 cudaGetErrorString(e));
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (!g_noalloc_ptr[dev]) {
-    void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess || !p)
-      return fail(TA_ERR_CUDA, std::string("cudaGetSymbolAddress(static scratch): ") +
-                                   cudaGetErrorString(e));
+  if (g_noalloc_ptr[dev] != p) {
     TA_CU(cudaMemsetAsync(p, 0, TA_V_UPDATE_NOALLOC_SCRATCH_BYTES, st));
     g_noalloc_ptr[dev] = p;
   }
-  *out = g_noalloc_ptr[dev];
+  *out = p;
   return TA_OK;
 }
 // 1 when the hardware pair rounding of (x, -x) differs from the portable one.
@@ -1070,6 +1073,18 @@ ta_status ta_selftest_fast_math(uint64_t* out_dev, void* stream) {
   return TA_OK;
 }
 
+ta_status ta_selftest_wait_timeout(uint64_t limit_ns, uint32_t* status_dev,
+                                   uint64_t* out_dev, void* stream) {
+  g_err.clear();
+  if (!status_dev || !out_dev) return fail(TA_ERR_INVALID, "null argument");
+  if (limit_ns == 0 || limit_ns > WAIT_LIMIT_NS)
+    return fail(TA_ERR_INVALID, "limit_ns must be in (0, 2e9]");
+  k_selftest_wait<<<1, NTHR, 0, (cudaStream_t)stream>>>(
+      limit_ns, status_dev, reinterpret_cast<unsigned long long*>(out_dev));
+  TA_CU(cudaGetLastError());
+  return TA_OK;
+}
+
 ta_status ta_v_update_noalloc(const uint8_t* idx_dev, const uint16_t* hdr_dev,
                               const void* grad_dev, int32_t grad_dtype, int64_t n,
                               int32_t block_size, int32_t v_bits, double beta2,
@@ -1089,10 +1104,21 @@ ta_status ta_v_update_noalloc(const uint8_t* idx_dev, const uint16_t* hdr_dev,
   if (n > 0) {
     const ta_status r = noalloc_scratch((cudaStream_t)stream, &scratch);
     if (r != TA_OK) return r;
+    // the status word (first 4 bytes) reports this call only
+    TA_CU(cudaMemsetAsync(scratch, 0, 4, (cudaStream_t)stream));
   }
   return ta_v_update(idx_dev, hdr_dev, grad_dev, grad_dtype, n, block_size, v_bits, beta2,
                      uniforms_dev, seed, tensor_id, step, out_idx_dev, out_hdr_dev, v_out_dev,
                      scratch, TA_V_UPDATE_NOALLOC_SCRATCH_BYTES, stream);
+}
+
+ta_status ta_v_update_noalloc_status(int32_t clear, uint32_t* status_out, void* stream) {
+  g_err.clear();
+  if (!status_out) return fail(TA_ERR_INVALID, "null status_out");
+  void* scratch = nullptr;
+  const ta_status r = noalloc_scratch((cudaStream_t)stream, &scratch);
+  if (r != TA_OK) return r;
+  return ta_read_status(scratch, clear, status_out, stream);
 }
 
 }  // extern "C"

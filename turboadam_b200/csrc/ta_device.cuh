@@ -17,7 +17,7 @@ constexpr int NCW = 4;              // consumer warps per CTA (4 blocks each)
 constexpr int NTHR = (NCW + 1) * 32;// + one producer warp
 constexpr int NSTAGE = 2;           // pass-1 smem pipeline depth (more CTAs per SM instead)
 constexpr int NSTAGE2 = 4;          // pass-2 depth (small stages, little compute per tile)
-constexpr uint32_t WAIT_LIMIT = 1u << 27;  // bounded mbarrier polling
+constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;  // bounded mbarrier waits (2 s)
 
 constexpr int FIN_THREADS = 256;    // alpha chunk CTA (tiles per chunk)
 constexpr int SEL_CHUNK = 16384;    // ratios per radix-select CTA (amortises the histogram clear / flush)
@@ -136,14 +136,6 @@ __device__ __forceinline__ uint32_t mbar_try_wait(uint64_t* bar, uint32_t parity
       : "r"(smem_u32(bar)), "r"(parity)
       : "memory");
   return ok;
-}
-// Bounded wait: gives up after WAIT_LIMIT polls, records the timeout in the
-// status word and reports false so the caller can drain and return.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status) {
-  for (uint32_t i = 0; i < WAIT_LIMIT; ++i)
-    if (mbar_try_wait(bar, parity)) return true;
-  atomicOr(status, 2u /* TA_STATUS_WAIT_TIMEOUT */);
-  return false;
 }
 // 1D bulk async copy global -> shared, completion counted on `bar`.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,

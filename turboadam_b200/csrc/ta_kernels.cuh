@@ -44,17 +44,56 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
-// Bounded mbarrier wait against wall time (2 s): on expiry the status word
-// records TA_STATUS_WAIT_TIMEOUT and the caller drains and returns.
-__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, uint32_t* status) {
+// Bounded mbarrier wait against wall time (WAIT_LIMIT_NS, 2 s, in the step's
+// kernels): on expiry the status word records TA_STATUS_WAIT_TIMEOUT and the
+// caller drains and returns.
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, uint32_t* status,
+                                         uint64_t limit_ns = WAIT_LIMIT_NS) {
   if (mbar_try_wait(bar, parity)) return true;
   uint64_t t0 = globaltimer_ns();
   for (;;) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (globaltimer_ns() - t0 > 2000000000ull) {
+    if (globaltimer_ns() - t0 > limit_ns) {
       atomicOr(status, 2u);
       return false;
     }
+  }
+}
+
+// Self-test of the bounded wait in the pass kernels' shape: one CTA with a
+// producer thread and NCW consumer warps. The producer arms the stage's
+// "full" barrier for 16 bytes that no copy delivers (a copy that never
+// lands; none is issued, so nothing is in flight), the consumers' waits run
+// out after limit_ns and they skip the stage without arriving on "done",
+// so the producer's wait on "done" runs out as well. Every thread returns;
+// status gets TA_STATUS_WAIT_TIMEOUT, elapsed the CTA's wall time.
+__global__ void __launch_bounds__(NTHR) k_selftest_wait(uint64_t limit_ns, uint32_t* status,
+                                                        unsigned long long* elapsed) {
+  __shared__ __align__(8) uint64_t full, done;
+  __shared__ uint32_t timeouts;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    mbar_init(&full, 1);
+    mbar_init(&done, NCW);
+    fence_barrier_init();
+    timeouts = 0;
+  }
+  __syncthreads();
+  const uint64_t t0 = globaltimer_ns();
+  if (warp == NCW) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&full, 16);
+      if (!wait_bar(&done, 0, status, limit_ns)) atomicAdd(&timeouts, 1u);
+    }
+  } else {
+    const bool ok = wait_bar(&full, 0, status, limit_ns);
+    if (!ok && lane == 0) atomicAdd(&timeouts, 1u);
+    if (ok && lane == 0) mbar_arrive(&done);  // not reached: the stage never fills
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    elapsed[0] = globaltimer_ns() - t0;
+    elapsed[1] = timeouts;  // NCW consumer warps + the producer
   }
 }
 

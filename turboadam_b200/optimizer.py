@@ -31,6 +31,57 @@ _DTYPES = {torch.float32: _lib.TA_F32, torch.bfloat16: _lib.TA_BF16}
 CAPTURE_TABLE_STEPS = 1 << 20
 
 
+class TurboAdamCommError(RuntimeError):
+    """An exchange between the phases of a step whose tensors are split over
+    ranks failed (a rank left, a transport error) or ran past its deadline.
+    The step stopped part way: parameters and 1Q state are updated, the
+    CoState encodings of the split tensors are not, so the optimizer refuses
+    further steps until a checkpoint is loaded (``load_state_dict``)."""
+
+
+# what each exchange of a phased step sums over the ranks
+_EXCHANGES = ("alpha chunk sums (after pass 1)", "threshold histogram, round 0",
+              "threshold histogram, round 1", "threshold histogram, round 2")
+
+
+def run_exchanges(gen, process_group=None, timeout=None):
+    """Drives a phased step: each region the generator yields is summed over
+    the ranks of ``process_group`` in place (all-reduce), then the generator
+    resumes; returns what it returns. ``timeout`` (seconds or None): wait on
+    the host for each all-reduce with that deadline -- a rank that left or a
+    failed transport then ends the step with :class:`TurboAdamCommError`
+    instead of a hang; with None the all-reduce is ordered on the current
+    stream and only the process group's own timeout bounds it."""
+    import datetime
+
+    import torch.distributed as dist
+
+    k = 0
+    try:
+        region = next(gen)
+    except StopIteration as done:
+        return done.value
+    while True:
+        what = _EXCHANGES[k] if k < len(_EXCHANGES) else f"exchange {k}"
+        try:
+            if timeout is None:
+                dist.all_reduce(region, op=dist.ReduceOp.SUM, group=process_group)
+            else:
+                work = dist.all_reduce(region, op=dist.ReduceOp.SUM, group=process_group,
+                                       async_op=True)
+                if work.wait(timeout=datetime.timedelta(seconds=float(timeout))) is False:
+                    raise RuntimeError(f"no completion within {timeout} s")
+        except Exception as e:
+            gen.close()
+            raise TurboAdamCommError(
+                f"exchange {k} of the sharded step ({what}) failed: {e}") from e
+        k += 1
+        try:
+            region = gen.send(None)
+        except StopIteration as done:
+            return done.value
+
+
 def _bias_table(betas, steps):
     """fp32 (1 - beta1^t, 1 - beta2^t) for t = 1..steps, each computed in
     Python float arithmetic exactly as the step does (optimizer.py:172-188)."""
@@ -69,6 +120,11 @@ class TurboAdam(Optimizer):
     threshold histograms all-reduced over ``process_group`` (default group)
     between them -- on every rank, also one that holds no split tensor -- which
     leaves every packed bit equal to the unsharded step's.
+    ``exchange_timeout`` (seconds, default None) puts a host deadline on each
+    of those all-reduces: a rank that left or a failed collective then ends
+    ``step()`` with :class:`TurboAdamCommError` (and the optimizer refuses
+    to step again until a checkpoint is loaded) instead of waiting for the
+    process group's own timeout.
     ``exact_params=True`` computes the parameter update's v / bc2, square root
     and division correctly rounded, so parameters equal the reference's op
     sequence bit for bit; by default they use the hardware rsqrt / rcp
@@ -105,6 +161,7 @@ class TurboAdam(Optimizer):
         spanning=None,
         process_group=None,
         exact_params: bool = False,
+        exchange_timeout: float | None = None,
     ):
         if v_bits not in (2, 3, 4, 6, 8):
             raise ValueError(f"v_bits must be one of {{2, 3, 4, 6, 8}}, got {v_bits}")
@@ -154,6 +211,8 @@ class TurboAdam(Optimizer):
         self._exact_params = bool(exact_params)
         self._btab = {}
         self._pg = process_group
+        self._exchange_timeout = exchange_timeout
+        self._failed = None  # why a sharded step stopped part way (TurboAdamCommError)
         self._xbuf = {}
         self._xslot = {}
         self._xbytes = (0, 0)
@@ -186,8 +245,17 @@ class TurboAdam(Optimizer):
 
     def load_state_dict(self, state_dict):
         """Load and re-home packed state into the padded device layout
-        (reference optimizer.py:194-218 migrates CoState tensors by hand)."""
+        (reference optimizer.py:194-218 migrates CoState tensors by hand).
+
+        Takes this optimizer's own state dicts and the reference's: a
+        ``m_mgr`` of another class with the reference CoStateManager's
+        attributes (the reference's class itself, or the stand-in that
+        ``turboadam_b200.checkpoint.load_reference_state_dict`` unpickles it
+        as) is converted to this package's manager; 1Q headers that torch
+        cast to the parameter dtype go back to fp16 (exact); the reference's
+        CUDA ``rand_buf`` is dropped (the draws are Philox here)."""
         super().load_state_dict(state_dict)
+        self._failed = None
         for group in self.param_groups:
             for p in group["params"]:
                 if p not in self.state:
@@ -196,6 +264,9 @@ class TurboAdam(Optimizer):
                 if "compressed_v" in st and not is_padded(st["compressed_v"], p.device):
                     st["compressed_v"] = adopt_compressed_v(st["compressed_v"], p.device)
                 mgr = st.get("m_mgr")
+                if mgr is not None and not isinstance(mgr, CoStateManager):
+                    mgr = CoStateManager.from_reference(mgr)
+                    st["m_mgr"] = mgr
                 if isinstance(mgr, CoStateManager):
                     mgr.adopt(p.numel(), p.device, p.shape)
                 for k in ("exp_avg", "exp_avg_sq"):
@@ -261,21 +332,15 @@ class TurboAdam(Optimizer):
     @torch.no_grad()
     def step(self, closure=None):
         """Perform a single optimization step."""
-        gen = self._step_gen(closure)
+        if self._failed is not None:
+            raise TurboAdamCommError(
+                f"a previous step stopped part way ({self._failed}); load a checkpoint "
+                "(load_state_dict) before stepping again")
         try:
-            region = next(gen)
-            while True:
-                self._exchange(region)
-                region = gen.send(None)
-        except StopIteration as done:
-            return done.value
-
-    def _exchange(self, region):
-        """Sum an exchange region over the ranks (NCCL all-reduce ordered on
-        the current stream)."""
-        import torch.distributed as dist
-
-        dist.all_reduce(region, op=dist.ReduceOp.SUM, group=self._pg)
+            return run_exchanges(self._step_gen(closure), self._pg, self._exchange_timeout)
+        except TurboAdamCommError as e:
+            self._failed = str(e)
+            raise
 
     def _step_gen(self, closure=None):
         """The step as a generator: yields each exchange region (fp64 alpha

@@ -1,21 +1,7 @@
-"""Block helpers (reference src/turboadam/utils.py)."""
-from __future__ import annotations
+"""Block size of the packed state (reference src/turboadam/utils.py:19).
 
-import torch
-
+The reference pads each tensor to whole blocks on every step
+(``pad_to_blocks``, utils.py:27-66); here the state buffers are allocated
+padded to whole 16-block tiles once, so no padding helper exists.
+"""
 BLOCK_SIZE = 128
-
-
-def pad_to_blocks(tensor: torch.Tensor, block_size: int = BLOCK_SIZE,
-                  pad_value: float = 0.0) -> tuple[torch.Tensor, int]:
-    """Pad a flat tensor to a multiple of block_size (utils.py:27-53)."""
-    n = tensor.shape[0]
-    rem = n % block_size
-    if rem == 0:
-        return tensor, n
-    fill = tensor.new_full((block_size - rem,), pad_value)
-    return torch.cat([tensor, fill]), n
-
-
-def unpad_from_blocks(padded: torch.Tensor, original_length: int) -> torch.Tensor:
-    return padded[:original_length]
