@@ -215,6 +215,15 @@ def test_gpt2_block_bitexact(oracle, parity, exact_params):
                 exact_params=exact_params)
 
 
+def test_stage_reuse_mid_size_bitexact(oracle):
+    """Tensors large enough that every CTA of both passes runs many tiles
+    (each shared-memory stage is refilled tens of times): a 4096 x 4096 and a
+    1000 x 4099 CoState + 4-bit tensor, 2 steps, bit-exact vs the checker."""
+    run_compare(oracle, [(4096, 4096), (1000, 4099)],
+                [dict(lr=6e-4, weight_decay=0.01, v_bits=4)], nsteps=2, seed=404,
+                grad_scale=1e-4)
+
+
 # BASELINE config 1 exactly: LayerNorm weights 1, biases 0, matrices N(0, 0.02)
 GPT2_BLOCK_INIT = ["ones", "zeros", "normal", "zeros", "normal", "zeros", "ones", "zeros",
                    "normal", "zeros", "normal", "zeros"]

@@ -16,7 +16,15 @@ constexpr int TE = BS * TB;         // elements per work tile
 constexpr int NCW = 4;              // consumer warps per CTA (4 blocks each)
 constexpr int NTHR = (NCW + 1) * 32;// + one producer warp
 constexpr int NSTAGE = 2;           // pass-1 smem pipeline depth (more CTAs per SM instead)
-constexpr int NSTAGE2 = 4;          // pass-2 depth (small stages, little compute per tile)
+constexpr int NSTAGE2 = 8;          // pass-2 depth: 2 stages per consumer warp (each warp
+                                    // takes whole tiles)
+constexpr int P2_CTAS = 3;          // pass-2 CTAs per SM (shared memory bound)
+// Pass 2's consumer warp w takes iterations w, w + NCW, ..., so iteration it
+// uses stage it % NSTAGE2; with NSTAGE2 a multiple of NCW every use of a stage
+// falls to the same warp, in order. A stage shared by two warps would break
+// the parity waits: a warp one use ahead waits for parity p of a barrier
+// whose previous phase (parity p as well) completed, and passes early.
+static_assert(NSTAGE2 % NCW == 0, "pass-2 stages must map to fixed consumer warps");
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;  // bounded mbarrier waits (2 s)
 
 constexpr int FIN_THREADS = 256;    // alpha chunk CTA (tiles per chunk)

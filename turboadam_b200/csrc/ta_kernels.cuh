@@ -1554,30 +1554,156 @@ __global__ void __launch_bounds__(FIN_THREADS) k_alpha_fin(const __grid_constant
 // ---------------------------------------------------------------------------
 // Pass 2: CoState encode (costate.py:419-425, :51-86, :213-258)
 // ---------------------------------------------------------------------------
-// HS (fast path only): the tensor holds a previous encoding (has_state as a
-// compile-time value, so the m_hat select of the first step is not paid later).
-template <int PT, bool FULL, bool AMP = false, bool HS = true>
-__device__ __forceinline__ void p2_block(const DevTensor* T, const StageMeta& M,
-                                         const uint8_t* st, uint2* wb) {
+// Each consumer warp takes whole tiles (16 blocks): the stages of iterations
+// w, w + NCW, ... of its CTA.
+
+// The per-block tail of pass 2: norms from the torch row-norm partials (the
+// 8 lane accumulators summed 0..7 in order), fp16 amplitude scale and the
+// block ratio (costate.py:51-86, :213-258).
+__device__ __forceinline__ void p2_block_norms(const StageMeta& M, int64_t b, float sd, float sm,
+                                               bool fast) {
+  const float sqbs = M.c.sqbs;
+  const float dn = __fsqrt_rn(sd);
+  const float mnorm = __fsqrt_rn(sm);
+  M.nrm[b] = dn;
+  if (fast && dn >= 0x1p-60f && dn <= 0x1p60f && mnorm >= 0x1p-60f && mnorm <= 0x1p60f) {
+    // Markstein quotients (y = RN(1/b): exact for these ranges); dn finite
+    M.amp[b] = f2h_fin(div_by(dn, sqbs, M.c.rsqbs));
+    M.ratios[b] = div_by(dn, mnorm, rcp_exact(mnorm));
+  } else {
+    M.amp[b] = f32_to_f16_dev(__fdiv_rn(dn, sqbs));
+    M.ratios[b] = (mnorm == 0.0f) ? 0.0f : __fdiv_rn(dn, mnorm);
+  }
+}
+
+// Fast path of one full tile, two lanes per block: lane l takes block
+// bi = 4 ((l >> 1) & 3) + (l >> 3) and, of its 8 torch row-norm accumulators
+// (element j + 8k feeds accumulator j), the half h = l & 1: elements
+// 8k + 4h + i, i = 0..3, k = 0..15 -- one 16-byte (fp32) shared load per k,
+// conflict-free because the 8 lanes of a quarter warp read 4 different
+// skewed 4-block copies. The arithmetic runs on packed pairs; each pair's two
+// accumulators stay sequential in k (torch's order). The new sign bits
+// (delta < 0, MSB first) of a lane form one nibble per k; the two lanes of a
+// block swap halves and each stores 8 sign bytes.
+// HS: the tensor holds a previous encoding (the m_hat select of the first
+// step is not paid later). AMP: gradients are unscaled on load.
+template <int PT, bool AMP, bool HS>
+__device__ __forceinline__ void p2_tile_fast(const StageMeta& M, const uint8_t* st) {
+  using L = P2L<PT>;
+  const int lane = threadIdx.x & 31;
+  const int h = lane & 1;
+  const int bi = 4 * ((lane >> 1) & 3) + (lane >> 3);
+  const int64_t b = M.b0 + bi;
+  const uint8_t* sg = st + L::OFF_G + L::AG::off(bi);
+  const PK P(M.c.one, M.c.nzero);
+
+  float cs_scale = 0.0f;
+  uint32_t w0 = 0, w1 = 0, w2 = 0, w3 = 0;  // old sign bytes 4c..4c+3, pre-shifted by 4h
+  if (HS) {
+    const uint8_t lab = st[L::OFF_LAB + bi];
+    const float nrm = reinterpret_cast<const float*>(st + L::OFF_NRM)[bi];
+    const uint16_t amp = reinterpret_cast<const uint16_t*>(st + L::OFF_AMP)[bi];
+    // as in pass 1: Markstein for norms in [2^-100, 2^100], 0, non-finite
+    const float ph = (nrm > 0.0f && nrm < 0x1p-100f) || nrm > 0x1p100f
+                         ? __fdiv_rn(nrm, M.c.sqbs)
+                         : div_by(nrm, M.c.sqbs, M.c.rsqbs);
+    cs_scale = lab == 1 ? ph : (lab == 2 ? f16_to_f32_dev(amp) : 0.0f);
+    const uint4 sw = *reinterpret_cast<const uint4*>(st + L::OFF_SGN + bi * 16);
+    w0 = sw.x << (4 * h);
+    w1 = sw.y << (4 * h);
+    w2 = sw.z << (4 * h);
+    w3 = sw.w << (4 * h);
+  }
+  const uint32_t sc = __float_as_uint(cs_scale);
+  const float2 ao2 = dup2(M.alpha_old), a2 = dup2(M.alpha_new);
+  const float2 b12 = dup2(M.c.b1), omb12 = dup2(M.c.omb1);
+  const float2 zero2 = dup2(0.0f);
+  float2 ad01 = zero2, ad23 = zero2, am01 = zero2, am23 = zero2;
+  uint32_t nib_lo = 0, nib_hi = 0;  // new sign nibbles of k = 0..7 / 8..15 (nibble k at 4k)
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    const float4 g4 = ld_quad<PT>(sg, 8 * k + 4 * h);
+    float2 g01 = lo2(g4), g23 = hi2(g4);
+    if (AMP) {  // GradScaler.unscale_: g * RN(1 / scale), stored in g's dtype
+      g01 = round_param2<PT>(P.mul(g01, dup2(M.c.ginv)));
+      g23 = round_param2<PT>(P.mul(g23, dup2(M.c.ginv)));
+    }
+    // element 8k + 4h + i: old bit 7 - 4h - i of byte k, moved to bit 31
+    const uint32_t w = (k >> 2) == 0 ? w0 : (k >> 2) == 1 ? w1 : (k >> 2) == 2 ? w2 : w3;
+    const int sh = 24 - 8 * (k & 3);
+    const float2 sd01 = make_float2(__uint_as_float(sc ^ ((w << sh) & 0x80000000u)),
+                                    __uint_as_float(sc ^ ((w << (sh + 1)) & 0x80000000u)));
+    const float2 sd23 = make_float2(__uint_as_float(sc ^ ((w << (sh + 2)) & 0x80000000u)),
+                                    __uint_as_float(sc ^ ((w << (sh + 3)) & 0x80000000u)));
+    float2 mh01 = P.add(P.mul(ao2, g01), sd01);  // costate.py:261-323
+    float2 mh23 = P.add(P.mul(ao2, g23), sd23);
+    if (!HS) {
+      mh01 = zero2;
+      mh23 = zero2;
+    }
+    const float2 m01 = P.add(P.mul(b12, mh01), P.mul(omb12, g01));  // costate.py:416
+    const float2 m23 = P.add(P.mul(b12, mh23), P.mul(omb12, g23));
+    const float2 dl01 = P.sub(m01, P.mul(a2, g01));  // costate.py:42
+    const float2 dl23 = P.sub(m23, P.mul(a2, g23));
+    ad01 = P.add(ad01, P.mul(dl01, dl01));
+    ad23 = P.add(ad23, P.mul(dl23, dl23));
+    am01 = P.add(am01, P.mul(m01, m01));
+    am23 = P.add(am23, P.mul(m23, m23));
+    const uint32_t nb = (dl01.x < 0.0f ? 8u : 0u) | (dl01.y < 0.0f ? 4u : 0u) |
+                        (dl23.x < 0.0f ? 2u : 0u) | (dl23.y < 0.0f ? 1u : 0u);
+    if (k < 8) nib_lo |= nb << (4 * k);
+    else nib_hi |= nb << (4 * (k - 8));
+  }
+  // torch row-norm order: accumulators 0..7 summed in sequence; lane h = 0
+  // holds 0..3, its partner 4..7
+  const float q0 = __shfl_xor_sync(0xffffffffu, ad01.x, 1);
+  const float q1 = __shfl_xor_sync(0xffffffffu, ad01.y, 1);
+  const float q2 = __shfl_xor_sync(0xffffffffu, ad23.x, 1);
+  const float q3 = __shfl_xor_sync(0xffffffffu, ad23.y, 1);
+  const float r0 = __shfl_xor_sync(0xffffffffu, am01.x, 1);
+  const float r1 = __shfl_xor_sync(0xffffffffu, am01.y, 1);
+  const float r2 = __shfl_xor_sync(0xffffffffu, am23.x, 1);
+  const float r3 = __shfl_xor_sync(0xffffffffu, am23.y, 1);
+  float sd = __fadd_rn(__fadd_rn(__fadd_rn(ad01.x, ad01.y), ad23.x), ad23.y);
+  float sm = __fadd_rn(__fadd_rn(__fadd_rn(am01.x, am01.y), am23.x), am23.y);
+  sd = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(sd, q0), q1), q2), q3);
+  sm = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(sm, r0), r1), r2), r3);
+  // sign bytes: lane h = 0 writes bytes 0..7 (its high nibbles, the partner's
+  // low ones), lane h = 1 bytes 8..15
+  const uint32_t recv = __shfl_xor_sync(0xffffffffu, h ? nib_lo : nib_hi, 1);
+  const uint32_t A = h ? recv : nib_lo;  // high nibbles (bits 7..4) of the 8 bytes
+  const uint32_t B = h ? nib_hi : recv;  // low nibbles (bits 3..0)
+  const uint32_t E = ((A & 0x0F0F0F0Fu) << 4) | (B & 0x0F0F0F0Fu);          // bytes 0, 2, 4, 6
+  const uint32_t O = (A & 0xF0F0F0F0u) | ((B >> 4) & 0x0F0F0F0Fu);          // bytes 1, 3, 5, 7
+  *reinterpret_cast<uint2*>(M.sgn + b * 16 + 8 * h) =
+      make_uint2(__byte_perm(E, O, 0x5140), __byte_perm(E, O, 0x7362));
+  if (h == 0) p2_block_norms(M, b, sd, sm, true);
+}
+
+// General path of one 4-block group of a tile (blocks 4q + sub, one per 8
+// lanes): per-element bounds, global loads for the ragged tail block, exact
+// special cases, error feedback and the m_out seam.
+template <int PT>
+__device__ __noinline__ void p2_block_general(const DevTensor* T, const StageMeta& M,
+                                              const uint8_t* st, int sub) {
   using L = P2L<PT>;
   const float b1 = M.c.b1, omb1 = M.c.omb1, sqbs = M.c.sqbs, ginv = M.c.ginv;
   const uint32_t flags = M.c.flags;
   const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
   const int q = lane >> 3;
   const int j = lane & 7;
-  const int bi = 4 * q + warp;
-  const bool active = FULL || bi < M.nblk;
+  const int bi = 4 * q + sub;
+  const bool active = bi < M.nblk;
   const int64_t b = M.b0 + bi;
   const int64_t e0 = b * BS;
-  const int nv = FULL ? BS : (active ? (int)min((int64_t)BS, M.n - e0) : 0);
-  const bool fullblk = FULL || nv == BS;
+  const int nv = active ? (int)min((int64_t)BS, M.n - e0) : 0;
+  const bool fullblk = nv == BS;
   const uint32_t gbase = lane & ~7u;
   const uint8_t* sg = st + L::OFF_G + L::AG::off(bi);
   const uint32_t* sgnw = reinterpret_cast<const uint32_t*>(st + L::OFF_SGN + bi * 16);
-  const DevTensor* D = FULL ? nullptr : &T[M.t];  // tail loads and seam outputs only
+  const DevTensor* D = &T[M.t];  // tail loads and seam outputs
 
-  const bool has_state = FULL ? HS : (flags & DF_M_HAS_STATE) != 0;
+  const bool has_state = (flags & DF_M_HAS_STATE) != 0;
   float cs_scale = 0.0f;
   const float alpha_old = M.alpha_old;
   const float alpha = M.alpha_new;
@@ -1585,78 +1711,38 @@ __device__ __forceinline__ void p2_block(const DevTensor* T, const StageMeta& M,
     const uint8_t lab = st[L::OFF_LAB + bi];
     const float nrm = reinterpret_cast<const float*>(st + L::OFF_NRM)[bi];
     const uint16_t amp = reinterpret_cast<const uint16_t*>(st + L::OFF_AMP)[bi];
-    if (FULL) {  // as in pass 1: Markstein for norms in [2^-100, 2^100], 0, non-finite
-      const float ph = (nrm > 0.0f && nrm < 0x1p-100f) || nrm > 0x1p100f
-                           ? __fdiv_rn(nrm, sqbs)
-                           : div_by(nrm, sqbs, M.c.rsqbs);
-      cs_scale = lab == 1 ? ph : (lab == 2 ? f16_to_f32_dev(amp) : 0.0f);
-    } else {
-      cs_scale = costate_scale(lab, nrm, amp, sqbs);
-    }
+    cs_scale = costate_scale(lab, nrm, amp, sqbs);
   }
   float accd = 0.0f, accm = 0.0f;
   uint32_t myw = 0;
-  if (FULL) {
-    // elements k, k + 1 of the lane as packed pairs; the two norm
-    // accumulations stay sequential in k (torch's lane order)
-    const PK P(M.c.one, M.c.nzero);
-    const float2 ao2 = dup2(alpha_old), a2 = dup2(alpha), b12 = dup2(b1), omb12 = dup2(omb1);
-    const uint32_t sc = __float_as_uint(cs_scale);
-#pragma unroll
-    for (int kq = 0; kq < 4; ++kq) {
-      // element j + 8k's sign is bit 7 - j of byte k: shifted left by j, the
-      // 4 bits of word kq sit at the byte tops (bits 7, 15, 23, 31)
-      const uint32_t sw = has_state ? (sgnw[kq] << j) : 0u;
-#pragma unroll
-      for (int i = 0; i < 4; i += 2) {
-        const int k = 4 * kq + i;
-        float2 g = make_float2(ld_smem_elem<PT>(sg, j + 8 * k),
-                               ld_smem_elem<PT>(sg, j + 8 * k + 8));
-        if (AMP) g = round_param2<PT>(P.mul(g, dup2(ginv)));
-        const float2 sd = make_float2(__uint_as_float(sc ^ ((sw << (24 - 8 * i)) & 0x80000000u)),
-                                      __uint_as_float(sc ^ ((sw << (16 - 8 * i)) & 0x80000000u)));
-        float2 mh = P.add(P.mul(ao2, g), sd);  // costate.py:261-323
-        if (!has_state) mh = dup2(0.0f);
-        const float2 m = P.add(P.mul(b12, mh), P.mul(omb12, g));  // costate.py:416
-        const float2 dl = P.sub(m, P.mul(a2, g));                 // costate.py:42
-        const float2 dd = P.mul(dl, dl), mm = P.mul(m, m);
-        accd = __fadd_rn(__fadd_rn(accd, dd.x), dd.y);
-        accm = __fadd_rn(__fadd_rn(accm, mm.x), mm.y);
-        const uint32_t w0 = __ballot_sync(0xffffffffu, dl.x < 0.0f);
-        const uint32_t w1 = __ballot_sync(0xffffffffu, dl.y < 0.0f);
-        if (lane == 0) wb[k >> 1] = make_uint2(w0, w1);  // sign words k, k + 1
-      }
-    }
-  } else {
 #pragma unroll 1
-    for (int kq = 0; kq < 4; ++kq) {
-      const uint32_t sw = (has_state && active) ? sgnw[kq] : 0u;
+  for (int kq = 0; kq < 4; ++kq) {
+    const uint32_t sw = (has_state && active) ? sgnw[kq] : 0u;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int k = 4 * kq + i;
-        const int t = j + 8 * k;
-        const bool ve = t < nv;
-        float g;
-        if (fullblk) g = ld_smem_elem<PT>(sg, t);
-        else g = ve ? to_f32<PT>(D->g, e0 + t) : 0.0f;
-        if (flags & DF_AMP) g = amp_unscale<PT>(g, ginv);
-        const uint32_t bit = (sw >> (8 * i + 7 - j)) & 1u;
-        float m;
-        if (flags & DF_EF_STATE) {
-          const float gm = ve ? __fadd_rn(g, D->ef[e0 + t]) : g;
-          m = costate_m_ef(g, gm, alpha_old, cs_scale, bit, has_state, b1, omb1);
-        } else {
-          m = costate_m(g, alpha_old, cs_scale, bit, has_state, b1, omb1);
-        }
-        const float dl = ve ? __fsub_rn(m, __fmul_rn(alpha, g)) : 0.0f;  // costate.py:42
-        if (ve && (flags & DF_EF)) D->efd[e0 + t] = dl;
-        const float mm = ve ? m : 0.0f;
-        accd = __fadd_rn(accd, __fmul_rn(dl, dl));
-        accm = __fadd_rn(accm, __fmul_rn(mm, mm));
-        const uint32_t w = __ballot_sync(0xffffffffu, dl < 0.0f);
-        myw = (lane == k) ? w : myw;
-        if (ve && (flags & DF_M_OUT)) D->m_out[e0 + t] = m;
+    for (int i = 0; i < 4; ++i) {
+      const int k = 4 * kq + i;
+      const int t = j + 8 * k;
+      const bool ve = t < nv;
+      float g;
+      if (fullblk) g = ld_smem_elem<PT>(sg, t);
+      else g = ve ? to_f32<PT>(D->g, e0 + t) : 0.0f;
+      if (flags & DF_AMP) g = amp_unscale<PT>(g, ginv);
+      const uint32_t bit = (sw >> (8 * i + 7 - j)) & 1u;
+      float m;
+      if (flags & DF_EF_STATE) {
+        const float gm = ve ? __fadd_rn(g, D->ef[e0 + t]) : g;
+        m = costate_m_ef(g, gm, alpha_old, cs_scale, bit, has_state, b1, omb1);
+      } else {
+        m = costate_m(g, alpha_old, cs_scale, bit, has_state, b1, omb1);
       }
+      const float dl = ve ? __fsub_rn(m, __fmul_rn(alpha, g)) : 0.0f;  // costate.py:42
+      if (ve && (flags & DF_EF)) D->efd[e0 + t] = dl;
+      const float mm = ve ? m : 0.0f;
+      accd = __fadd_rn(accd, __fmul_rn(dl, dl));
+      accm = __fadd_rn(accm, __fmul_rn(mm, mm));
+      const uint32_t w = __ballot_sync(0xffffffffu, dl < 0.0f);
+      myw = (lane == k) ? w : myw;
+      if (ve && (flags & DF_M_OUT)) D->m_out[e0 + t] = m;
     }
   }
   // torch row-norm order: lane accumulators summed 0..7 in sequence
@@ -1667,45 +1753,19 @@ __device__ __forceinline__ void p2_block(const DevTensor* T, const StageMeta& M,
     sd = __fadd_rn(sd, __shfl_sync(0xffffffffu, accd, gbase + i));
     sm = __fadd_rn(sm, __shfl_sync(0xffffffffu, accm, gbase + i));
   }
-  const float dn = __fsqrt_rn(sd);
-  const float mnorm = __fsqrt_rn(sm);
   // sign bytes k = 2j, 2j+1 of this block (MSB = lane 0)
-  uint32_t w0, w1;
-  if (FULL) {
-    __syncwarp();
-    const uint2 ww = wb[j];
-    w0 = ww.x;
-    w1 = ww.y;
-  } else {
-    w0 = __shfl_sync(0xffffffffu, myw, 2 * j);
-    w1 = __shfl_sync(0xffffffffu, myw, 2 * j + 1);
-  }
+  const uint32_t w0 = __shfl_sync(0xffffffffu, myw, 2 * j);
+  const uint32_t w1 = __shfl_sync(0xffffffffu, myw, 2 * j + 1);
   if (active) {
     const uint32_t by0 = __brev((w0 >> (8 * q)) & 0xffu) >> 24;
     const uint32_t by1 = __brev((w1 >> (8 * q)) & 0xffu) >> 24;
     reinterpret_cast<uint16_t*>(M.sgn + b * 16)[j] = (uint16_t)(by0 | (by1 << 8));
-    if (j == 0) {
-      M.nrm[b] = dn;
-      if (FULL && dn >= 0x1p-60f && dn <= 0x1p60f && mnorm >= 0x1p-60f && mnorm <= 0x1p60f) {
-        // Markstein quotients (y = RN(1/b): exact for these ranges); dn finite
-        M.amp[b] = f2h_fin(div_by(dn, sqbs, M.c.rsqbs));
-        M.ratios[b] = div_by(dn, mnorm, rcp_exact(mnorm));
-      } else {
-        M.amp[b] = f32_to_f16_dev(__fdiv_rn(dn, sqbs));
-        M.ratios[b] = (mnorm == 0.0f) ? 0.0f : __fdiv_rn(dn, mnorm);
-      }
-    }
+    if (j == 0) p2_block_norms(M, b, sd, sm, false);
   }
 }
 
 template <int PT>
-__device__ __noinline__ void p2_block_general(const DevTensor* T, const StageMeta& M,
-                                              const uint8_t* st) {
-  p2_block<PT, false>(T, M, st, nullptr);
-}
-
-template <int PT>
-__global__ void __launch_bounds__(NTHR, 6) k_pass2(const __grid_constant__ KParams kp) {
+__global__ void __launch_bounds__(NTHR, P2_CTAS) k_pass2(const __grid_constant__ KParams kp) {
   if (step_skipped(kp.skip)) return;
   using L = P2L<PT>;
   using AG = typename L::AG;
@@ -1714,13 +1774,12 @@ __global__ void __launch_bounds__(NTHR, 6) k_pass2(const __grid_constant__ KPara
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + NSTAGE2 * L::STAGE);
   uint64_t* done = full + NSTAGE2;
   StageMeta* meta = reinterpret_cast<StageMeta*>(done + NSTAGE2);
-  uint2* wbufs = reinterpret_cast<uint2*>(meta + NSTAGE2);  // [NCW][8] sign words
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < NSTAGE2; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&done[s], NCW);
+      mbar_init(&done[s], 1);  // one consumer warp per stage
     }
     fence_barrier_init();
   }
@@ -1781,24 +1840,30 @@ __global__ void __launch_bounds__(NTHR, 6) k_pass2(const __grid_constant__ KPara
     }
     return;
   }
-  int it = 0;
-  for (int64_t tile = blockIdx.x; tile < kp.total; tile += gridDim.x, ++it) {
+  // consumer warp w: iterations w, w + NCW, ... of this CTA
+  int it = warp;
+  for (int64_t tile = blockIdx.x + (int64_t)warp * gridDim.x; tile < kp.total;
+       tile += (int64_t)NCW * gridDim.x, it += NCW) {
     const int s = it % NSTAGE2;
     const uint32_t ph = (uint32_t)(it / NSTAGE2) & 1u;
     if (!wait_bar(&full[s], ph, kp.status)) break;
     const StageMeta& pm = meta[s];
     const uint8_t* st = stages + s * L::STAGE;
-    const bool fast = pm.nfull >= 13 + warp && !(pm.c.flags & (DF_M_OUT | DF_EF));
-    const bool hs = pm.c.flags & DF_M_HAS_STATE;
-    uint2* wb = wbufs + warp * 8;
-    if (fast && (pm.c.flags & DF_AMP)) {
-      if (hs) p2_block<PT, true, true, true>(kp.T, pm, st, wb);
-      else p2_block<PT, true, true, false>(kp.T, pm, st, wb);
-    } else if (fast) {
-      if (hs) p2_block<PT, true, false, true>(kp.T, pm, st, wb);
-      else p2_block<PT, true, false, false>(kp.T, pm, st, wb);
+    const uint32_t f = pm.c.flags;
+    const bool fast = pm.nfull == TB && !(f & (DF_M_OUT | DF_EF));
+    if (fast) {
+      const bool hs = f & DF_M_HAS_STATE;
+      if (f & DF_AMP) {
+        if (hs) p2_tile_fast<PT, true, true>(pm, st);
+        else p2_tile_fast<PT, true, false>(pm, st);
+      } else {
+        if (hs) p2_tile_fast<PT, false, true>(pm, st);
+        else p2_tile_fast<PT, false, false>(pm, st);
+      }
+    } else {
+#pragma unroll 1
+      for (int sub = 0; sub < 4; ++sub) p2_block_general<PT>(kp.T, pm, st, sub);
     }
-    else p2_block_general<PT>(kp.T, pm, st);
     __syncwarp();
     if (lane == 0) mbar_arrive(&done[s]);
   }
@@ -1806,8 +1871,7 @@ __global__ void __launch_bounds__(NTHR, 6) k_pass2(const __grid_constant__ KPara
 
 template <int PT>
 constexpr size_t p2_smem_bytes() {
-  return (size_t)NSTAGE2 * P2L<PT>::STAGE + 2 * NSTAGE2 * 8 + NSTAGE2 * sizeof(StageMeta) +
-         NCW * 8 * sizeof(uint2);
+  return (size_t)NSTAGE2 * P2L<PT>::STAGE + 2 * NSTAGE2 * 8 + NSTAGE2 * sizeof(StageMeta);
 }
 
 // ---------------------------------------------------------------------------
