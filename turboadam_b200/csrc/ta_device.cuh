@@ -16,9 +16,10 @@ constexpr int TE = BS * TB;         // elements per work tile
 constexpr int NCW = 4;              // consumer warps per CTA (4 blocks each)
 constexpr int NTHR = (NCW + 1) * 32;// + one producer warp
 constexpr int NSTAGE = 2;           // pass-1 smem pipeline depth (more CTAs per SM instead)
-constexpr int NSTAGE2 = 8;          // pass-2 depth: 2 stages per consumer warp (each warp
-                                    // takes whole tiles)
-constexpr int P2_CTAS = 3;          // pass-2 CTAs per SM (shared memory bound)
+constexpr int NSTAGE2 = 4;          // pass-2 depth: 1 stage per consumer warp (each warp
+                                    // takes whole tiles); more warps beat deeper stages
+                                    // (8 stages at 3 CTAs/SM: 14 % slower, 12 at 2: 44 %)
+constexpr int P2_CTAS = 6;          // pass-2 CTAs per SM (shared memory bound)
 // Pass 2's consumer warp w takes iterations w, w + NCW, ..., so iteration it
 // uses stage it % NSTAGE2; with NSTAGE2 a multiple of NCW every use of a stage
 // falls to the same warp, in order. A stage shared by two warps would break
