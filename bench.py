@@ -11,10 +11,21 @@ Workload (default): the Llama-3-8B parameter set
 (8,030,261,248 fp32 params, 291 tensors), random init N(0, 0.02), seeded
 N(0, 1e-4) gradients, 4-bit v + CoState, lr 6e-4, wd 0.01. Gradients are
 generated once on the device and reused every step (the step does not read
-them differently); inputs (>= 64 GB) exceed the 126 MB L2, so no flush is
-needed between steps. At N > 1 GPUs whole tensors are assigned to ranks by
-longest-processing-time (no tensor spans ranks, so the step has no
-collective); the total parameter set is fixed, i.e. strong scaling.
+them differently). When a workload's bytes exceed 4x the 126 MB L2 nothing
+is flushed between steps; a smaller one (config 1) gets a 512 MB buffer
+written between steps and is timed per step. At N > 1 GPUs whole tensors are
+assigned to ranks by longest-processing-time (no tensor spans ranks, so the
+step has no collective); the total parameter set is fixed, i.e. strong
+scaling. Rank 0 also reports every rank's phase times.
+
+The GPT-2 configs follow BASELINE.json: LayerNorm weights 1 and biases 0;
+config 2's gradients are N(0, sigma_t) with one sigma_t per tensor drawn
+log-uniform in [1e-5, 1e-2] and 5 % of the wte rows zero.
+
+At N = 1 rank 0 also times the reference's own GPU step (its Triton kernels,
+from the unmodified install in baseline/_ref) and ours on the same sample
+of the workload (``reference_gpu``), and the reference algorithm's CPU
+restatement on all host threads and on one (``cpu_baseline``).
 
 --impl reference times the reference algorithm's CPU restatement (oracle/,
 C + OpenMP, all host threads) on a bounded sample of the same workload.
@@ -36,6 +47,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "params updated/sec per optimizer step"
+L2_BYTES = 126 * 1000 * 1000  # B200 L2
 UNIT = "params/s"
 
 
@@ -88,10 +100,12 @@ CONFIGS = {
     # bf16 params and grads, 3-bit v + CoState, ZeRO-1 at 4 and 8 GPUs
     "llama3-70b": dict(shapes=llama3_70b_shapes, kw=dict(lr=6e-4, weight_decay=0.01, v_bits=3),
                        grad_std=1e-4, dtype="bf16", partition="zero1"),
+    # LayerNorm weights 1, biases 0, N(0, 1e-3) gradients
     "gpt2-block": dict(shapes=gpt2_block_shapes, kw=dict(lr=6e-4, weight_decay=0.01, v_bits=4),
-                       grad_std=1e-3, dtype="fp32"),
+                       grad_std=1e-3, dtype="fp32", init="gpt2"),
+    # per-tensor sigma log-uniform in [1e-5, 1e-2], 5 % zero wte rows
     "gpt2-124m": dict(shapes=gpt2_124m_shapes, kw=dict(lr=6e-4, weight_decay=0.01, v_bits=4),
-                      grad_std=1e-3, dtype="fp32"),
+                      grad_std=1e-3, dtype="fp32", init="gpt2", grad_dist="gpt2_c2"),
     # Student-t (nu = 3) gradients scaled by 1e-3
     "flat-vonly": dict(shapes=lambda: [("flat", (2 ** 30 + 37,))],
                        kw=dict(lr=1e-3, compress_m=False, v_bits=4), grad_std=1e-3,
@@ -111,6 +125,41 @@ def student_t3_(out, scale, gen, chunk=1 << 26):
         chi = (z[1] * z[1] + z[2] * z[2] + z[3] * z[3]) / 3.0
         flat[lo:lo + n].copy_(z[0] / chi.sqrt() * scale)
     return out
+
+
+def init_param_(p, name, cfg, gen):
+    """BASELINE init: N(0, 0.02); the GPT-2 configs' LayerNorm weights 1 and
+    biases 0."""
+    if cfg.get("init") == "gpt2" and name.endswith(".b"):
+        return p.zero_()
+    if cfg.get("init") == "gpt2" and name.endswith(".w") and "ln_" in name:
+        return p.fill_(1.0)
+    return p.normal_(0.0, 0.02, generator=gen)
+
+
+def grad_sigma(cfg, t):
+    """Gradient scale of global tensor t (config 2: log-uniform per tensor)."""
+    if cfg.get("grad_dist") == "gpt2_c2":
+        return float(10.0 ** np.random.default_rng(5000 + t).uniform(-5.0, -2.0))
+    return cfg["grad_std"]
+
+
+def make_grad(p, name, t, cfg, gen, row0=0):
+    """Seeded synthetic gradient of (a shard starting at flat element row0 of)
+    global tensor t, in p's shape and dtype."""
+    import torch
+
+    sig = grad_sigma(cfg, t)
+    if cfg.get("grad_dist") == "student_t3":
+        return student_t3_(torch.empty_like(p), sig, gen)
+    g = torch.empty_like(p).normal_(0.0, sig, generator=gen)
+    if cfg.get("grad_dist") == "gpt2_c2" and name == "wte":
+        # 5 % of the embedding rows (768 = 6 blocks each) get zero gradient
+        rows = g.view(-1, 768)
+        mask = torch.from_numpy(np.random.default_rng(6000).random(50257) < 0.05)
+        r0 = row0 // 768
+        rows[mask[r0:r0 + rows.shape[0]].to(g.device)] = 0.0
+    return g
 
 
 def numel(shape):
@@ -224,47 +273,89 @@ def _cpu_pick(cfg_name, shapes):
     return shapes
 
 
-def cpu_sample(cfg_name, target_s=15.0):
+def np_sample_tensors(cfg_name, rng):
+    """The CPU sample's parameters and gradients (numpy), initialised as the
+    GPU workload is (BASELINE init and gradient model)."""
+    from oracle import oracle as O
+
+    cfg = CONFIGS[cfg_name]
+    shapes = cfg["shapes"]()
+    pick = _cpu_pick(cfg_name, shapes)
+    index = {name: t for t, (name, _) in enumerate(shapes)}
+    params = []
+    for name, shp in pick:
+        n = numel(shp)
+        if cfg.get("init") == "gpt2" and name.endswith(".b"):
+            x = np.zeros(n, np.float32)
+        elif cfg.get("init") == "gpt2" and name.endswith(".w") and "ln_" in name:
+            x = np.ones(n, np.float32)
+        else:
+            x = rng.standard_normal(n, dtype=np.float32) * np.float32(0.02)
+        p = O.OracleParam(x)
+        g = rng.standard_normal(n, dtype=np.float32) * np.float32(
+            grad_sigma(cfg, index.get(name, 0)))
+        if cfg.get("grad_dist") == "gpt2_c2" and name == "wte":
+            g.reshape(-1, 768)[np.random.default_rng(6000).random(50257) < 0.05] = 0.0
+        p.grad = g
+        params.append(p)
+    return pick, params
+
+
+def cpu_cpu_model():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return "unknown"
+
+
+def cpu_sample(cfg_name, target_s=12.0):
     """Times the CPU restatement of the step on a bounded sample of the
-    workload (whole tensors, in workload order) on all host threads."""
+    workload (whole tensors, in workload order) on all host threads, and
+    then on one thread."""
+    import torch
+
     from oracle import oracle as O
 
     O.build()
     threads = len(os.sched_getaffinity(0))
-    O.set_threads(threads)
     cfg = CONFIGS[cfg_name]
-    shapes = cfg["shapes"]()
     kw = cfg["kw"]
-    rng = np.random.default_rng(0)
-    # sample: one transformer layer for llama, the whole set for small configs
-    pick = _cpu_pick(cfg_name, shapes)
-    params = [O.OracleParam(rng.standard_normal(numel(s), dtype=np.float32) * np.float32(0.02))
-              for _, s in pick]
-    grads = [rng.standard_normal(p.n, dtype=np.float32) * np.float32(cfg["grad_std"])
-             for p in params]
-    opt = O.OracleTurboAdam([O.OracleTurboAdam.make_group(params, **kw)])
-    for p, g in zip(params, grads):
-        p.grad = g
+    pick, params = np_sample_tensors(cfg_name, np.random.default_rng(0))
     n_total = sum(p.n for p in params)
-    times = []
-    t_all = time.perf_counter()
-    while True:
-        t0 = time.perf_counter()
-        opt.step(uniforms=lambda i, st, npad: O.sr_uniforms(params[i].n, i, st, 1))
-        times.append(time.perf_counter() - t0)
-        if time.perf_counter() - t_all > target_s or len(times) >= 50:
-            break
-    best = statistics.median(times)
+
+    def timed(nthreads, budget):
+        O.set_threads(nthreads)
+        opt = O.OracleTurboAdam([O.OracleTurboAdam.make_group(params, **kw)])
+        times = []
+        t_all = time.perf_counter()
+        while True:
+            t0 = time.perf_counter()
+            opt.step(uniforms=lambda i, st, npad: O.sr_uniforms(params[i].n, i, st, 1))
+            times.append(time.perf_counter() - t0)
+            if time.perf_counter() - t_all > budget or len(times) >= 50:
+                break
+        return statistics.median(times), len(times)
+
+    best, nsteps = timed(threads, target_s)
+    best1, nsteps1 = timed(1, target_s / 2)
+    O.set_threads(threads)
     names = ",".join(n for n, _ in pick)
     return {
         "value": n_total / best,
         "unit": UNIT,
-        "cores": O.threads(),
+        "cores": threads,
         "kind": "port",
         "sample": f"{len(pick)} tensors ({n_total} params: {names[:80]}"
-                  f"{'...' if len(names) > 80 else ''}), {len(times)} steps, median step "
+                  f"{'...' if len(names) > 80 else ''}), {nsteps} steps, median step "
                   f"{best * 1e3:.1f} ms, SR uniforms from the same Philox stream",
+        "single_thread": {"value": n_total / best1, "cores": 1, "steps": nsteps1,
+                          "ms_per_step": best1 * 1e3},
+        "cpu_model": cpu_cpu_model(),
         "host_threads_available": threads,
+        "torch": torch.__version__,
     }
 
 
@@ -276,13 +367,7 @@ def run_reference(args, rank, world):
 
     O.build()
     O.set_threads(len(os.sched_getaffinity(0)))  # all host cores (torchrun sets 1)
-    shapes = cfg["shapes"]()
-    pick = _cpu_pick(args.config, shapes)
-    rng = np.random.default_rng(0)
-    params = [O.OracleParam(rng.standard_normal(numel(s), dtype=np.float32) * np.float32(0.02))
-              for _, s in pick]
-    for p in params:
-        p.grad = rng.standard_normal(p.n, dtype=np.float32) * np.float32(cfg["grad_std"])
+    pick, params = np_sample_tensors(args.config, np.random.default_rng(0))
     opt = O.OracleTurboAdam([O.OracleTurboAdam.make_group(params, **cfg["kw"])])
     ufn = lambda i, st, npad: O.sr_uniforms(params[i].n, i, st, 1)  # noqa: E731
     for _ in range(args.warmup):
@@ -300,7 +385,7 @@ def run_reference(args, rank, world):
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic", "config": {"workload": args.config, "sample_params": n_total},
         "cpu_baseline": {"value": val, "unit": UNIT, "cores": O.threads(), "kind": "port",
-                         "sample": sample},
+                         "sample": sample, "cpu_model": cpu_cpu_model()},
         "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(out), flush=True)
@@ -309,6 +394,91 @@ def run_reference(args, rank, world):
 # ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
+
+def _gpu_ref_pick(cfg_name, shapes):
+    """Sample of the workload for the reference's GPU step: one transformer
+    layer of the Llama configs (its Python loop is per tensor; a layer has
+    every tensor kind), a 2^26 + 37 slice of the flat tensor, else all."""
+    if cfg_name in ("llama3-8b", "llama3-70b"):
+        return [(t, s) for t, s in enumerate(shapes) if s[0].startswith("l0.")]
+    if cfg_name == "flat-vonly":
+        return [(0, ("flat", (2 ** 26 + 37,)))]
+    return list(enumerate(shapes))
+
+
+def reference_gpu(cfg_name, kw, dev, steps=3, warmup=2):
+    """The reference's own optimizer step on this GPU -- TurboAdam.step() of
+    the unmodified package installed in baseline/_ref, whose CUDA path runs
+    its Triton kernels (triton_kernels.py) -- and ours, timed on the same
+    sample tensors with CUDA events around each step() call."""
+    import torch
+
+    from turboadam_b200 import TurboAdam
+
+    ref_dir = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_dir, "turboadam")):
+        return {"unavailable": "the reference is not installed in baseline/_ref"}
+    sys.path.insert(0, ref_dir)
+    try:
+        import turboadam as ref
+        from turboadam import optimizer as ref_optimizer
+    except Exception as e:  # pragma: no cover
+        return {"unavailable": f"import of the reference failed: {e!r}"}
+    finally:
+        sys.path.remove(ref_dir)
+    if not getattr(ref_optimizer, "_HAS_TRITON", False):
+        return {"unavailable": "the reference's Triton kernels did not import"}
+    cfg = CONFIGS[cfg_name]
+    shapes = cfg["shapes"]()
+    pick = _gpu_ref_pick(cfg_name, shapes)
+    pdtype = torch.bfloat16 if cfg["dtype"] == "bf16" else torch.float32
+    gen = torch.Generator(device=dev)
+
+    def tensors():
+        ps = []
+        for t, (name, shp) in pick:
+            gen.manual_seed(1234 + 7919 * t)
+            p = torch.nn.Parameter(init_param_(torch.empty(shp, dtype=pdtype, device=dev), name,
+                                               cfg, gen))
+            p.grad = make_grad(p, name, t, cfg, gen)
+            ps.append(p)
+        return ps
+
+    def timed(opt):
+        for _ in range(warmup):
+            opt.step()
+        torch.cuda.synchronize(dev)
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+        evs[0].record()
+        for k in range(steps):
+            opt.step()
+            evs[k + 1].record()
+        torch.cuda.synchronize(dev)
+        return [evs[k].elapsed_time(evs[k + 1]) for k in range(steps)]
+
+    n = sum(numel(s) for _, (_, s) in pick)
+    try:
+        ps = tensors()
+        ref_ms = timed(ref.TurboAdam(ps, betas=(0.9, 0.999), **kw))
+        del ps
+        torch.cuda.empty_cache()
+        ps = tensors()
+        our_ms = timed(TurboAdam(ps, betas=(0.9, 0.999), seed=2024, **kw))
+        del ps
+        torch.cuda.empty_cache()
+    except Exception as e:
+        return {"unavailable": f"the reference's GPU step failed: {e!r}"[:300]}
+    rm, om = statistics.median(ref_ms), statistics.median(our_ms)
+    return {
+        "value": n / (rm / 1e3), "unit": UNIT, "ms_per_step": rm,
+        "ours_ms_per_step": om, "ours_value": n / (om / 1e3), "speedup": rm / om,
+        "sample": f"{len(pick)} tensors of {cfg_name} ({n} params: "
+                  f"{','.join(s[0] for _, s in pick)[:80]}), {warmup} warm-up + {steps} timed "
+                  "steps each, CUDA events around step(), median",
+        "path": "reference TurboAdam.step() on CUDA tensors from baseline/_ref (unmodified): "
+                "Triton fused_v_update + CoState codec, torch ops for the rest",
+    }
+
 
 def measured_peak():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
@@ -357,10 +527,14 @@ def run_ours(args, rank, world, local_rank):
         parts = zero1_partition([numel(s) for _, s in shapes], world)
         local = [((e1 - e0,), t, (boff, gn)) for t, e0, e1, boff, gn in parts[rank]]
         spanning = zero1_spanning(parts)
+        # the gpt2 init and the wte zero rows need the tensor names; a shard
+        # of wte starts at whole rows only if it starts at element 0
+        row0 = {t: e0 for t, e0, _, _, _ in parts[rank]}
     else:
         owner = lpt_assign(shapes, world)
         local = [(shapes[i][1], i, None) for i in range(len(shapes)) if owner[i] == rank]
         spanning = None
+        row0 = {}
     mine = [(numel(shp), sh[1] if sh else numel(shp)) for shp, _, sh in local]  # (n, n_policy)
     total_params = sum(numel(s) for _, s in shapes)
     my_params = sum(n for n, _ in mine)
@@ -368,13 +542,12 @@ def run_ours(args, rank, world, local_rank):
     params = []
     for shp, t, sh in local:  # data keyed by the global tensor (and shard) index
         gen.manual_seed(1234 + 7919 * t + (sh[0] // 4096 if sh else 0))
-        p = torch.empty(shp, dtype=pdtype, device=dev)
-        p.normal_(0.0, 0.02, generator=gen)
+        name = shapes[t][0]
+        p = init_param_(torch.empty(shp, dtype=pdtype, device=dev), name, cfg, gen)
         p = torch.nn.Parameter(p)
-        if cfg.get("grad_dist") == "student_t3":
-            p.grad = student_t3_(torch.empty_like(p), cfg["grad_std"], gen)
-        else:
-            p.grad = torch.empty_like(p).normal_(0.0, cfg["grad_std"], generator=gen)
+        if name == "wte" and row0.get(t, 0) % 768:
+            raise ValueError("a wte shard must start at a whole row")
+        p.grad = make_grad(p, name, t, cfg, gen, row0.get(t, 0))
         params.append(p)
     opt = TurboAdam(params, betas=(0.9, 0.999), seed=2024, tensor_ids=[t for _, t, _ in local],
                     shards=[sh for _, _, sh in local] if part == "zero1" else None,
@@ -399,14 +572,19 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize(dev)
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
-    clocks = Clocks(torch.cuda.get_device_properties(dev).index if hasattr(
-        torch.cuda.get_device_properties(dev), "index") else local_rank)
-    clocks.index = local_rank
+    clocks = Clocks(local_rank)
+    # a working set that L2 could hold between steps is timed per step, with
+    # a 512 MB buffer written between steps (outside the step's events)
+    ws_bytes = sum(step_bytes(n, kw, psize, npol) for n, npol in mine)
+    flush = ws_bytes < 4 * L2_BYTES
+    fbuf = torch.empty(512 << 20, dtype=torch.uint8, device=dev) if flush else None
     barrier()
     torch.cuda.synchronize(dev)
     clocks.start()
     t_start.record(stream)
     for k in range(args.steps):
+        if flush:
+            fbuf.fill_(k & 0xFF)
         opt._phase_events = evs[k]
         opt.step()
     t_end.record(stream)
@@ -414,19 +592,32 @@ def run_ours(args, rank, world, local_rank):
     clk = clocks.stop()
     barrier()
     opt._phase_events = None
-    ms = t_start.elapsed_time(t_end) / args.steps
+    if flush:
+        ms = sum(row[0].elapsed_time(row[4]) for row in evs) / args.steps
+    else:
+        ms = t_start.elapsed_time(t_end) / args.steps
     phase = np.zeros(4)
     for row in evs:
         for i in range(4):
             phase[i] += row[i].elapsed_time(row[i + 1])
     phase /= args.steps
+    del fbuf
     status = opt.read_status()
+    per_rank = None
     if world > 1:
         import torch.distributed as dist
 
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms_max = float(t.item())
+        mine_t = torch.tensor([ms, *phase.tolist(), float(my_params)], dtype=torch.float64,
+                              device=dev)
+        allr = [torch.empty_like(mine_t) for _ in range(world)]
+        dist.all_gather(allr, mine_t)
+        per_rank = [{"rank": r, "ms_per_step": float(x[0]), "params": int(x[5]),
+                     "phase_ms": {"pass1": float(x[1]), "alpha": float(x[2]),
+                                  "pass2": float(x[3]), "select_labels": float(x[4])}}
+                    for r, x in enumerate(allr)]
     else:
         ms_max = ms
 
@@ -532,7 +723,10 @@ def run_ours(args, rank, world, local_rank):
                                    "at 4096-block boundaries, 4 all-reduces per step (alpha "
                                    "chunk sums, 3 histogram rounds)" if part == "zero1" else
                                    f"by-tensor LPT over {world} GPU(s), no collective"),
-                   "l2": "inputs >= 64 GB exceed the 126 MB L2; no flush"},
+                   "l2": (f"{ws_bytes / 1e6:.0f} MB per rank per step < 4 x 126 MB L2: a 512 MB "
+                          "buffer is written between steps, each step timed by its own events"
+                          if flush else f"{ws_bytes / 1e9:.1f} GB per rank per step exceed the "
+                          "126 MB L2; no flush")},
         "roofline": {
             "bound": "hbm",
             "kernel": "k_pass1 (weight decay + m + 1Q v + AdamW, one HBM pass)",
@@ -555,10 +749,16 @@ def run_ours(args, rank, world, local_rank):
         "gpu_launches": launches_per_step * args.steps,
         "device_status": status,
     }
+    if per_rank:
+        out["per_rank"] = per_rank
     if clk:
         out["clocks"] = clk
     if e2e:
         out["e2e"] = e2e
+    if world == 1 and not args.no_reference_gpu:
+        del opt, params
+        torch.cuda.empty_cache()
+        out["reference_gpu"] = reference_gpu(args.config, kw, dev)
     if world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_sample(args.config)
     print(json.dumps(out), flush=True)
@@ -575,6 +775,8 @@ def main():
     ap.add_argument("--partition", default="auto", choices=["auto", "tensor", "zero1"])
     ap.add_argument("--e2e-steps", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-reference-gpu", action="store_true",
+                    help="skip timing the reference's own GPU step (baseline/_ref)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

@@ -594,8 +594,9 @@ ta_status run_step(const ta_tensor* ts, int nT, const ta_group* groups, uint64_t
   const unsigned xsel_chunks = (unsigned)xsel.beg.back();
   const unsigned xa_chunks = (unsigned)xalist.beg.back();
 
-  if (mode != 2)
-    TA_CU(cudaMemcpyAsync(ws + L.table, host.data() + L.table, host.size() - L.table,
+  if (mode != 2)  // the descriptor table and the list slots in use
+    TA_CU(cudaMemcpyAsync(ws + L.table, host.data() + L.table,
+                          L.lists + L.list_stride * (size_t)slot - L.table,
                           cudaMemcpyHostToDevice, st));
   if (mode == 1) return TA_OK;
   // the select state (alpha's last-CTA counter first of all) starts each step

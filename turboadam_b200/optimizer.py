@@ -229,6 +229,9 @@ class TurboAdam(Optimizer):
             self._xslot = {t: (int(c), int(h)) for (t, _), c, h in zip(spanning, coff, hoff)}
             self._xbytes = (cb.value, hb.value)
         self._plans = None
+        self._ready = set()  # id() of parameters whose state is fully initialised
+        self._devices = set()  # devices of those parameters
+        self._bc_cache = {}  # (beta1, beta2, step) -> fp32 bias corrections
         self._ws = {}
         # test hook: {"uniforms": {param: fp32 [B*128] cuda}, "alpha": {param: fp32 [1] cuda}}
         self._parity = None
@@ -242,6 +245,9 @@ class TurboAdam(Optimizer):
     def add_param_group(self, param_group):
         super().add_param_group(param_group)
         self._plans = None
+        if hasattr(self, "_ready"):
+            self._ready.clear()
+            self._devices.clear()
 
     def load_state_dict(self, state_dict):
         """Load and re-home packed state into the padded device layout
@@ -256,6 +262,8 @@ class TurboAdam(Optimizer):
         CUDA ``rand_buf`` is dropped (the draws are Philox here)."""
         super().load_state_dict(state_dict)
         self._failed = None
+        self._ready.clear()
+        self._devices.clear()
         for group in self.param_groups:
             for p in group["params"]:
                 if p not in self.state:
@@ -318,15 +326,26 @@ class TurboAdam(Optimizer):
             self._plans = None
 
     def _bias_corrections(self):
-        """optimizer.py:172-188: per group, the last param holding state wins."""
+        """optimizer.py:172-188: per group, the last param holding state wins
+        (found from the end of the group; the fp32 values are cached per
+        (betas, step))."""
         out = {}
+        ready = self._ready
         for gi, group in enumerate(self.param_groups):
             beta1, beta2 = group["betas"]
-            for p in group["params"]:
-                if p not in self.state:
+            for p in reversed(group["params"]):
+                if id(p) not in ready and p not in self.state:
                     continue
                 nxt = self.state[p]["step"] + 1
-                out[gi] = (np.float32(1.0 - beta1 ** nxt), np.float32(1.0 - beta2 ** nxt))
+                key = (beta1, beta2, nxt)
+                bc = self._bc_cache.get(key)
+                if bc is None:
+                    if len(self._bc_cache) > 4096:
+                        self._bc_cache.clear()
+                    bc = (np.float32(1.0 - beta1 ** nxt), np.float32(1.0 - beta2 ** nxt))
+                    self._bc_cache[key] = bc
+                out[gi] = bc
+                break
         return out
 
     @torch.no_grad()
@@ -352,18 +371,23 @@ class TurboAdam(Optimizer):
                 loss = closure()
 
         work = []
+        ready = self._ready
         for gi, group in enumerate(self.param_groups):
             for p in group["params"]:
                 if p.grad is None:
                     continue
-                _lib.require_cuda(p)
-                if p.dtype not in _DTYPES:
-                    raise NotImplementedError(
-                        f"param dtype {p.dtype}: the sm_100a step is built for float32 and "
-                        "bfloat16 parameters")
-                if group["block_size"] != 128:
-                    raise NotImplementedError("block_size != 128 is not built for the device step")
-                self._init_state(gi, group, p)
+                if id(p) not in ready:  # checks and lazy state, once per parameter
+                    _lib.require_cuda(p)
+                    if p.dtype not in _DTYPES:
+                        raise NotImplementedError(
+                            f"param dtype {p.dtype}: the sm_100a step is built for float32 and "
+                            "bfloat16 parameters")
+                    if group["block_size"] != 128:
+                        raise NotImplementedError(
+                            "block_size != 128 is not built for the device step")
+                    self._init_state(gi, group, p)
+                    ready.add(id(p))
+                    self._devices.add(p.device)
                 work.append((gi, p))
         if not work:
             return loss
@@ -397,9 +421,12 @@ class TurboAdam(Optimizer):
                     gt["bc1"].fill_(float(bc1))
                     gt["bc2"].fill_(float(bc2))
 
-        by_dev = {}
-        for gi, p in work:
-            by_dev.setdefault(p.device, []).append((gi, p))
+        if len(self._devices) == 1:
+            by_dev = {next(iter(self._devices)): work}
+        else:
+            by_dev = {}
+            for gi, p in work:
+                by_dev.setdefault(p.device, []).append((gi, p))
         for dev, items in by_dev.items():
             yield from self._run_device(dev, items, bcs)
         return loss
@@ -479,29 +506,32 @@ class TurboAdam(Optimizer):
             if xb is None:
                 xb = torch.zeros(cb + hb, dtype=torch.uint8, device=dev)
                 self._xbuf[dev] = xb
-        return {"key": tuple(id(p) for _, p in items), "arr": arr, "groups": groups,
-                "xbytes": cb + hb, "chunk_bytes": cb, "hist_bytes": hb}
+        ps = [p for _, p in items]
+        sts = [self.state[p] for p in ps]
+        return {"key": tuple(id(p) for p in ps), "arr": arr, "groups": groups,
+                "xbytes": cb + hb, "chunk_bytes": cb, "hist_bytes": hb,
+                # per-step fast path: the parameters, their state dicts and
+                # managers in plan order, the parameter storage the table
+                # points at, and whether every manager already holds state
+                "params": ps, "states": sts, "mgrs": [st.get("m_mgr") for st in sts],
+                "pdtypes": [p.dtype for p in ps], "pptrs": [p.data_ptr() for p in ps],
+                "settled": False, "parity_set": False}
 
-    def _run_device(self, dev, items, bcs):
-        lib = _lib.load()
-        if self._plans is None:
-            self._plans = {}
-        plan = self._plans.get(dev)
-        key = tuple(id(p) for _, p in items)
-        if plan is None or plan["key"] != key:
-            plan = self._build_plan(dev, items)
-            self._plans[dev] = plan
-        arr = plan["arr"]
+    def _refresh_grads(self, plan):
+        """Points the plan's table at this step's gradients; returns the
+        tensors to keep alive until the step is enqueued. The common case --
+        contiguous, 16-byte aligned gradients of the parameter's dtype -- is
+        one pass over the list."""
+        ps = plan["params"]
+        grads = [p.grad for p in ps]
+        gptrs = [g.data_ptr() for g in grads]
+        if ([g.dtype for g in grads] == plan["pdtypes"]
+                and all([g.is_contiguous() for g in grads]) and not any([x & 15 for x in gptrs])):
+            plan["arr"]["grad_dev"] = gptrs
+            return grads
         keep = []
-        grad_ptr = arr["grad_dev"]
-        steps = arr["step"]
-        flags = arr["flags"]
-        uni = arr["sr_uniforms_dev"]
-        ainj = arr["alpha_inject_dev"]
-        parity = self._parity
-        for i, (gi, p) in enumerate(items):
-            st = self.state[p]
-            g = p.grad
+        grad_ptr = plan["arr"]["grad_dev"]
+        for i, (p, g) in enumerate(zip(ps, grads)):
             if g.dtype != p.dtype:
                 if p.dtype == torch.float32 and g.dtype == torch.bfloat16:
                     g = g.float()
@@ -510,25 +540,57 @@ class TurboAdam(Optimizer):
             if not g.is_contiguous() or g.data_ptr() % 16:
                 g = g.contiguous().clone() if g.data_ptr() % 16 else g.contiguous()
             keep.append(g)
-            st["step"] += 1  # optimizer.py:103
             grad_ptr[i] = g.data_ptr()
-            steps[i] = st["step"]
-            f = int(flags[i]) & ~(_lib.TA_M_HAS_STATE | _lib.TA_M_EF_STATE)
-            mgr = st.get("m_mgr")
-            if mgr is not None and mgr._has_state:
-                f |= _lib.TA_M_HAS_STATE
-            if mgr is not None and mgr._ef_residual is not None:
-                f |= _lib.TA_M_EF_STATE
-            flags[i] = f
-            if parity is not None:
-                u = parity.get("uniforms", {}).get(p)
-                a = parity.get("alpha", {}).get(p)
-                uni[i] = u.data_ptr() if u is not None else 0
-                ainj[i] = a.data_ptr() if a is not None else 0
-                keep += [u, a]
-            elif uni[i] or ainj[i]:
-                uni[i] = 0
-                ainj[i] = 0
+        return keep
+
+    def _run_device(self, dev, items, bcs):
+        lib = _lib.load()
+        if self._plans is None:
+            self._plans = {}
+        plan = self._plans.get(dev)
+        key = tuple([id(p) for _, p in items])
+        if (plan is None or plan["key"] != key
+                or [p.data_ptr() for p in plan["params"]] != plan["pptrs"]):
+            plan = self._build_plan(dev, items)
+            self._plans[dev] = plan
+        arr = plan["arr"]
+        keep = self._refresh_grads(plan)
+        sts = plan["states"]
+        for st in sts:
+            st["step"] += 1  # optimizer.py:103
+        arr["step"] = [st["step"] for st in sts]
+        settled = plan["settled"]
+        if not settled:
+            # the CoState flags change until every manager holds an encoding
+            # (and, with error feedback, a residual); then they stay put
+            flags = arr["flags"]
+            settled = True
+            for i, mgr in enumerate(plan["mgrs"]):
+                if mgr is None:
+                    continue
+                f = int(flags[i]) & ~(_lib.TA_M_HAS_STATE | _lib.TA_M_EF_STATE)
+                if mgr._has_state:
+                    f |= _lib.TA_M_HAS_STATE
+                if mgr._ef_residual is not None:
+                    f |= _lib.TA_M_EF_STATE
+                flags[i] = f
+                settled = settled and mgr._has_state and (
+                    not mgr._error_feedback or mgr._ef_residual is not None)
+        parity = self._parity
+        if parity is not None or plan["parity_set"]:
+            uni = arr["sr_uniforms_dev"]
+            ainj = arr["alpha_inject_dev"]
+            plan["parity_set"] = parity is not None
+            for i, p in enumerate(plan["params"]):
+                if parity is not None:
+                    u = parity.get("uniforms", {}).get(p)
+                    a = parity.get("alpha", {}).get(p)
+                    uni[i] = u.data_ptr() if u is not None else 0
+                    ainj[i] = a.data_ptr() if a is not None else 0
+                    keep += [u, a]
+                else:
+                    uni[i] = 0
+                    ainj[i] = 0
         groups = plan["groups"]
         self._fill_groups(groups, bcs)
         ws = self._ws[dev]
@@ -557,10 +619,7 @@ class TurboAdam(Optimizer):
                     yield xb[:cb].view(torch.float64)
                 elif phase < _lib.TA_PHASE_LABELS:
                     yield xb[cb:cb + hb].view(torch.int32)
-            for _, p in items:
-                mgr = self.state[p].get("m_mgr")
-                if mgr is not None:
-                    mgr.mark_updated()
+            self._mark_updated(plan, settled)
             del keep
             return
         with torch.cuda.device(dev):
@@ -573,13 +632,21 @@ class TurboAdam(Optimizer):
                                           len(groups), self._seed, ws.data_ptr(), ws.numel(),
                                           _lib.stream_ptr(dev), evs)
         _lib.check(rc, "ta_step")
-        for _, p in items:
-            mgr = self.state[p].get("m_mgr")
-            if mgr is not None:
-                mgr.mark_updated()
+        self._mark_updated(plan, settled)
         # Temporaries in `keep` were allocated on the current stream, so the
         # caching allocator only reuses them for work ordered after ta_step.
         del keep
+
+    @staticmethod
+    def _mark_updated(plan, settled):
+        """Exposes the managers' new encodings (nothing to do once every
+        manager of the plan held state before this step)."""
+        if settled:
+            plan["settled"] = True
+            return
+        for mgr in plan["mgrs"]:
+            if mgr is not None:
+                mgr.mark_updated()
 
     def _fill_groups(self, groups, bcs):
         for gi, group in enumerate(self.param_groups):
