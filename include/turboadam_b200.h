@@ -249,7 +249,9 @@ TA_API ta_status ta_exchange_layout(const int64_t* global_blocks, int32_t n, int
  * region after PASS2, SEL1 and SEL2 -- on every rank, also on ranks that hold
  * no split tensor. Each rank then holds exactly the packed state the
  * unsharded ta_step gives its shards. Tensors without TA_M_SPANNING complete
- * as in ta_step. No counterpart in the reference.
+ * as in ta_step. TA_PHASE_PASS1 uploads the step's descriptor table into the
+ * workspace and the later phases run on it: pass the same tensor and group
+ * arrays to all five calls of a step. No counterpart in the reference.
  */
 TA_API ta_status ta_step_phase(const ta_tensor* tensors, int32_t n_tensors,
                                const ta_group* groups, int32_t n_groups, uint64_t seed,

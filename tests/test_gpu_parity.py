@@ -97,7 +97,13 @@ def _init_np(shape, rng, kind):
 P_RTOL = 1e-6
 
 
-def assert_params_close(got, ref, before, bf16, tag):
+def assert_params_close(got, ref, before, bf16, tag, wdf=None):
+    """Parameters of the default (fast) update against the checker's exact op
+    sequence. fp32 with ``wdf`` = fp32(1 - lr wd) also pins the update
+    itself: t = ref - fl(before * wdf) is the reference's update, and the
+    device's result must be within 1e-6 of |t| plus two ulp of the result
+    (the fast path fuses the weight decay into its final fma, one rounding
+    fewer than the reference)."""
     if bf16:
         g, r = GU.bf16_to_f32(got), GU.bf16_to_f32(ref)
         ulp = np.abs(r) * 2.0 ** -7
@@ -108,6 +114,14 @@ def assert_params_close(got, ref, before, bf16, tag):
         scale = np.abs(ref.astype(np.float64) - before)
         ok = GU.p_close(got, ref, scale, rtol=P_RTOL)
         assert ok.all(), f"{tag}: {(~ok).sum()} params beyond 1e-6 relative"
+        if wdf is not None:
+            w = (np.asarray(before, np.float32) * np.float32(wdf)).astype(np.float64)
+            t = ref.astype(np.float64) - w
+            err = np.abs(got.astype(np.float64) - ref)
+            lim = P_RTOL * np.abs(t) + 2.0 * np.spacing(np.abs(ref).astype(np.float32))
+            bad = err > lim
+            assert not bad.any(), (f"{tag}: {bad.sum()} updates beyond 1e-6 relative "
+                                   f"(worst {np.max(err / np.maximum(np.abs(t), 1e-30)):.3g})")
 
 
 def run_compare(oracle, shapes, groups_kw, nsteps, dtype=torch.float32, parity=False,
@@ -171,7 +185,9 @@ def run_compare(oracle, shapes, groups_kw, nsteps, dtype=torch.float32, parity=F
             st, ost = opt.state[tp], oopt.state[id(op)]
             if not exact_params:
                 got = bits16(tp.data).reshape(-1) if bf else to_np(tp.data).reshape(-1)
-                assert_params_close(got, op.data, before[i], bf, tag)
+                gkw = groups_kw[assign[i]]
+                wdf = np.float32(1.0 - gkw.get("lr", 1e-3) * gkw.get("weight_decay", 0.0))
+                assert_params_close(got, op.data, before[i], bf, tag, wdf=wdf)
                 op.data[:] = got  # both sides continue from the same parameters
             elif bf:
                 np.testing.assert_array_equal(bits16(tp.data).reshape(-1), op.data, err_msg=tag)

@@ -594,7 +594,9 @@ ta_status run_step(const ta_tensor* ts, int nT, const ta_group* groups, uint64_t
   const unsigned xsel_chunks = (unsigned)xsel.beg.back();
   const unsigned xa_chunks = (unsigned)xalist.beg.back();
 
-  if (mode != 2)  // the descriptor table and the list slots in use
+  // the descriptor table and the list slots in use; phases after the first
+  // of a sharded step run on the table that phase uploaded
+  if (mode != 2 && phase <= 0)
     TA_CU(cudaMemcpyAsync(ws + L.table, host.data() + L.table,
                           L.lists + L.list_stride * (size_t)slot - L.table,
                           cudaMemcpyHostToDevice, st));

@@ -206,6 +206,7 @@ struct __align__(16) StageMeta {
   int32_t nfull;    // leading full blocks of this tile
   float alpha_old;  // CoState alpha of the previous step (state)
   float alpha_new;  // this step's alpha (pass 2)
+  float nlrb;       // RN(-lr / bc1): the fast fp32 parameter update's step factor (pass 1)
 };
 
 struct KParams {
@@ -543,6 +544,19 @@ __device__ __forceinline__ float2 adam_pair_fast(float2 w, float2 x, float2 m, c
   const float2 nden = P.mul(fma2(x, y, dup2(c.eps)), dup2(-c.bc1));  // -(d bc1)
   const float2 yr = make_float2(rcp_approx(-nden.x), rcp_approx(-nden.y));
   return P.add(w, P.mul(P.mul(dup2(c.nlr), m), yr));
+}
+
+// The same for fp32 parameters from the old parameter p: the update
+// t = RN(RN(c m) rcp.approx(d)) with c = RN(-lr / bc1) has the roundings and
+// estimates of adam_pair_fast (four roundings, two estimates), and the
+// weight decay is fused: p' = RN(p (1 - lr wd) + t), one rounding fewer than
+// the reference's fl(fl(p (1 - lr wd)) + t).
+__device__ __forceinline__ float2 adam_pair_fast_f32(float2 p, float2 x, float2 m, const Sc& c,
+                                                     float nlrb, const PK& P) {
+  const float2 y = make_float2(rsqrt_approx(x.x), rsqrt_approx(x.y));
+  const float2 d = fma2(x, y, dup2(c.eps));
+  const float2 r = make_float2(rcp_approx(d.x), rcp_approx(d.y));
+  return fma2(p, dup2(c.wdf), P.mul(P.mul(dup2(nlrb), m), r));
 }
 
 // Three-input min / max (one instruction on sm_100; NaN operands are
@@ -1084,12 +1098,15 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
         // optimizer.py:106-107, 163/167, 170:
         // p = fl(p * (1 - lr wd)); d = sqrt(v / bc2) + eps; p += fl(-lr m) / fl(d bc1)
         const float4 p4 = ld_quad<PT>(sp, t0);
-        const float2 w01 = round_param2<PT>(P.mul(lo2(p4), dup2(c.wdf)));
-        const float2 w23 = round_param2<PT>(P.mul(hi2(p4), dup2(c.wdf)));
         float2 x01 = P.mul(v01, dup2(c.rbc2)), x23 = P.mul(v23, dup2(c.rbc2));
         if (!RBE) nanacc = fma2(x01, zero2, fma2(x23, zero2, nanacc));  // v, v / bc2 not finite
         float2 p01, p23;
-        if (EX) {
+        if (!EX && !PT) {
+          p01 = adam_pair_fast_f32(lo2(p4), x01, m01, c, M.nlrb, P);
+          p23 = adam_pair_fast_f32(hi2(p4), x23, m23, c, M.nlrb, P);
+        } else if (EX) {
+          const float2 w01 = round_param2<PT>(P.mul(lo2(p4), dup2(c.wdf)));
+          const float2 w23 = round_param2<PT>(P.mul(hi2(p4), dup2(c.wdf)));
           // v / bc2 by Markstein with y = RN(1/bc2): exact for v in the unflagged range
           x01 = fma2(fma2(x01, dup2(-c.bc2), v01), dup2(c.rbc2), x01);
           x23 = fma2(fma2(x23, dup2(-c.bc2), v23), dup2(c.rbc2), x23);
@@ -1099,7 +1116,9 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
           const float2 den01 = P.mul(d01, dup2(c.bc1)), den23 = P.mul(d23, dup2(c.bc1));
           p01 = P.add(w01, make_float2(__fdiv_rn(n01.x, den01.x), __fdiv_rn(n01.y, den01.y)));
           p23 = P.add(w23, make_float2(__fdiv_rn(n23.x, den23.x), __fdiv_rn(n23.y, den23.y)));
-        } else {
+        } else {  // bf16: p (1 - lr wd) rounds to bf16 before the update, as torch stores it
+          const float2 w01 = round_param2<PT>(P.mul(lo2(p4), dup2(c.wdf)));
+          const float2 w23 = round_param2<PT>(P.mul(hi2(p4), dup2(c.wdf)));
           p01 = adam_pair_fast(w01, x01, m01, c, P);
           p23 = adam_pair_fast(w23, x23, m23, c, P);
         }
@@ -1350,7 +1369,7 @@ __global__ void __launch_bounds__(NTHR, 4) k_pass1(const __grid_constant__ KPara
       int it = 0;
       EntryWalk walk;
       int cur_t = -1;
-      float cur_alpha = 0.0f;
+      float cur_alpha = 0.0f, cur_nlrb = 0.0f;
       Sc cur_c;
       DevTensor D;  // the current tensor's descriptor, copied once per tensor change
       for (int64_t tile = blockIdx.x; tile < kp.total; tile += gridDim.x, ++it) {
@@ -1364,12 +1383,14 @@ __global__ void __launch_bounds__(NTHR, 4) k_pass1(const __grid_constant__ KPara
           D = kp.T[t];
           cur_c = load_sc(D);
           cur_alpha = (MK == MK_COSTATE && (D.flags & DF_M_HAS_STATE)) ? *D.alpha_state : 0.0f;
+          cur_nlrb = __fdiv_rn(D.nlr, D.bc1);
         }
         const int64_t b0 = (tile - walk.first) * TB;
         const int nblk = (int)min((int64_t)TB, D.nblk - b0);
         if (it >= NSTAGE && !wait_bar(&done[s], ph ^ 1u, kp.status)) break;
         StageMeta& m = meta[s];
         fill_meta_common(m, D, cur_c, t, nblk, b0, cur_alpha);
+        m.nlrb = cur_nlrb;
         m.p = D.p;
         m.v_idx = D.v_idx;
         m.v_hdr = D.v_hdr;
