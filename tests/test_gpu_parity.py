@@ -509,3 +509,62 @@ def test_bf16_special_parameter_values(oracle):
         assert nan_ref.sum() == 3 * 7, f"step {step}"  # the planted NaNs stay NaN
         st, ost = opt.state[tp], oopt.state[id(op)]
         np.testing.assert_array_equal(to_np(st["compressed_v"]["indices"]), ost.v_idx)
+
+
+def test_persistent_zero_rows_and_tiny_v_bitexact(oracle):
+    """Embedding rows whose gradient stays zero keep v = exp(-69.0625) (the
+    fp16 header cannot decay further) and take the fast path; blocks whose
+    headers are set around the fast path's floor ln v = -69.25 (and below
+    it, where the exact path takes over) match the checker bit for bit."""
+    from turboadam_b200 import TurboAdam
+
+    rng = np.random.default_rng(31)
+    rows, cols = 512, 768
+    n = rows * cols
+    kw = dict(lr=6e-4, betas=(0.9, 0.999), weight_decay=0.01, v_bits=4)
+    init = (rng.standard_normal(n) * 0.02).astype(np.float32)
+    tp = torch.nn.Parameter(torch.from_numpy(init.reshape(rows, cols).copy()).cuda())
+    op = oracle.OracleParam(init.copy())
+    opt = TurboAdam([tp], seed=77, **kw)
+    oopt = oracle.OracleTurboAdam([oracle.OracleTurboAdam.make_group([op], **kw)])
+    dead = rng.random(rows) < 0.2  # the same rows every step
+    # fp16 headers around the floor: -69.0625 (a dead row's), -69.1875, -69.25,
+    # -69.3125 and -70 (both below it), as (lmin, lmax) with lmax a little higher
+    tiny = np.array([-69.0625, -69.1875, -69.25, -69.3125, -70.0], np.float16).view(np.uint16)
+    for s in range(6):
+        g = (rng.standard_normal((rows, cols)) * 1e-4).astype(np.float32)
+        g[dead] = 0.0
+        tp.grad = torch.from_numpy(g).cuda()
+        op.grad = g.reshape(-1).copy()
+        if s == 3:  # set block headers around the floor on both sides
+            cv = opt.state[tp]["compressed_v"]
+            ost = oopt.state[id(op)]
+            hdr = ost.v_hdr.reshape(-1, 2).copy()
+            blocks = np.flatnonzero(np.repeat(dead, cols // 128))[: 5 * 6]
+            for k, b in enumerate(blocks):
+                hdr[b, 0] = tiny[k % 5]
+                hdr[b, 1] = np.float16(np.float16(tiny[k % 5:k % 5 + 1].view(np.float16)[0])
+                                       + np.float16(0.5 * (k % 2))).view(np.uint16)
+            ost.v_hdr = hdr.reshape(-1).copy()
+            cv["scales"].copy_(torch.from_numpy(hdr.view(np.float16)).cuda())
+        before = op.data.astype(np.float64)
+        opt.step()
+        oopt.step(uniforms=lambda i, st, npad: oracle.sr_uniforms(n, i, st, 77))
+        torch.cuda.synchronize()
+        tag = f"step {s}"
+        st, ost = opt.state[tp], oopt.state[id(op)]
+        got = to_np(tp.data).reshape(-1)
+        assert_params_close(got, op.data, before, False, tag)
+        op.data[:] = got
+        np.testing.assert_array_equal(to_np(st["compressed_v"]["indices"]), ost.v_idx,
+                                      err_msg=tag)
+        np.testing.assert_array_equal(bits16(st["compressed_v"]["scales"]).reshape(-1),
+                                      ost.v_hdr, err_msg=tag)
+        enc, om = st["m_mgr"]._encoded, ost.mgr
+        np.testing.assert_array_equal(to_np(enc["sign_packed"]), om.signs, err_msg=tag)
+        np.testing.assert_array_equal(to_np(enc["labels"]), om.labels, err_msg=tag)
+    # the dead rows' other blocks stayed at the fresh header, -69.0625
+    hdr = ost.v_hdr.reshape(-1, 2).view(np.float16)
+    untouched = np.repeat(dead, cols // 128)
+    untouched[blocks] = False
+    assert (hdr[untouched] == np.float16(-69.0625)).all()

@@ -778,7 +778,11 @@ __device__ __noinline__ void p1_requant_exact(const float4* scr4, const float* s
 // ---------------------------------------------------------------------------
 constexpr float LN2_F = 0x1.62e43p-1f;       // RN(ln 2)
 constexpr float RINT_MAGIC = 0x1.8p23f;      // x + 1.5 * 2^23 rounds x to an integer
-constexpr float FAST_V_MIN = 0x1p-99f;       // smaller v_new -> exact path (L < -68.6)
+// smaller v_new -> exact path. ln(0x1.1p-100) = -69.25 lies inside the range
+// L >= -69.3 that the lg2 bound is checked over; a block whose gradient stays
+// zero keeps v = exp(-69.0625) (its fp16 header absorbs the beta2 decay), so
+// it stays on the fast path.
+constexpr float FAST_V_MIN = 0x1.1p-100f;
 
 __device__ __forceinline__ float lg2_approx(float x) {
   float r;
