@@ -514,10 +514,14 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.set_device(dev)
     cfg = CONFIGS[args.config]
     shapes = cfg["shapes"]()
+    if args.layers:  # a labelled subset: the first L transformer layers, no embedding / head
+        shapes = [s for s in shapes if any(s[0].startswith(f"l{i}.") for i in range(args.layers))]
     kw = dict(cfg["kw"])
     if args.v_bits:
         kw["v_bits"] = args.v_bits
     part = args.partition if args.partition != "auto" else cfg.get("partition", "tensor")
+    if args.layers and world == 1:
+        part = "tensor"
     pdtype = torch.bfloat16 if cfg["dtype"] == "bf16" else torch.float32
     psize = 2 if cfg["dtype"] == "bf16" else 4
     # local tensors: (shape, global tensor index, shard (block_offset, global_numel) or None)
@@ -717,7 +721,9 @@ def run_ours(args, rank, world, local_rank):
                  "device once and reused each step"
                  % ("Student-t(3) x %g" % cfg["grad_std"] if cfg.get("grad_dist") == "student_t3"
                     else "N(0,%g)" % cfg["grad_std"])),
-        "config": {"workload": args.config, "params": total_params, "tensors": len(shapes),
+        "config": {"workload": args.config + (f"[first {args.layers} layers]" if args.layers
+                                              else ""),
+                   "params": total_params, "tensors": len(shapes),
                    "v_bits": kw["v_bits"], "costate": kw.get("compress_m", True),
                    "parallelism": (f"ZeRO-1 flat partition over {world} GPU(s); tensors split "
                                    "at 4096-block boundaries, 4 all-reduces per step (alpha "
@@ -775,6 +781,9 @@ def main():
     ap.add_argument("--partition", default="auto", choices=["auto", "tensor", "zero1"])
     ap.add_argument("--e2e-steps", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="Llama configs: time only the first L transformer layers (a labelled "
+                         "subset, e.g. the 70B shape on one GPU)")
     ap.add_argument("--no-reference-gpu", action="store_true",
                     help="skip timing the reference's own GPU step (baseline/_ref)")
     args = ap.parse_args()
