@@ -725,9 +725,12 @@ def run_ours(args, rank, world, local_rank):
                                               else ""),
                    "params": total_params, "tensors": len(shapes),
                    "v_bits": kw["v_bits"], "costate": kw.get("compress_m", True),
-                   "parallelism": (f"ZeRO-1 flat partition over {world} GPU(s); tensors split "
-                                   "at 4096-block boundaries, 4 all-reduces per step (alpha "
-                                   "chunk sums, 3 histogram rounds)" if part == "zero1" else
+                   "parallelism": (f"ZeRO-1 flat partition over {world} GPU(s); " + (
+                                       f"{len(spanning)} tensor(s) split at 4096-block "
+                                       "boundaries, 4 all-reduces per step (alpha chunk sums, 3 "
+                                       "histogram rounds)" if spanning else
+                                       "every cut falls on a tensor boundary: no tensor is "
+                                       "split, no collective") if part == "zero1" else
                                    f"by-tensor LPT over {world} GPU(s), no collective"),
                    "l2": (f"{ws_bytes / 1e6:.0f} MB per rank per step < 4 x 126 MB L2: a 512 MB "
                           "buffer is written between steps, each step timed by its own events"
