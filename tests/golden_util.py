@@ -41,3 +41,16 @@ def p_close(ours, ref, update_scale, rtol=1e-6):
     ref = np.asarray(ref, np.float64)
     tol = rtol * (np.abs(ref) + np.asarray(update_scale, np.float64))
     return np.abs(ours - ref) <= tol
+
+
+def bf16_p_close(ours_bits, ref_bits, before, wdf, rtol=1e-6):
+    """bf16 parameter agreement: the fp32 results before the final rounding
+    agree as p_close says (rtol of |ref| plus the update), and rounding each
+    to bf16 adds at most one ulp, so |ours - ref| <= ulp(ref) + rtol *
+    (|ref| + |ref - before * wdf|). The update term matters where the update
+    cancels the decayed parameter (the result is then tiny and an ulp of it
+    says nothing about the update's accuracy)."""
+    o = bf16_to_f32(ours_bits).astype(np.float64)
+    r = bf16_to_f32(ref_bits).astype(np.float64)
+    t = np.abs(r - np.asarray(before, np.float64) * float(wdf))
+    return np.abs(o - r) <= np.abs(r) * 2.0 ** -7 + rtol * (np.abs(r) + t) + 1e-38

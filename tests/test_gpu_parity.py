@@ -92,8 +92,9 @@ def _init_np(shape, rng, kind):
 
 # Parameter tolerance of the default (fast) update: 1e-6 relative (the north
 # star's bar) to |p| + the size of the step's update (GU.p_close: where p
-# crosses zero the update is the scale). bf16 parameters may differ by one
-# bf16 ulp where the fp32 result lies next to a bf16 rounding boundary (rare).
+# crosses zero the update is the scale). bf16 parameters may in addition
+# differ by one bf16 ulp where the fp32 result lies next to a bf16 rounding
+# boundary (rare).
 P_RTOL = 1e-6
 
 
@@ -104,11 +105,10 @@ def assert_params_close(got, ref, before, bf16, tag, wdf=None):
     device's result must be within 1e-6 of |t| plus two ulp of the result
     (the fast path fuses the weight decay into its final fma, one rounding
     fewer than the reference)."""
-    if bf16:
-        g, r = GU.bf16_to_f32(got), GU.bf16_to_f32(ref)
-        ulp = np.abs(r) * 2.0 ** -7
-        off = np.abs(g.astype(np.float64) - r) > 0
-        assert np.all(np.abs(g.astype(np.float64) - r) <= ulp + 1e-38), tag
+    if bf16:  # one bf16 ulp plus 1e-6 of the update (golden_util.bf16_p_close)
+        ok = GU.bf16_p_close(got, ref, before, 1.0 if wdf is None else wdf, rtol=P_RTOL)
+        assert ok.all(), f"{tag}: {(~ok).sum()} bf16 params beyond an ulp + 1e-6 of the update"
+        off = np.asarray(got) != np.asarray(ref)
         assert off.mean() <= 1e-3, f"{tag}: {off.sum()} bf16 params differ"
     else:
         scale = np.abs(ref.astype(np.float64) - before)
@@ -175,7 +175,8 @@ def run_compare(oracle, shapes, groups_kw, nsteps, dtype=torch.float32, parity=F
         else:
             n_of = [tparams[order[k]].numel() for k in range(len(order))]
             ufn = lambda oi, st, npad: oracle.sr_uniforms(n_of[oi], oi, st, seed)  # noqa: E731
-        before = [op.data.astype(np.float64) for op in oparams]
+        before = [(GU.bf16_to_f32(op.data) if op.bf16 else op.data).astype(np.float64)
+                  for op in oparams]
         opt.step()
         oopt.step(uniforms=ufn)
         torch.cuda.synchronize()
