@@ -210,16 +210,70 @@ def step_bytes(n, kw, psize=4, n_policy=None):
 # ---------------------------------------------------------------------------
 
 class Clocks:
+    """SM clock and clock-event (throttle) reasons of this rank's GPU during
+    the timed region. NVML is read from a thread every 10 ms and once more
+    when the region ends (the GPU has just finished its last step then), so
+    even a region of a few milliseconds has samples; without NVML bindings
+    `nvidia-smi -lms 200` runs alongside (a region shorter than its start-up
+    may then have none). Reading clocks changes no setting."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clocks-event reason bits (nvml.h nvmlClocksEventReason*)
+    REASONS = (("sw_power_cap", 0x4), ("hw_slowdown", 0x8), ("sw_thermal_slowdown", 0x20),
+               ("hw_thermal_slowdown", 0x40), ("hw_power_brake_slowdown", 0x80))
 
-    def __init__(self, index):
+    def __init__(self, index, device=None):
         self.index = index
+        self.device = device
         self.proc = None
         self.path = None
+        self.nvml = None
+        self.samples = []
+        self.thread = None
+        self.halt = None
+
+    def _nvml_handle(self):
+        import pynvml
+
+        pynvml.nvmlInit()
+        if self.device is not None:
+            try:
+                import torch
+
+                pr = torch.cuda.get_device_properties(self.device)
+                bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+                return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            except Exception:
+                pass
+        return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.index)
+
+    def _read(self):
+        nv, h = self.nvml
+        sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+        self.samples.append((sm, mx, rs))
 
     def start(self):
+        try:
+            import threading
+
+            self.nvml = self._nvml_handle()
+            self.halt = threading.Event()
+
+            def poll():
+                while not self.halt.wait(0.01):
+                    try:
+                        self._read()
+                    except Exception:
+                        return
+
+            self.thread = threading.Thread(target=poll, daemon=True)
+            self.thread.start()
+            return
+        except Exception:
+            self.nvml = None
         try:
             fd, self.path = tempfile.mkstemp(suffix=".csv")
             os.close(fd)
@@ -231,6 +285,18 @@ class Clocks:
             self.proc = None
 
     def stop(self):
+        if self.nvml is not None:
+            self.halt.set()
+            self.thread.join(timeout=5)
+            try:
+                self._read()
+            except Exception:
+                pass
+            reasons = sorted({nm for _, _, rs in self.samples for nm, bit in self.REASONS
+                              if rs & bit})
+            return {"sm_mhz": statistics.median(sm for sm, _, _ in self.samples),
+                    "sm_max_mhz": max(mx for _, mx, _ in self.samples),
+                    "reasons": reasons, "samples": len(self.samples), "source": "nvml"}
         if self.proc is None:
             return None
         self.proc.terminate()
@@ -256,7 +322,7 @@ class Clocks:
         if not sm:
             return None
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx),
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "source": "nvidia-smi"}
 
 
 # ---------------------------------------------------------------------------
@@ -576,7 +642,7 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize(dev)
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
-    clocks = Clocks(local_rank)
+    clocks = Clocks(local_rank, dev)
     # a working set that L2 could hold between steps is timed per step, with
     # a 512 MB buffer written between steps (outside the step's events)
     ws_bytes = sum(step_bytes(n, kw, psize, npol) for n, npol in mine)
