@@ -1006,6 +1006,20 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
   float vmin = INFINITY, vmax = -INFINITY;
   float mgs = 0.0f, ggs = 0.0f;  // lane partials of m.g and g.g
   bool fix = false;              // FULL: this group's block needs the exact path
+  // bf16 parameters: the lane's two lead draws are made here, so their integer
+  // chains can fill the waits of phase A (0.2-1.1 % faster in two A/B runs;
+  // with fp32 parameters the 8 extra live words spill at 96 registers and it
+  // is 2 % slower)
+  constexpr bool EARLY = FULL && VK == VK_ONEQ && !UNI && PT == 1;
+  uint32_t lead_e[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+  if (EARLY) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      uint32_t ctr[4];
+      ta_sr_lead_counter((uint64_t)(b + M.boff), (uint32_t)j, (uint32_t)h, c.tid, c.step, ctr);
+      philox_rk(ctr[0], ctr[1], ctr[2], ctr[3], kp.rk0, kp.rk1, lead_e[h]);
+    }
+  }
   if (FULL) {
     float2 am = dup2(0.0f), ag = dup2(0.0f), nanacc = dup2(0.0f);
     // CoState + 1Q: the range flags come from per-lane reductions instead of a
@@ -1297,7 +1311,10 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
           u4 = *reinterpret_cast<const float4*>(suni + t0);
           w4 = cat4(P.sub(dup2(0.5f), lo2(u4)), P.sub(dup2(0.5f), hi2(u4)));
         } else {
-          if ((k & 1) == 0) {  // one draw per quad pair: the lead halves of 8 elements
+          if (EARLY && (k & 1) == 0) {
+#pragma unroll
+            for (int w = 0; w < 4; ++w) lead[w] = lead_e[k >> 1][w];
+          } else if ((k & 1) == 0) {  // one draw per quad pair: the lead halves of 8 elements
             uint32_t ctr[4];
             ta_sr_lead_counter(gb, (uint32_t)j, (uint32_t)(k >> 1), c.tid, c.step, ctr);
             philox_rk(ctr[0], ctr[1], ctr[2], ctr[3], kp.rk0, kp.rk1, lead);
