@@ -556,11 +556,16 @@ def measured_peak():
 
 
 def profiled_traffic(config):
-    """Per-param DRAM bytes of pass 1 from the committed ncu summary (a
-    GPT-2 124M capture; the traffic per element does not depend on the tensor
-    count, so it scales to a full launch by the elements processed)."""
-    p = os.path.join(ROOT, "profiles", "k_pass1_gpt2-124m.txt")
-    if not os.path.exists(p):
+    """Per-param DRAM bytes of pass 1 from the committed ncu summary of the
+    same kernel kind (fp32 CoState + 4-bit 1Q: a GPT-2 124M capture; bf16
+    CoState + 3-bit: one Llama-3-70B layer). The traffic per element does not
+    depend on the tensor count, so it scales to a full launch by the elements
+    processed; a config whose kernel kind has no capture gets None."""
+    name = {"llama3-8b": "k_pass1_gpt2-124m.txt", "gpt2-124m": "k_pass1_gpt2-124m.txt",
+            "gpt2-block": "k_pass1_gpt2-124m.txt",
+            "llama3-70b": "k_pass1_llama3-70b-layer.txt"}.get(config)
+    p = os.path.join(ROOT, "profiles", name) if name else None
+    if p is None or not os.path.exists(p):
         return None
     for line in open(p):
         if line.startswith("dram_bytes_per_param"):
