@@ -486,13 +486,21 @@ __device__ __forceinline__ uint32_t bf16x2_rn(float lo, float hi) {
   if (isnan(lo) || isnan(hi)) r = bf16x2_portable(lo, hi);
   return r;
 }
+// The same for inputs the caller knows are not NaN (the hardware conversion
+// alone).
+__device__ __forceinline__ uint32_t bf16x2_rn_fin(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
 
-template <int PT>
+// FIN: the values are not NaN (bf16 conversions without the NaN test)
+template <int PT, bool FIN = false>
 __device__ __forceinline__ void st_quad(void* p, int64_t e, float4 v) {
   if (PT) {
     uint2 w;
-    w.x = bf16x2_rn(v.x, v.y);
-    w.y = bf16x2_rn(v.z, v.w);
+    w.x = FIN ? bf16x2_rn_fin(v.x, v.y) : bf16x2_rn(v.x, v.y);
+    w.y = FIN ? bf16x2_rn_fin(v.z, v.w) : bf16x2_rn(v.z, v.w);
     *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(p) + e) = w;
   } else {
     *reinterpret_cast<float4*>(reinterpret_cast<float*>(p) + e) = v;
@@ -509,10 +517,10 @@ __device__ __forceinline__ float amp_unscale(float g, float ginv) {
   return PT ? ta_bf16_to_f32(ta_f32_to_bf16(u)) : u;
 }
 
-template <int PT>
+template <int PT, bool FIN = false>
 __device__ __forceinline__ float2 round_param2(float2 v) {
   if (PT) {
-    const uint32_t r = bf16x2_rn(v.x, v.y);
+    const uint32_t r = FIN ? bf16x2_rn_fin(v.x, v.y) : bf16x2_rn(v.x, v.y);
     return make_float2(__uint_as_float(r << 16), __uint_as_float(r & 0xffff0000u));
   }
   return v;
@@ -1028,6 +1036,7 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
     // v_new is infinite), and v / bc2 overflows only where the largest v_new
     // times RN(1/bc2) does.
     constexpr bool RBE = MK == MK_COSTATE && VK == VK_ONEQ;
+    constexpr bool PFIN = PT == 1 && !EX && VK != VK_NONE;  // see the bf16 update below
     float vmin_fp = INFINITY;  // VK_FP32: smallest v_new
     uint32_t idor = 0;
     const float2 zero2 = dup2(0.0f);
@@ -1135,12 +1144,17 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
           p01 = P.add(w01, make_float2(__fdiv_rn(n01.x, den01.x), __fdiv_rn(n01.y, den01.y)));
           p23 = P.add(w23, make_float2(__fdiv_rn(n23.x, den23.x), __fdiv_rn(n23.y, den23.y)));
         } else {  // bf16: p (1 - lr wd) rounds to bf16 before the update, as torch stores it
-          const float2 w01 = round_param2<PT>(P.mul(lo2(p4), dup2(c.wdf)));
-          const float2 w23 = round_param2<PT>(P.mul(hi2(p4), dup2(c.wdf)));
+          // A NaN or infinite parameter flags the block for the exact path (which
+          // keeps torch's NaN encoding); the conversions here then see finite
+          // values only (w finite, the update finite or infinite) and skip the
+          // NaN test. The m-only kernel has no exact path and keeps the test.
+          if (PFIN) nanacc = fma2(lo2(p4), zero2, fma2(hi2(p4), zero2, nanacc));
+          const float2 w01 = round_param2<PT, PFIN>(P.mul(lo2(p4), dup2(c.wdf)));
+          const float2 w23 = round_param2<PT, PFIN>(P.mul(hi2(p4), dup2(c.wdf)));
           p01 = adam_pair_fast(w01, x01, m01, c, P);
           p23 = adam_pair_fast(w23, x23, m23, c, P);
         }
-        st_quad<PT>(gp, e, cat4(p01, p23));
+        st_quad<PT, PFIN>(gp, e, cat4(p01, p23));
       }
     }
     if (MK == MK_COSTATE) {
