@@ -947,8 +947,12 @@ __device__ __noinline__ void p1_requant_redo(uint32_t redo, const StageMeta& M, 
 // IEEE divisions and exact special cases everywhere. ln v_new goes through a
 // per-lane smem scratch between the v update and the re-quantisation.
 // EX (fast path only): TA_EXACT_PARAM as a compile-time value, so the default
-// update's hot loop carries no code of the correctly rounded one.
-template <int MK, int VK, int PT, bool UNI, bool TABLE, bool FULL, bool EX = false>
+// update's hot loop carries no code of the correctly rounded one. NOAMP (fast
+// path only): no GradScaler unscale, known at compile time (bf16 parameters:
+// 2.5 % faster than the per-quad test; with fp32 the extra instance of the
+// block is 1.4 % slower, and it is not used there).
+template <int MK, int VK, int PT, bool UNI, bool TABLE, bool FULL, bool EX = false,
+          bool NOAMP = false>
 __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
                                          const uint8_t* st, float* table, float* scr,
                                          const KParams& kp) {
@@ -1080,7 +1084,7 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
       const int64_t e = e0 + t0;
       const float4 g4 = ld_quad<PT>(sg, t0);
       float2 g01 = lo2(g4), g23 = hi2(g4);
-      if (c.flags & DF_AMP) {  // GradScaler.unscale_: g * RN(1 / scale), stored in g's dtype
+      if (!NOAMP && (c.flags & DF_AMP)) {  // GradScaler.unscale_: g * RN(1 / scale), stored in g's dtype
         g01 = round_param2<PT>(P.mul(g01, dup2(c.ginv)));
         g23 = round_param2<PT>(P.mul(g23, dup2(c.ginv)));
       }
@@ -1502,6 +1506,8 @@ __global__ void __launch_bounds__(NTHR, 4) k_pass1(const __grid_constant__ KPara
     const bool fast = pm.nfull >= 13 + warp && !(pm.c.flags & (DF_M_OUT | DF_V_OUT | DF_EF));
     if (fast && (pm.c.flags & DF_EXACT_P))
       p1_block<MK, VK, PT, UNI, TABLE, true, true>(kp.T, pm, st, table, scr, kp);
+    else if (fast && PT == 1 && !(pm.c.flags & DF_AMP))
+      p1_block<MK, VK, PT, UNI, TABLE, true, false, true>(kp.T, pm, st, table, scr, kp);
     else if (fast)
       p1_block<MK, VK, PT, UNI, TABLE, true, false>(kp.T, pm, st, table, scr, kp);
     else
