@@ -948,9 +948,10 @@ __device__ __noinline__ void p1_requant_redo(uint32_t redo, const StageMeta& M, 
 // per-lane smem scratch between the v update and the re-quantisation.
 // EX (fast path only): TA_EXACT_PARAM as a compile-time value, so the default
 // update's hot loop carries no code of the correctly rounded one. NOAMP (fast
-// path only): no GradScaler unscale, known at compile time (bf16 parameters:
-// 2.5 % faster than the per-quad test; with fp32 the extra instance of the
-// block is 1.4 % slower, and it is not used there).
+// path only): no GradScaler unscale and a parameter to update, known at
+// compile time (bf16 parameters: 2.5 % and 1.3 % faster than the per-quad
+// tests; with fp32 the extra instance of the block is 1.4 % slower, and it is
+// not used there).
 template <int MK, int VK, int PT, bool UNI, bool TABLE, bool FULL, bool EX = false,
           bool NOAMP = false>
 __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
@@ -969,7 +970,7 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
   const int64_t e0 = b * BS;
   const int nv = FULL ? BS : (active ? (int)min((int64_t)BS, M.n - e0) : 0);
   const bool fullblk = FULL || nv == BS;
-  const bool param = !(c.flags & DF_NO_PARAM);
+  const bool param = NOAMP || !(c.flags & DF_NO_PARAM);
   void* const gp = M.p;
   float* const gea = M.ea;
   float* const geas = M.eas;
@@ -1506,7 +1507,7 @@ __global__ void __launch_bounds__(NTHR, 4) k_pass1(const __grid_constant__ KPara
     const bool fast = pm.nfull >= 13 + warp && !(pm.c.flags & (DF_M_OUT | DF_V_OUT | DF_EF));
     if (fast && (pm.c.flags & DF_EXACT_P))
       p1_block<MK, VK, PT, UNI, TABLE, true, true>(kp.T, pm, st, table, scr, kp);
-    else if (fast && PT == 1 && !(pm.c.flags & DF_AMP))
+    else if (fast && PT == 1 && !(pm.c.flags & (DF_AMP | DF_NO_PARAM)))
       p1_block<MK, VK, PT, UNI, TABLE, true, false, true>(kp.T, pm, st, table, scr, kp);
     else if (fast)
       p1_block<MK, VK, PT, UNI, TABLE, true, false>(kp.T, pm, st, table, scr, kp);
