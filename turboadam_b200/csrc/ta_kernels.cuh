@@ -537,28 +537,30 @@ __device__ __forceinline__ float rcp_approx(float x) {
   return r;
 }
 
-// Parameter update of a pair without TA_EXACT_PARAM (optimizer.py:163-170):
-// p = w + fl(-lr m) / fl(d bc1), d = sqrt(x) + eps, x = fl(v * RN(1/bc2)).
-// d = RN(x * rsqrt.approx(x) + eps) in one fma, the quotient n * rcp.approx(den):
-// the shortest chain (the step is latency-bound here). The relative error of
-// the update is at most the two estimates' (each <= 2^-22, checked
-// exhaustively on the device by ta_selftest_fast_math) plus a few roundings,
-// about 5e-7 -- inside the 1e-6 parameter tolerance; no state depends on it.
-// Inputs come from unflagged blocks: x is a finite normal number, den a
-// positive normal number.
-__device__ __forceinline__ float2 adam_pair_fast(float2 w, float2 x, float2 m, const Sc& c,
-                                                 const PK& P) {
+// Parameter update of a pair without TA_EXACT_PARAM (optimizer.py:163-170),
+// reference p' = w + fl(-lr m) / fl(d bc1), d = sqrt(x) + eps,
+// x = fl(v * RN(1/bc2)), w = fl(p (1 - lr wd)). Fast form of the update
+// term: t = RN(RN(c m) rcp.approx(d)) with c = RN(-lr / bc1) and
+// d = RN(x rsqrt.approx(x) + eps) in one fma -- the shortest chain (the step
+// is latency-bound here). Its relative error is at most the two estimates'
+// (each <= 2^-22, checked exhaustively on the device by
+// ta_selftest_fast_math) plus four roundings, about 5e-7 -- inside the 1e-6
+// parameter tolerance; no state depends on it. Inputs come from unflagged
+// blocks: x is a finite normal number, d a positive normal number.
+
+// bf16 parameters, from w = the bf16-rounded p (1 - lr wd): w + t (the error
+// of t is far below the bf16 rounding of the result).
+__device__ __forceinline__ float2 adam_pair_fast_w(float2 w, float2 x, float2 m, const Sc& c,
+                                                   float nlrb, const PK& P) {
   const float2 y = make_float2(rsqrt_approx(x.x), rsqrt_approx(x.y));
-  const float2 nden = P.mul(fma2(x, y, dup2(c.eps)), dup2(-c.bc1));  // -(d bc1)
-  const float2 yr = make_float2(rcp_approx(-nden.x), rcp_approx(-nden.y));
-  return P.add(w, P.mul(P.mul(dup2(c.nlr), m), yr));
+  const float2 d = fma2(x, y, dup2(c.eps));
+  const float2 r = make_float2(rcp_approx(d.x), rcp_approx(d.y));
+  return P.add(w, P.mul(P.mul(dup2(nlrb), m), r));
 }
 
-// The same for fp32 parameters from the old parameter p: the update
-// t = RN(RN(c m) rcp.approx(d)) with c = RN(-lr / bc1) has the roundings and
-// estimates of adam_pair_fast (four roundings, two estimates), and the
-// weight decay is fused: p' = RN(p (1 - lr wd) + t), one rounding fewer than
-// the reference's fl(fl(p (1 - lr wd)) + t).
+// fp32 parameters, from the old parameter p, with the weight decay fused:
+// p' = RN(p (1 - lr wd) + t), one rounding fewer than the reference's
+// fl(fl(p (1 - lr wd)) + t).
 __device__ __forceinline__ float2 adam_pair_fast_f32(float2 p, float2 x, float2 m, const Sc& c,
                                                      float nlrb, const PK& P) {
   const float2 y = make_float2(rsqrt_approx(x.x), rsqrt_approx(x.y));
@@ -1190,8 +1192,8 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
           if (PFIN) nanacc = fma2(lo2(p4), zero2, fma2(hi2(p4), zero2, nanacc));
           const float2 w01 = round_param2<PT, PFIN>(P.mul(lo2(p4), dup2(c.wdf)));
           const float2 w23 = round_param2<PT, PFIN>(P.mul(hi2(p4), dup2(c.wdf)));
-          p01 = adam_pair_fast(w01, x01, m01, c, P);
-          p23 = adam_pair_fast(w23, x23, m23, c, P);
+          p01 = adam_pair_fast_w(w01, x01, m01, c, M.nlrb, P);
+          p23 = adam_pair_fast_w(w23, x23, m23, c, M.nlrb, P);
         }
         st_quad<PT, PFIN>(gp, e, cat4(p01, p23));
       }
