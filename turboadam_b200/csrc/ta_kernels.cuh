@@ -1056,9 +1056,10 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
   float mgs = 0.0f, ggs = 0.0f;  // lane partials of m.g and g.g
   bool fix = false;              // FULL: this group's block needs the exact path
   // bf16 parameters: the lane's two lead draws are made here, so their integer
-  // chains can fill the waits of phase A (0.2-1.1 % faster in two A/B runs;
-  // with fp32 parameters the 8 extra live words spill at 96 registers and it
-  // is 2 % slower)
+  // chains can fill the waits of phase A (4.3 % faster than drawing them in
+  // the re-quantisation loop, in the current bf16 kernel; with fp32
+  // parameters the 8 extra live words spill at 96 registers and it is 2 %
+  // slower)
   constexpr bool EARLY = FULL && VK == VK_ONEQ && !UNI && PT == 1;
   uint32_t lead_e[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
   if (EARLY) {
