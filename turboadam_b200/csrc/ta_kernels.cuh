@@ -1384,7 +1384,7 @@ __device__ __forceinline__ void p1_block(const DevTensor* T, const StageMeta& M,
         uint32_t word = requant_quad_fast(la, w4, lmin2, k12, tops, P, &emax);
         // rare: an element near a decision boundary. fp32 parameters: the quad is
         // redone after the loop (one test per block in the hot loop: 1.7 % faster);
-        // bf16 parameters: here (the later redo spills there: 1.6 % slower)
+        // bf16 parameters: here (the later redo was 0.7-1.6 % slower there)
         if (REDO) {
           redo |= (emax >= (UNI ? thr : thr_lead)) ? (1u << k) : 0u;
         } else if (emax >= (UNI ? thr : thr_lead)) {
